@@ -1,0 +1,158 @@
+/*
+ * pir2b — C ABI of the B200 (sm_100a) quantized-Linear library.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*), launches asynchronously on that stream,
+ * allocates nothing, never synchronizes, and returns a status:
+ *     0                 success
+ *     PIR2B_EINVAL (1)  bad shape / size / mode / null pointer
+ *     PIR2B_EALIGN (2)  pointer or stride alignment not met
+ *     PIR2B_ECUDA (-1)  a CUDA runtime call failed (launch error)
+ * pir2b_last_error() returns the message of the last failure on the calling
+ * thread.  Because nothing allocates or syncs, calls can be captured into
+ * CUDA graphs once the library has been loaded.
+ *
+ * Formats ("symmetric-row-v1", piR2 coexecution/kernels/ampere_ada/integer.py):
+ *   Kpad = ceil(K / 128) * 128, Npad = ceil(N / 8) * 8, L = 2^(bits-1) - 1.
+ *   Activations: per-row fp32 scale s = max|v| * (1/L) (1.0 for an all-zero
+ *   row), q = clamp(rint(v / s), -L, L); int8 rows of Kpad bytes, or int4
+ *   rows of Kpad/2 bytes, low nibble = even column.
+ *   Weights: per-output-channel fp32 scale, same code layout, [Npad, Kpad].
+ */
+#ifndef PIR2B_H
+#define PIR2B_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PIR2B_OK 0
+#define PIR2B_EINVAL 1
+#define PIR2B_EALIGN 2
+#define PIR2B_ECUDA (-1)
+
+/* Activation selection modes of the quantizer (integer.py:27-47). */
+#define PIR2B_MODE_PLAIN 0 /* v = x                                  */
+#define PIR2B_MODE_GATED 1 /* v = bf16(lut[x] * up)  (SiLU/GELU * up) */
+#define PIR2B_MODE_LUT 2   /* v = lut[x]             (GELU)           */
+
+/* Bias handling of the GEMM epilogue (integer_gemm.cu:73-76, 164-168). */
+#define PIR2B_BIAS_NONE 0 /* gemm_biasless without bias: no add         */
+#define PIR2B_BIAS_ZERO 1 /* gemm with a null bias: adds +0 (-0 -> +0)  */
+#define PIR2B_BIAS_ADD 2  /* y + f32(bias[n])                           */
+
+/* Norm kinds of the fused producer. */
+#define PIR2B_NORM_NONE 0 /* input already normalized                      */
+#define PIR2B_NORM_RMS 1  /* x * rsqrt(mean(x^2) + eps), then * gamma       */
+#define PIR2B_NORM_LN 2   /* non-affine LayerNorm                          */
+
+/* Output formats of the fused producer. */
+#define PIR2B_OUT_INT8 8
+#define PIR2B_OUT_INT4 4
+#define PIR2B_OUT_NVFP4 16
+
+/* Library version (major * 100 + minor). */
+int pir2b_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *pir2b_last_error(void);
+
+/* Reads, then clears, the device status word that bounded in-kernel waits
+ * set when they give up (0: no wait expired).  Synchronizes `stream`.
+ * No counterpart in the reference (which has no bounded device waits). */
+int pir2b_device_status(int *status_out, void *stream);
+
+/* Per-row symmetric quantization and packing of BF16 activations.
+ * Replaces the Triton `_prepare` kernel and its native twin
+ * `prepare_integer<Bits>`:
+ *   coexecution/kernels/ampere_ada/integer.py:50-94, :107-173
+ *   coexecution/kernels/ampere_ada/csrc/integer_dispatch.cu:11-65, :262-303
+ *   coexecution/optimization/backends/integer/linear.py:51-90 (`prepare`)
+ * x: bf16 [rows, k] with row stride ldx (elements); up: bf16 rows (stride
+ * ldu) for MODE_GATED, else NULL; lut: bf16[65536] for MODE_GATED/MODE_LUT;
+ * smooth: optional fp32 [k] SmoothQuant divisor applied as bf16(bf16(v)/s)
+ * before quantization (thor/packing.py:69-73), NULL to skip.
+ * q: int8 [rows, Kpad] (bits 8) or uint8 [rows, Kpad/2] (bits 4);
+ * scales: fp32 [rows].  1 <= k <= 65536, rows >= 0. */
+int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
+                     const void *lut, const float *smooth, int mode, int bits,
+                     int64_t rows, int64_t k, void *q, float *scales,
+                     void *stream);
+
+/* Fused norm (+ AdaLN modulation) (+ gated residual) + quantize/pack.
+ * Replaces the Triton producers of
+ *   coexecution/kernels/ampere_ada/modulation.py:14-239 (modulation,
+ *     non-affine LayerNorm + modulation, residual + LayerNorm + modulation)
+ *   coexecution/kernels/ampere_ada/producers.py:19-90 (`prepare_rmsnorm`)
+ *   coexecution/kernels/ampere_ada/csrc/layernorm_pack.cu:125-303
+ *   coexecution/optimization/backends/thor/packing.py:84-448 (FP4 outputs)
+ * Row r of x (bf16, contiguous [rows, k]):
+ *   if y_in:  x' = bf16(x + bf16(y_in * gate[r / tokens]))  (written to
+ *             res_out, modulation.py:212-216)
+ *   norm:     NONE: n = x'; RMS: n = bf16(bf16(x' * rsqrt(var + eps)) *
+ *             gamma); LN: n = bf16((x' - mean) * rsqrt(var + eps))
+ *   if scale: v = bf16(bf16(n * bf16(1 + scale[r / tokens])) + shift[...])
+ *             (modulation.py:103-107); scale/shift rows have stride ld_mod
+ *   smooth:   optional SmoothQuant divisor as in pir2b_quant_rows
+ *   out_format INT8 / INT4: symmetric-row-v1 q + scales;
+ *   out_format NVFP4: q = packed E2M1 [rows, k/2], scales = swizzled UE4M3
+ *             block-16 factors (layout of pir2b_pack_nvfp4).
+ * 8 <= k <= 8192, k % 8 == 0 (k % 32 == 0 for NVFP4); pointers 16-byte
+ * aligned.  (The reference RMS producer has the same k <= 8192 bound,
+ * producers.py:295.) */
+int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
+                          void *res_out, const void *gamma, const void *scale,
+                          const void *shift, int64_t ld_mod, int64_t tokens,
+                          const float *smooth, int norm_kind, float eps,
+                          int out_format, int64_t rows, int64_t k, void *q,
+                          void *scales, void *stream);
+
+/* Quantized GEMM with fused dequant epilogue on tcgen05 (kind::i8).
+ * Replaces pir2_integer::gemm / gemm_biasless
+ *   coexecution/kernels/ampere_ada/csrc/integer_gemm.cu:22-195
+ * and its Ada-only twins (split-K reduce_scale, integer_split_k.cu:27-52;
+ * int4 small-M tiles, int4_small_m.cu:17-42; int4 GEMV, int4_gemv.cu:29-61).
+ * qa: activations int8 [m, Kpad] / uint8 [m, Kpad/2]; sa fp32 [m];
+ * qw: weights int8 [npad, Kpad] / uint8 [npad, Kpad/2]; sw fp32 [npad];
+ * bias: bf16 [npad] (bias_mode ADD) or NULL; out_lut: optional bf16[65536]
+ * table applied to the bf16 result (fuses GELU/SiLU producers);
+ * out: bf16, row stride ldo, columns [0, n_store) written.
+ * kpad % 128 == 0, npad % 8 == 0, n_store <= npad, m >= 1.
+ * tactic: -1 selects the tile shape by heuristic; piR2's Ada tactic ids
+ * 0..7 are accepted and ignored (tiles are chosen for B200). */
+int pir2b_gemm(const void *qa, const float *sa, const void *qw,
+               const float *sw, const void *bias, int bias_mode,
+               const void *out_lut, int bits, int64_t m, int64_t npad,
+               int64_t kpad, void *out, int64_t ldo, int64_t n_store,
+               int tactic, void *stream);
+
+/* NVFP4 (E2M1 values, UE4M3 scale per 16 elements) packing of bf16 rows.
+ * Replaces pack_matrix_fp4_ue_rowmajor_kernel / pack_activation_gemm_bf16 /
+ * pack_linear_weight_gemm_bf16:
+ *   coexecution/kernels/blackwell/csrc/fp4_cutlass_linear.cu:789-842,
+ *   :1530-1587, :1714-1749; Triton twin thor/packing.py:24-54.
+ * x: bf16 [rows, k] contiguous, k % 32 == 0.  packed: uint8 [rows, k/2];
+ * sf: uint8 [ceil(rows/128)*128, ceil(k/64)*4] in the 128x4 swizzled layout
+ * (sfa_offset, fp4_cutlass_linear.cu:686-690).  Division is IEEE
+ * round-to-nearest (the Triton variant). */
+int pir2b_pack_nvfp4(const void *x, int64_t rows, int64_t k, void *packed,
+                     void *sf, void *stream);
+
+/* NVFP4 GEMM on tcgen05 kind::mxf4nvf4 (block16 UE4M3 scales), fp32
+ * accumulate, out = bf16(alpha * acc [+ bias]).
+ * Replaces linear_forward_packed_gemm_bf16_tactic
+ *   coexecution/kernels/blackwell/csrc/fp4_cutlass_linear.cu:1751-1847.
+ * qa [m, k/2] + sfa (swizzled, rows padded to 128); qw [n, k/2] + sfw;
+ * bias bf16 [n] or NULL; out bf16 [m, ldo]. k % 64 == 0, n % 32 == 0. */
+int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
+                     const void *sfw, const void *bias, float alpha,
+                     int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,
+                     void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PIR2B_H */

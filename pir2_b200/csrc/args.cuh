@@ -1,0 +1,68 @@
+// Argument blocks shared between the C ABI (capi.cu) and the kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace pir2b {
+
+struct QuantArgs {
+  const __nv_bfloat16 *x;   // [rows, ldx]
+  int64_t ldx;
+  const __nv_bfloat16 *up;  // [rows, ldu] (gated mode) or null
+  int64_t ldu;
+  const uint16_t *lut;      // bf16 bits [65536] or null
+  const float *smooth;      // [k] or null
+  uint8_t *q;
+  float *scales;
+  int k;
+  int kpad;
+  int mode;
+};
+
+struct NormArgs {
+  const __nv_bfloat16 *x;        // [rows, k]
+  const __nv_bfloat16 *y_in;     // [rows, k] or null
+  const __nv_bfloat16 *gate;     // [rows / tokens, ld_mod] or null (= 1)
+  __nv_bfloat16 *res_out;        // [rows, k] or null
+  const __nv_bfloat16 *gamma;    // [k] (RMS)
+  const __nv_bfloat16 *scale;    // [rows / tokens, ld_mod] or null
+  const __nv_bfloat16 *shift;
+  const float *smooth;
+  uint8_t *q;
+  uint8_t *scales;               // fp32 [rows] or NVFP4 swizzled bytes
+  int64_t ld_mod;
+  int64_t tokens;
+  int k;
+  int kpad;
+  float eps;
+};
+
+struct GemmArgs {
+  const float *sa;                  // [M] activation row scales
+  const float *sw;                  // [Npad] weight channel scales
+  const __nv_bfloat16 *bias;        // [Npad] or null
+  const __nv_bfloat16 *out_lut;     // [65536] activation table or null
+  __nv_bfloat16 *out;               // [M, ldo]
+  int64_t ldo;                      // output row stride (elements)
+  int m;                            // token rows
+  int n_store;                      // channels written (<= Npad)
+  int num_kb;                       // K blocks of 128 elements
+  int bias_mode;                    // 0: none, 1: add +0, 2: add bias
+  int bn;                           // token tile (multiple of 16, <= 256)
+  int stages;                       // pipeline depth
+  int splits;                       // cluster size along z (1,2,4,8)
+};
+
+cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
+                           bool vec, cudaStream_t st);
+cudaError_t run_norm_quant(const NormArgs &a, int out_format, int64_t rows,
+                           int norm, bool mod, bool res, cudaStream_t st);
+
+template <int kBits>
+__global__ void gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w,
+                               const __grid_constant__ CUtensorMap tm_a,
+                               const GemmArgs args);
+
+} // namespace pir2b

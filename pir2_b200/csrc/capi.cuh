@@ -1,0 +1,461 @@
+// C ABI of the library (include/pir2b.h): argument validation, tile-shape
+// selection, TMA tensor-map encoding and kernel launches.  Nothing here
+// allocates device memory or synchronizes, so every entry point can be
+// captured into a CUDA graph once the library is loaded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/pir2b.h"
+#pragma once
+#include "args.cuh"
+#include "ptx.cuh"
+
+namespace pir2b {
+
+
+
+
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_last_error[512] = "";
+
+static int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int cuda_status(cudaError_t e, const char *what) {
+  if (e == cudaSuccess)
+    return PIR2B_OK;
+  return fail(PIR2B_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static bool aligned(const void *p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+// ------------------------------------------------------------------ device info
+struct DeviceInfo {
+  int sms = 0;
+  int max_smem = 0;
+  bool attrs_set = false;
+};
+
+static std::mutex g_mutex;
+static DeviceInfo g_devices[64];
+
+static int device_info(DeviceInfo **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64)
+    return fail(PIR2B_EINVAL, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceInfo &d = g_devices[dev];
+  if (d.sms == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return fail(PIR2B_EINVAL,
+                  "pir2b kernels are built for sm_100a (B200); device %d is "
+                  "sm_%d%d",
+                  dev, major, minor);
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.max_smem,
+                           cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  }
+  if (!d.attrs_set) {
+    e = cudaFuncSetAttribute(gemm_i8_kernel<8>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             d.max_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_i8_kernel<4>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               d.max_smem);
+    if (e != cudaSuccess)
+      return cuda_status(e, "cudaFuncSetAttribute");
+    d.attrs_set = true;
+  }
+  *out = &d;
+  return PIR2B_OK;
+}
+
+// ------------------------------------------------------------------ TMA maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t,
+                                  void *, const cuuint64_t *, const cuuint64_t *,
+                                  const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault,
+                                &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D uint8 map over a row-major [rows, cols] byte matrix, box [box_rows,
+// box_cols] (box_cols bytes innermost).
+static int make_map(CUtensorMap *map, const void *base, uint64_t cols,
+                    uint64_t rows, uint64_t row_bytes, uint32_t box_cols,
+                    uint32_t box_rows, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr)
+    return fail(PIR2B_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                  const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PIR2B_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return PIR2B_OK;
+}
+
+// ------------------------------------------------------------------ GEMM plan
+struct GemmPlan {
+  int bn, mtiles, splits, stages;
+  size_t smem;
+};
+
+static size_t gemm_smem(int bits, int bn, int stages) {
+  const size_t stage = 16384 + size_t(bn) * 128;
+  const size_t packed = bits == 4 ? ((size_t(128 + bn) * 64 + 1023) & ~size_t(1023)) : 0;
+  return 1024 + stages * (stage + packed) + (4 * stages + 1) * 8 + 16;
+}
+
+static int stages_for(int bits, int bn, int max_smem) {
+  int s = 8;
+  while (s > 2 && gemm_smem(bits, bn, s) > size_t(max_smem))
+    --s;
+  return s;
+}
+
+// Picks the token tile, number of token tiles and the split-K cluster size
+// with a small cost model: per-CTA cycles ~ (K blocks / split) *
+// (fixed weight-tile cost + per-token cost) + epilogue, times the number of
+// waves over the SMs.
+static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
+                          int sms, int max_smem) {
+  const int ntiles = int((npad + 127) / 128);
+  const int num_kb = int(kpad / 128);
+  GemmPlan best{16, 1, 1, 2, 0};
+  double best_cost = 1e30;
+  const int mt0 = int((m + 255) / 256);
+  for (int mt = mt0; mt <= mt0 + 3; ++mt) {
+    int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
+    if (bn > 256 || bn < 16)
+      continue;
+    if (int64_t(mt - 1) * bn >= m)
+      continue;  // an empty token tile
+    const int stages = stages_for(bits, bn, max_smem);
+    if (size_t(stages) * (16384 + size_t(bn) * 128) < size_t(bn) * 512)
+      continue;  // split-K partials must fit in the stage buffers
+    for (int s = 1; s <= 8; s *= 2) {
+      if (s > num_kb)
+        break;
+      const int ctas = ntiles * mt * s;
+      const int waves = (ctas + sms - 1) / sms;
+      const double kb = double(num_kb) / s;
+      const double per_cta = kb * (700.0 + 6.0 * bn) + 1500.0 +
+                             (s > 1 ? 2.0 * bn * 128 / 32 : 0.0);
+      const double cost = waves * per_cta;
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = GemmPlan{bn, mt, s, stages, gemm_smem(bits, bn, stages)};
+      }
+    }
+  }
+  return best;
+}
+
+} // namespace pir2b
+
+using namespace pir2b;
+
+extern "C" {
+
+int pir2b_version(void) { return 100; }
+
+const char *pir2b_last_error(void) { return g_last_error; }
+
+int pir2b_device_status(int *status_out, void *stream) {
+  if (status_out == nullptr)
+    return fail(PIR2B_EINVAL, "status_out is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int value = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&value, g_device_status,
+                                            sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess)
+    e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess)
+    return cuda_status(e, "reading the device status word");
+  if (value != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(int), 0,
+                                cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+      e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+      return cuda_status(e, "clearing the device status word");
+  }
+  *status_out = value;
+  return PIR2B_OK;
+}
+
+int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
+                     const void *lut, const float *smooth, int mode, int bits,
+                     int64_t rows, int64_t k, void *q, float *scales,
+                     void *stream) {
+  if (bits != 4 && bits != 8)
+    return fail(PIR2B_EINVAL, "bits must be 4 or 8, got %d", bits);
+  if (mode < 0 || mode > 2)
+    return fail(PIR2B_EINVAL, "mode must be 0, 1 or 2, got %d", mode);
+  if (k < 1 || k > 65536)
+    return fail(PIR2B_EINVAL, "row width k=%lld outside [1, 65536]",
+                (long long)k);
+  if (rows < 0 || rows > 0x7fffffffLL)
+    return fail(PIR2B_EINVAL, "row count %lld out of range", (long long)rows);
+  if (rows == 0)
+    return PIR2B_OK;
+  if (x == nullptr || q == nullptr || scales == nullptr)
+    return fail(PIR2B_EINVAL, "x, q and scales must be non-null");
+  if (ldx < k || (mode == 1 && ldu < k))
+    return fail(PIR2B_EINVAL, "row stride smaller than the row width");
+  if (mode != 0 && lut == nullptr)
+    return fail(PIR2B_EINVAL, "mode %d needs a 65536-entry bf16 lookup table",
+                mode);
+  if (mode == 1 && up == nullptr)
+    return fail(PIR2B_EINVAL, "mode 1 needs the multiplier rows (up)");
+  if (!aligned(x, 2) || (up && !aligned(up, 2)) || !aligned(q, 16) ||
+      !aligned(scales, 4) || (lut && !aligned(lut, 2)) ||
+      (smooth && !aligned(smooth, 4)))
+    return fail(PIR2B_EALIGN, "pointer alignment not met");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  QuantArgs a;
+  a.x = static_cast<const __nv_bfloat16 *>(x);
+  a.ldx = ldx;
+  a.up = mode == 1 ? static_cast<const __nv_bfloat16 *>(up) : nullptr;
+  a.ldu = ldu;
+  a.lut = static_cast<const uint16_t *>(lut);
+  a.smooth = smooth;
+  a.q = static_cast<uint8_t *>(q);
+  a.scales = scales;
+  a.k = int(k);
+  a.kpad = int((k + 127) / 128 * 128);
+  a.mode = mode;
+  const bool vec = (k % 8 == 0) && (ldx % 8 == 0) && aligned(x, 16) &&
+                   (mode != 1 || ((ldu % 8 == 0) && aligned(up, 16)));
+  return cuda_status(
+      run_quant_rows(a, bits, rows, vec, static_cast<cudaStream_t>(stream)),
+      "quant_rows launch");
+}
+
+int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
+                          void *res_out, const void *gamma, const void *scale,
+                          const void *shift, int64_t ld_mod, int64_t tokens,
+                          const float *smooth, int norm_kind, float eps,
+                          int out_format, int64_t rows, int64_t k, void *q,
+                          void *scales, void *stream) {
+  if (out_format != PIR2B_OUT_INT8 && out_format != PIR2B_OUT_INT4 &&
+      out_format != PIR2B_OUT_NVFP4)
+    return fail(PIR2B_EINVAL, "out_format must be 8, 4 or 16, got %d",
+                out_format);
+  if (norm_kind < 0 || norm_kind > 2)
+    return fail(PIR2B_EINVAL, "norm_kind must be 0, 1 or 2");
+  if (k < 8 || k > 8192 || k % 8 != 0)
+    return fail(PIR2B_EINVAL,
+                "fused producers need k %% 8 == 0 and 8 <= k <= 8192 (k=%lld)",
+                (long long)k);
+  if (out_format == PIR2B_OUT_NVFP4 && k % 32 != 0)
+    return fail(PIR2B_EINVAL, "NVFP4 output needs k %% 32 == 0 (k=%lld)",
+                (long long)k);
+  if (rows < 0 || rows > 0x7fffffffLL)
+    return fail(PIR2B_EINVAL, "row count out of range");
+  if (rows == 0)
+    return PIR2B_OK;
+  const bool mod = scale != nullptr;
+  const bool res = y_in != nullptr;
+  if (x == nullptr || q == nullptr || scales == nullptr)
+    return fail(PIR2B_EINVAL, "x, q and scales must be non-null");
+  if (mod != (shift != nullptr))
+    return fail(PIR2B_EINVAL, "modulation needs both scale and shift");
+  if (res && res_out == nullptr)
+    return fail(PIR2B_EINVAL, "a residual input needs res_out");
+  if (norm_kind == PIR2B_NORM_RMS && gamma == nullptr)
+    return fail(PIR2B_EINVAL, "RMSNorm needs gamma");
+  if (norm_kind != PIR2B_NORM_NONE && !(eps > 0.f))
+    return fail(PIR2B_EINVAL, "epsilon must be positive");
+  if ((mod || gate) && (tokens < 1 || ld_mod < k || ld_mod % 8 != 0))
+    return fail(PIR2B_EINVAL,
+                "modulation rows need tokens >= 1 and ld_mod >= k, %% 8 == 0");
+  if (tokens < 1)
+    tokens = 1;
+  const void *ptrs16[] = {x, y_in, gate, res_out, gamma, scale, shift, q};
+  for (const void *p : ptrs16)
+    if (p && !aligned(p, 16))
+      return fail(PIR2B_EALIGN, "producer operands must be 16-byte aligned");
+  if (!aligned(scales, 4) || (smooth && !aligned(smooth, 4)))
+    return fail(PIR2B_EALIGN, "scale/smoothing pointer alignment not met");
+  if (res && norm_kind == PIR2B_NORM_NONE)
+    return fail(PIR2B_EINVAL, "a residual input needs a norm");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  NormArgs a;
+  a.x = static_cast<const __nv_bfloat16 *>(x);
+  a.y_in = static_cast<const __nv_bfloat16 *>(y_in);
+  a.gate = static_cast<const __nv_bfloat16 *>(gate);
+  a.res_out = static_cast<__nv_bfloat16 *>(res_out);
+  a.gamma = static_cast<const __nv_bfloat16 *>(gamma);
+  a.scale = static_cast<const __nv_bfloat16 *>(scale);
+  a.shift = static_cast<const __nv_bfloat16 *>(shift);
+  a.smooth = smooth;
+  a.q = static_cast<uint8_t *>(q);
+  a.scales = static_cast<uint8_t *>(scales);
+  a.ld_mod = ld_mod;
+  a.tokens = tokens;
+  a.k = int(k);
+  a.kpad = out_format == PIR2B_OUT_NVFP4 ? int(k) : int((k + 127) / 128 * 128);
+  a.eps = eps;
+  return cuda_status(run_norm_quant(a, out_format, rows, norm_kind, mod, res,
+                                    static_cast<cudaStream_t>(stream)),
+                     "norm_quant_rows launch");
+}
+
+int pir2b_pack_nvfp4(const void *x, int64_t rows, int64_t k, void *packed,
+                     void *sf, void *stream) {
+  return pir2b_norm_quant_rows(x, nullptr, nullptr, nullptr, nullptr, nullptr,
+                               nullptr, 0, 1, nullptr, PIR2B_NORM_NONE, 0.f,
+                               PIR2B_OUT_NVFP4, rows, k, packed, sf, stream);
+}
+
+int pir2b_gemm(const void *qa, const float *sa, const void *qw,
+               const float *sw, const void *bias, int bias_mode,
+               const void *out_lut, int bits, int64_t m, int64_t npad,
+               int64_t kpad, void *out, int64_t ldo, int64_t n_store,
+               int tactic, void *stream) {
+  (void)tactic;
+  if (bits != 4 && bits != 8)
+    return fail(PIR2B_EINVAL, "bits must be 4 or 8, got %d", bits);
+  if (bias_mode < 0 || bias_mode > 2)
+    return fail(PIR2B_EINVAL, "bias_mode must be 0, 1 or 2");
+  if (m < 1 || m > 0x7fffffffLL || npad < 8 || npad % 8 != 0 || kpad < 128 ||
+      kpad % 128 != 0 || npad > 0x7fffffffLL || kpad > (1LL << 20))
+    return fail(PIR2B_EINVAL,
+                "GEMM requires m >= 1, npad %% 8 == 0 and kpad %% 128 == 0 "
+                "(m=%lld npad=%lld kpad=%lld)",
+                (long long)m, (long long)npad, (long long)kpad);
+  if (n_store < 1 || n_store > npad || ldo < n_store)
+    return fail(PIR2B_EINVAL, "n_store must be in [1, npad] and ldo >= n_store");
+  if (qa == nullptr || sa == nullptr || qw == nullptr || sw == nullptr ||
+      out == nullptr)
+    return fail(PIR2B_EINVAL, "GEMM operands must be non-null");
+  if (bias_mode == PIR2B_BIAS_ADD && bias == nullptr)
+    return fail(PIR2B_EINVAL, "bias_mode ADD needs a bias vector");
+  if (!aligned(qa, 16) || !aligned(qw, 16))
+    return fail(PIR2B_EALIGN, "packed operands must be 16-byte aligned");
+  if (!aligned(out, 2) || !aligned(sa, 4) || !aligned(sw, 4) ||
+      (bias && !aligned(bias, 2)) || (out_lut && !aligned(out_lut, 2)))
+    return fail(PIR2B_EALIGN, "scale/bias/output alignment not met");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  const GemmPlan plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem);
+  const uint64_t row_bytes = bits == 8 ? uint64_t(kpad) : uint64_t(kpad / 2);
+  const uint32_t box_cols = bits == 8 ? 128u : 64u;
+  CUtensorMap tm_w, tm_a;
+  if (int r = make_map(&tm_w, qw, row_bytes, uint64_t(npad), row_bytes,
+                       box_cols, 128u, bits == 8))
+    return r;
+  if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, box_cols,
+                       uint32_t(plan.bn), bits == 8))
+    return r;
+  GemmArgs args;
+  args.sa = sa;
+  args.sw = sw;
+  args.bias = bias_mode == PIR2B_BIAS_ADD
+                  ? static_cast<const __nv_bfloat16 *>(bias)
+                  : nullptr;
+  args.out_lut = static_cast<const __nv_bfloat16 *>(out_lut);
+  args.out = static_cast<__nv_bfloat16 *>(out);
+  args.ldo = ldo;
+  args.m = int(m);
+  args.n_store = int(n_store);
+  args.num_kb = int(kpad / 128);
+  args.bias_mode = bias_mode;
+  args.bn = plan.bn;
+  args.stages = plan.stages;
+  args.splits = plan.splits;
+
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(unsigned((npad + 127) / 128), unsigned(plan.mtiles),
+                     unsigned(plan.splits));
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = unsigned(plan.splits);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = bits == 8
+                      ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, args)
+                      : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, args);
+  return cuda_status(e, "gemm launch");
+}
+
+int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
+                     const void *sfw, const void *bias, float alpha,
+                     int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,
+                     void *stream) {
+  (void)qa; (void)sfa; (void)qw; (void)sfw; (void)bias; (void)alpha;
+  (void)m; (void)n; (void)k; (void)out; (void)ldo; (void)stream;
+  return fail(PIR2B_EINVAL, "pir2b_gemm_nvfp4: NVFP4 GEMM kernel not built");
+}
+
+// Plan introspection for tests and the benchmark (not part of the public
+// header's contract; exported for diagnostics).
+int pir2b_gemm_plan(int bits, int64_t m, int64_t npad, int64_t kpad,
+                    int sms, int *bn, int *mtiles, int *splits, int *stages) {
+  const GemmPlan p = plan_gemm(bits, m, npad, kpad, sms, 232448);
+  *bn = p.bn;
+  *mtiles = p.mtiles;
+  *splits = p.splits;
+  *stages = p.stages;
+  return PIR2B_OK;
+}
+
+} // extern "C"

@@ -1,0 +1,322 @@
+// W8A8 / W4A4 GEMM on the 5th-generation tensor cores (tcgen05 kind::i8).
+//
+// Computes, for the symmetric-row-v1 format
+//   acc[m, n] = sum_k qa[m, k] * qw[n, k]                (exact int32)
+//   y[m, n]   = bf16_rn( (f32_rn(f32_rn(i2f_rn(acc) * sa[m]) * sw[n])) [+ b] )
+// which is the epilogue order of piR2's pir2_integer::gemm
+// (coexecution/kernels/ampere_ada/csrc/integer_gemm.cu:37-59, accumulator
+// times the per-row scale, times the per-column scale, plus the BF16 bias,
+// one round-to-nearest per step) and of the explicit torch formula the
+// reference pins it with (tests/gpu/test_quantization_gpu.py:37-44).
+//
+// Layout of the work:
+//  * the weight matrix is the UMMA "A" operand: one CTA owns 128 output
+//    channels (UMMA_M = 128) and a tile of BN tokens (UMMA_N = BN, 16..256),
+//    so the accumulator tile lives in TMEM as 128 lanes (channels) x BN
+//    columns (tokens).  Small token counts therefore cost no padding of the
+//    weight stream, which is what bounds robot-control GEMMs;
+//  * both operands are K-major; TMA brings 128-byte K slices with the
+//    128-byte swizzle straight into the canonical UMMA shared-memory layout;
+//  * warp 0 issues TMA, warp 1 owns TMEM and issues MMAs from one thread,
+//    warps 2..5 read TMEM and run the epilogue (and, for W4A4, unpack int4
+//    to int8 in shared memory during the main loop);
+//  * split-K runs as a thread-block cluster along grid z; each CTA reduces a
+//    channel slice of the cluster's partial sums through distributed shared
+//    memory, so no global workspace is needed and the int32 sum stays exact.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#pragma once
+#include "args.cuh"
+#include "ptx.cuh"
+
+namespace pir2b {
+
+
+constexpr int kThreads = 192;
+constexpr int kTileN = 128;          // channels per CTA (UMMA_M)
+constexpr int kBlockK = 128;         // K elements per stage
+constexpr int kWeightTileBytes = kTileN * kBlockK;  // 16 KB int8
+
+__device__ __forceinline__ __nv_bfloat16 epilogue_value(int acc, float sa,
+                                                        float sw, float bias,
+                                                        int bias_mode,
+                                                        const uint16_t *lut) {
+  float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
+  if (bias_mode != 0)
+    y = __fadd_rn(y, bias);
+  __nv_bfloat16 o = __float2bfloat16_rn(y);
+  if (lut != nullptr) {
+    uint16_t bits = __bfloat16_as_ushort(o);
+    o = __ushort_as_bfloat16(__ldg(lut + bits));
+  }
+  return o;
+}
+
+// Unpacks a stage of low-nibble-first int4 bytes into sign-extended int8,
+// written in the 128-byte-swizzled K-major layout UMMA reads.  `src` holds
+// `rows` rows of 64 packed bytes (128 int4 values); `dst` holds `rows` rows
+// of 128 bytes.
+__device__ __forceinline__ uint32_t sext_nibbles(uint32_t v) {
+  // Each byte of v holds a value 0..15 (two's-complement int4); return the
+  // sign-extended int8 in every byte. ((v ^ 8) + 0x78) ^ 0x80 == v - 16*(v>=8)
+  // with no carry between bytes.
+  return (((v ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u);
+}
+
+__device__ __forceinline__ void unpack_int4_stage(const uint8_t *src,
+                                                  uint8_t *dst, int rows,
+                                                  int tid, int nthreads) {
+  // 16 packed bytes -> 32 int8 = two 16-byte chunks of one row.
+  const int pieces = rows * 4;
+  for (int p = tid; p < pieces; p += nthreads) {
+    const int row = p >> 2;
+    const int part = p & 3;
+    const uint4 w = *reinterpret_cast<const uint4 *>(src + row * 64 + part * 16);
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo = sext_nibbles(words[i] & 0x0F0F0F0Fu);
+      const uint32_t hi = sext_nibbles((words[i] >> 4) & 0x0F0F0F0Fu);
+      out[2 * i] = __byte_perm(lo, hi, 0x5140);
+      out[2 * i + 1] = __byte_perm(lo, hi, 0x7362);
+    }
+    uint8_t *rowp = dst + row * 128;
+    const int c0 = (2 * part) ^ (row & 7);
+    const int c1 = (2 * part + 1) ^ (row & 7);
+    *reinterpret_cast<uint4 *>(rowp + c0 * 16) =
+        make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4 *>(rowp + c1 * 16) =
+        make_uint4(out[4], out[5], out[6], out[7]);
+  }
+}
+
+// kBits == 8: operands arrive as int8 through TMA in the swizzled layout.
+// kBits == 4: operands arrive as packed int4 (64 bytes per row and K block,
+// no swizzle) and the four epilogue warps unpack them per stage.
+template <int kBits>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_a,
+                   const GemmArgs args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzle atoms.
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int bn = args.bn;
+  const int stages = args.stages;
+  const int op_a_bytes = kWeightTileBytes;        // unpacked int8 weight tile
+  const int op_b_bytes = bn * kBlockK;            // unpacked int8 token tile
+  const int stage_bytes = op_a_bytes + op_b_bytes;
+  // W4A4 keeps the packed TMA destination next to the unpacked operands.
+  const int packed_bytes = (kBits == 4) ? (kTileN + bn) * 64 : 0;
+  const int packed_stride = (packed_bytes + 1023) & ~1023;
+  uint8_t *packed_base = smem + stages * stage_bytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(packed_base +
+                                                stages * packed_stride);
+  uint64_t *full = bars;                  // TMA -> consumer
+  uint64_t *empty = bars + stages;        // MMA done -> producer
+  uint64_t *ready = bars + 2 * stages;    // (W4A4) unpacked -> MMA
+  uint64_t *accum_full = bars + 3 * stages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * stages + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kTileN;
+  const int m0 = blockIdx.y * bn;
+  const int split = blockIdx.z;
+  const int kb_begin = (split * args.num_kb) / args.splits;
+  const int kb_end = ((split + 1) * args.num_kb) / args.splits;
+  const int nkb = kb_end - kb_begin;
+  const uint32_t tmem_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&ready[s], 128);
+    }
+    mbar_init(accum_full, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_a);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      const uint64_t wpolicy = policy_evict_first();
+      const uint32_t tx = (kBits == 8) ? uint32_t(stage_bytes)
+                                       : uint32_t((kTileN + bn) * 64);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        const uint32_t phase = (i / stages) & 1;
+        if (!mbar_wait(&empty[s], phase ^ 1, kStatusTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(&full[s], tx);
+        const int kx = (kb_begin + i) * (kBits == 8 ? kBlockK : 64);
+        if (kBits == 8) {
+          uint8_t *a = smem + s * stage_bytes;
+          tma_load_2d_hint(a, &tm_w, &full[s], kx, n0, wpolicy);
+          tma_load_2d(a + op_a_bytes, &tm_a, &full[s], kx, m0);
+        } else {
+          uint8_t *p = packed_base + s * packed_stride;
+          tma_load_2d_hint(p, &tm_w, &full[s], kx, n0, wpolicy);
+          tma_load_2d(p + kTileN * 64, &tm_a, &full[s], kx, m0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (elect_one_sync()) {
+      const uint32_t idesc = idesc_i8(kTileN, bn);
+      bool ok = true;
+      for (int i = 0; i < nkb && ok; ++i) {
+        const int s = i % stages;
+        const uint32_t phase = (i / stages) & 1;
+        ok = (kBits == 8) ? mbar_wait(&full[s], phase, kStatusTimeoutMma)
+                          : mbar_wait(&ready[s], phase, kStatusTimeoutMma);
+        if (!ok)
+          break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
+        const uint32_t b_addr = a_addr + op_a_bytes;
+#pragma unroll
+        for (int k = 0; k < kBlockK / 32; ++k) {
+          mma_i8(tmem_base, smem_desc_sw128(a_addr + k * 32),
+                 smem_desc_sw128(b_addr + k * 32), idesc,
+                 (i > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);
+      }
+      // Always signal the epilogue; the commit also orders every MMA issued
+      // so far, so TMEM is quiescent once the epilogue has seen it.
+      mma_commit(accum_full);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int et = threadIdx.x - 64;   // 0..127
+    if (kBits == 4) {
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        const uint32_t phase = (i / stages) & 1;
+        if (!mbar_wait(&full[s], phase, kStatusTimeoutConvert))
+          break;
+        const uint8_t *p = packed_base + s * packed_stride;
+        uint8_t *a = smem + s * stage_bytes;
+        unpack_int4_stage(p, a, kTileN, et, 128);
+        unpack_int4_stage(p + kTileN * 64, a + op_a_bytes, bn, et, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&ready[s]);
+      }
+    }
+    const bool have_acc = mbar_wait(accum_full, 0, kStatusTimeoutEpilogue);
+    tc_fence_after();
+    const int quarter = warp & 3;
+    const int ch = quarter * 32 + lane;       // channel within the tile
+    const int c = n0 + ch;
+    const int valid_m = min(bn, args.m - m0);
+    if (have_acc) {
+      if (args.splits == 1) {
+        const float sw = (c < args.n_store) ? __ldg(args.sw + c) : 0.f;
+        const float b = (args.bias_mode == 2 && c < args.n_store)
+                            ? __bfloat162float(args.bias[c])
+                            : 0.f;
+        const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
+        for (int j0 = 0; j0 < bn; j0 += 16) {
+          uint32_t r[16];
+          tmem_ld_16(tmem_base + (uint32_t(quarter * 32) << 16) + j0, r);
+          tmem_ld_wait();
+          if (j0 < valid_m && c < args.n_store) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int j = j0 + i;
+              if (j < valid_m) {
+                const float sa = __ldg(args.sa + m0 + j);
+                args.out[int64_t(m0 + j) * args.ldo + c] = epilogue_value(
+                    int(r[i]), sa, sw, b, args.bias_mode, lut);
+              }
+            }
+          }
+        }
+      } else {
+        // Partial sums to shared memory as [token][channel] int32, reusing
+        // the (now idle) pipeline buffers.
+        int *part = reinterpret_cast<int *>(smem);
+        for (int j0 = 0; j0 < bn; j0 += 16) {
+          uint32_t r[16];
+          tmem_ld_16(tmem_base + (uint32_t(quarter * 32) << 16) + j0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            part[(j0 + i) * kTileN + ch] = int(r[i]);
+        }
+      }
+    }
+  }
+
+  if (args.splits > 1) {
+    // Every thread of every CTA in the cluster takes part in both barriers.
+    cluster_sync();
+    if (warp >= 2) {
+      const int et = threadIdx.x - 64;
+      const uint32_t rank = cluster_ctarank();
+      const int slice = kTileN / args.splits;        // channels per rank
+      const int quads = slice / 4;
+      const int valid_m = min(bn, args.m - m0);
+      const uint32_t part_addr = smem_u32(smem);
+      const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
+      for (int idx = et; idx < valid_m * quads; idx += 128) {
+        const int j = idx / quads;
+        const int cq = rank * slice + (idx % quads) * 4;
+        int4 acc = make_int4(0, 0, 0, 0);
+        const uint32_t off = part_addr + uint32_t((j * kTileN + cq) * 4);
+        for (int p = 0; p < args.splits; ++p) {
+          const int4 v = ld_cluster_v4(map_peer(off, uint32_t(p)));
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        const float sa = __ldg(args.sa + m0 + j);
+        const int accs[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int cc = n0 + cq + e;
+          if (cc < args.n_store) {
+            const float b = args.bias_mode == 2
+                                ? __bfloat162float(args.bias[cc])
+                                : 0.f;
+            args.out[int64_t(m0 + j) * args.ldo + cc] = epilogue_value(
+                accs[e], sa, __ldg(args.sw + cc), b, args.bias_mode, lut);
+          }
+        }
+      }
+    }
+    cluster_sync();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tmem_cols);
+  }
+}
+
+
+
+
+} // namespace pir2b

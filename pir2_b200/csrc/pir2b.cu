@@ -1,0 +1,5 @@
+// Single translation unit of libpir2b.so: the kernels and the C ABI share
+// one definition of the device status word without relocatable device code.
+#include "quant.cuh"
+#include "gemm_i8.cuh"
+#include "capi.cuh"

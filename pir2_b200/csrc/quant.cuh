@@ -1,0 +1,546 @@
+// Activation producers: per-row symmetric int8/int4 quantization and packing
+// (symmetric-row-v1), fused with the optional LUT activation (GELU, SiLU*up),
+// SmoothQuant channel division, RMSNorm / non-affine LayerNorm, AdaLN
+// modulation and the gated residual add, plus the NVFP4 (E2M1 + UE4M3
+// block-16) output format.
+//
+// One CTA per row.  Each thread owns whole 8-element chunks (one 16-byte
+// load of bf16), strided by the block size, keeps the row in registers
+// across the reductions, and reduces with warp shuffles plus one
+// shared-memory hop.  Every BF16 rounding boundary of the reference
+// producers is kept (see the per-function citations).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#pragma once
+#include "args.cuh"
+#include "ptx.cuh"
+
+namespace pir2b {
+
+
+
+
+
+__device__ __forceinline__ float bf16r(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float lut_value(const uint16_t *lut,
+                                           __nv_bfloat16 x) {
+  return __bfloat162float(
+      __ushort_as_bfloat16(__ldg(lut + __bfloat16_as_ushort(x))));
+}
+
+// Block-wide reductions over blockDim.x (a multiple of 32, <= 1024).
+__device__ __forceinline__ float block_max(float v, float *red) {
+  for (int d = 16; d; d >>= 1)
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0)
+    red[w] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  v = l < nw ? red[l] : 0.f;
+  for (int d = 16; d; d >>= 1)
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+  return v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  for (int d = 16; d; d >>= 1)
+    v += __shfl_xor_sync(0xffffffffu, v, d);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0)
+    red[w] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  v = l < nw ? red[l] : 0.f;
+  for (int d = 16; d; d >>= 1)
+    v += __shfl_xor_sync(0xffffffffu, v, d);
+  return v;
+}
+
+// Loads 8 consecutive bf16 starting at column c0 of a row (zero past k).
+template <bool kVec>
+__device__ __forceinline__ void load8(const __nv_bfloat16 *row, int c0, int k,
+                                      __nv_bfloat16 (&v)[8]) {
+  if (kVec) {
+    if (c0 < k) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(row + c0));
+      const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = p[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = __ushort_as_bfloat16(0);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      v[i] = (c0 + i < k) ? row[c0 + i] : __ushort_as_bfloat16(0);
+  }
+}
+
+// Quantize 8 values with the row scale and store them (int8: 8 bytes at
+// q + c0; int4: 4 bytes at q + c0 / 2, low nibble = even column).
+template <int kBits>
+__device__ __forceinline__ void store_codes(const float (&v)[8], float s,
+                                            uint8_t *qrow, int c0) {
+  constexpr int L = (1 << (kBits - 1)) - 1;
+  int c[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = __float2int_rn(__fdiv_rn(v[i], s));
+    c[i] = max(-L, min(L, r));
+  }
+  if (kBits == 8) {
+    uint32_t lo = (c[0] & 255) | ((c[1] & 255) << 8) | ((c[2] & 255) << 16) |
+                  (uint32_t(c[3] & 255) << 24);
+    uint32_t hi = (c[4] & 255) | ((c[5] & 255) << 8) | ((c[6] & 255) << 16) |
+                  (uint32_t(c[7] & 255) << 24);
+    *reinterpret_cast<uint2 *>(qrow + c0) = make_uint2(lo, hi);
+  } else {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      w |= uint32_t(c[i] & 15) << (4 * i);
+    *reinterpret_cast<uint32_t *>(qrow + c0 / 2) = w;
+  }
+}
+
+// Row scale from the absolute maximum: m * (1/L) as an fp32 multiply by the
+// fp32 constant, 1.0 for an all-zero row (integer.py:69-71,
+// integer_dispatch.cu:237).
+template <int kBits>
+__device__ __forceinline__ float row_scale(float m) {
+  constexpr float inv = 1.0f / float((1 << (kBits - 1)) - 1);
+  return m > 0.f ? __fmul_rn(m, inv) : 1.0f;
+}
+
+// ------------------------------------------------------------------ quant_rows
+// integer.py:27-94 (_activation_values, _prepare).
+template <int kBits, int kCpt, bool kVec>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const QuantArgs a) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int nchunks = a.kpad >> 3;
+  const __nv_bfloat16 *xr = a.x + int64_t(row) * a.ldx;
+  const __nv_bfloat16 *ur = a.up ? a.up + int64_t(row) * a.ldu : nullptr;
+  float v[kCpt][8];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j) {
+    const int chunk = threadIdx.x + j * blockDim.x;
+    const int c0 = chunk * 8;
+    __nv_bfloat16 xv[8];
+    load8<kVec>(xr, chunk < nchunks ? c0 : a.k, a.k, xv);
+    __nv_bfloat16 uv[8];
+    if (a.mode == 1)
+      load8<kVec>(ur, chunk < nchunks ? c0 : a.k, a.k, uv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float t;
+      if (a.mode == 0) {
+        t = __bfloat162float(xv[i]);
+      } else {
+        t = lut_value(a.lut, xv[i]);
+        if (a.mode == 1)
+          t = bf16r(__fmul_rn(t, __bfloat162float(uv[i])));
+      }
+      if (c0 + i >= a.k)
+        t = 0.f;
+      if (a.smooth != nullptr && c0 + i < a.k)
+        t = bf16r(__fdiv_rn(bf16r(t), __ldg(a.smooth + c0 + i)));
+      v[j][i] = t;
+      m = fmaxf(m, fabsf(t));
+    }
+  }
+  m = block_max(m, red);
+  const float s = row_scale<kBits>(m);
+  if (threadIdx.x == 0)
+    a.scales[row] = s;
+  uint8_t *qrow = a.q + int64_t(row) * (kBits == 8 ? a.kpad : a.kpad / 2);
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j) {
+    const int chunk = threadIdx.x + j * blockDim.x;
+    if (chunk < nchunks)
+      store_codes<kBits>(v[j], s, qrow, chunk * 8);
+  }
+}
+
+// Rows wider than 8192: pass 1 reduces the absolute maximum, pass 2
+// recomputes each value (same arithmetic) and stores the codes.
+template <int kBits, bool kVec>
+__device__ __forceinline__ void chunk_values(const QuantArgs &a,
+                                             const __nv_bfloat16 *xr,
+                                             const __nv_bfloat16 *ur,
+                                             int chunk, float (&v)[8]) {
+  const int c0 = chunk * 8;
+  __nv_bfloat16 xv[8], uv[8];
+  load8<kVec>(xr, c0, a.k, xv);
+  if (a.mode == 1)
+    load8<kVec>(ur, c0, a.k, uv);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float t;
+    if (a.mode == 0) {
+      t = __bfloat162float(xv[i]);
+    } else {
+      t = lut_value(a.lut, xv[i]);
+      if (a.mode == 1)
+        t = bf16r(__fmul_rn(t, __bfloat162float(uv[i])));
+    }
+    if (c0 + i >= a.k)
+      t = 0.f;
+    if (a.smooth != nullptr && c0 + i < a.k)
+      t = bf16r(__fdiv_rn(bf16r(t), __ldg(a.smooth + c0 + i)));
+    v[i] = t;
+  }
+}
+
+template <int kBits, bool kVec>
+__global__ void __launch_bounds__(512) quant_rows_stream_kernel(const QuantArgs a) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int nchunks = a.kpad >> 3;
+  const __nv_bfloat16 *xr = a.x + int64_t(row) * a.ldx;
+  const __nv_bfloat16 *ur = a.up ? a.up + int64_t(row) * a.ldu : nullptr;
+  float m = 0.f;
+  for (int chunk = threadIdx.x; chunk < nchunks; chunk += blockDim.x) {
+    float v[8];
+    chunk_values<kBits, kVec>(a, xr, ur, chunk, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m = fmaxf(m, fabsf(v[i]));
+  }
+  m = block_max(m, red);
+  const float s = row_scale<kBits>(m);
+  if (threadIdx.x == 0)
+    a.scales[row] = s;
+  uint8_t *qrow = a.q + int64_t(row) * (kBits == 8 ? a.kpad : a.kpad / 2);
+  for (int chunk = threadIdx.x; chunk < nchunks; chunk += blockDim.x) {
+    float v[8];
+    chunk_values<kBits, kVec>(a, xr, ur, chunk, v);
+    store_codes<kBits>(v, s, qrow, chunk * 8);
+  }
+}
+
+// ------------------------------------------------------------------ NVFP4
+// Per 16-element block: m = max|v|; s = m / 6 (1 if m == 0); e = e4m3_rn(min(s,
+// 448)); d = f32(e), or s when e decodes to 0; codes = e2m1_rn_satfinite(v *
+// (1 / d)).  thor/packing.py:24-54 (IEEE division variant).
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 p;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 p, %2, %1;\n\t"
+      "cvt.u32.u8 %0, p;\n\t}"
+      : "=r"(r)
+      : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cvt_e4m3(float v) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.f), "f"(v));
+  return r & 0xFFu;
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint32_t e) {
+  // e4m3fn: 1 sign, 4 exponent bits (bias 7), 3 mantissa bits; exact in fp32.
+  const uint32_t sign = (e & 0x80u) << 24, ex = (e >> 3) & 0xFu, man = e & 7u;
+  const float mag = ex == 0 ? __fmul_rn(float(man), 1.0f / 512.0f)
+                            : __uint_as_float(((ex + 120u) << 23) | (man << 20));
+  return __uint_as_float(__float_as_uint(mag) | sign);
+}
+
+__device__ __forceinline__ int64_t nvfp4_sf_offset(int64_t row, int64_t sf,
+                                                   int64_t blocks_k) {
+  // 128 rows x 4 factors per 512-byte atom (fp4_cutlass_linear.cu:686-690).
+  return ((row >> 7) * blocks_k << 9) + ((row & 31) << 4) +
+         (((row & 127) >> 5) << 2) + ((sf >> 2) << 9) + (sf & 3);
+}
+
+// One thread holds 8 values = half a 16-block; its neighbour lane holds the
+// other half (chunks 2b and 2b+1 belong to lanes 2l and 2l+1).
+__device__ __forceinline__ void store_nvfp4_chunk(const float (&v)[8],
+                                                  int64_t row, int chunk,
+                                                  int k, uint8_t *packed,
+                                                  uint8_t *sf) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    m = fmaxf(m, fabsf(v[i]));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  const float s = m > 0.f ? __fdiv_rn(m, 6.0f) : 1.0f;
+  const uint32_t e = cvt_e4m3(fminf(s, 448.0f));
+  float d = e4m3_to_f32(e);
+  if (!(d > 0.f))
+    d = s;
+  const float r = __fdiv_rn(1.0f, d);
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i += 2)
+    w |= cvt_e2m1x2(__fmul_rn(v[i], r), __fmul_rn(v[i + 1], r)) << (4 * i);
+  const int c0 = chunk * 8;
+  if (c0 < k) {
+    *reinterpret_cast<uint32_t *>(packed + row * (k / 2) + c0 / 2) = w;
+    if ((chunk & 1) == 0) {
+      const int64_t blocks_k = (k / 16 + 3) / 4;
+      sf[nvfp4_sf_offset(row, chunk / 2, blocks_k)] = uint8_t(e);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ norm
+// modulation.py:86-219 (AdaLN, LayerNorm + AdaLN, residual + LayerNorm +
+// AdaLN), producers.py:19-53 (RMSNorm tail), thor/packing.py:109-150, :395-415
+// (the same producers to NVFP4).
+template <int kOut, int kCpt, int kNorm, bool kMod, bool kRes>
+__global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nchunks = a.kpad >> 3;
+  const int64_t cond = row / a.tokens;
+  float v[kCpt][8];
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j) {
+    const int chunk = threadIdx.x + j * blockDim.x;
+    const int c0 = chunk < nchunks ? chunk * 8 : a.k;
+    __nv_bfloat16 xv[8];
+    load8<true>(a.x + row * a.k, c0, a.k, xv);
+    if (kRes) {
+      __nv_bfloat16 yv[8], gv[8];
+      load8<true>(a.y_in + row * a.k, c0, a.k, yv);
+      if (a.gate != nullptr)
+        load8<true>(a.gate + cond * a.ld_mod, c0, a.k, gv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        // A null gate is an ungated residual: bf16(y * 1) == y.
+        const float prod =
+            a.gate != nullptr
+                ? bf16r(__fmul_rn(__bfloat162float(yv[i]), __bfloat162float(gv[i])))
+                : __bfloat162float(yv[i]);
+        xv[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xv[i]), prod));
+      }
+      if (c0 < a.k) {
+        uint4 raw;
+        __nv_bfloat16 *p = reinterpret_cast<__nv_bfloat16 *>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          p[i] = xv[i];
+        *reinterpret_cast<uint4 *>(a.res_out + row * a.k + c0) = raw;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      v[j][i] = (c0 + i < a.k) ? __bfloat162float(xv[i]) : 0.f;
+  }
+  const float kf = float(a.k);
+  if (kNorm == 1) {
+    // RMSNorm: var = mean(x^2); n = bf16(x * rsqrt(var + eps)); v = bf16(n*g)
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        ss = __fadd_rn(ss, __fmul_rn(v[j][i], v[j][i]));
+    ss = block_sum(ss, red);
+    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, kf), a.eps));
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j) {
+      const int chunk = threadIdx.x + j * blockDim.x;
+      const int c0 = chunk < nchunks ? chunk * 8 : a.k;
+      __nv_bfloat16 gv[8];
+      load8<true>(a.gamma, c0, a.k, gv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float n = bf16r(__fmul_rn(v[j][i], inv));
+        v[j][i] = (c0 + i < a.k) ? bf16r(__fmul_rn(n, __bfloat162float(gv[i])))
+                                 : 0.f;
+      }
+    }
+  } else if (kNorm == 2) {
+    // Non-affine LayerNorm: mean, centred variance, n = bf16(c * rsqrt(var+eps))
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        sum = __fadd_rn(sum, v[j][i]);
+    sum = block_sum(sum, red);
+    const float mean = __fdiv_rn(sum, kf);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j) {
+      const int chunk = threadIdx.x + j * blockDim.x;
+      const int c0 = chunk < nchunks ? chunk * 8 : a.k;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float c = (c0 + i < a.k) ? __fsub_rn(v[j][i], mean) : 0.f;
+        v[j][i] = c;
+        ss = __fadd_rn(ss, __fmul_rn(c, c));
+      }
+    }
+    ss = block_sum(ss, red);
+    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, kf), a.eps));
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[j][i] = bf16r(__fmul_rn(v[j][i], inv));
+  }
+  if (kMod) {
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j) {
+      const int chunk = threadIdx.x + j * blockDim.x;
+      const int c0 = chunk < nchunks ? chunk * 8 : a.k;
+      __nv_bfloat16 sv[8], hv[8];
+      load8<true>(a.scale + cond * a.ld_mod, c0, a.k, sv);
+      load8<true>(a.shift + cond * a.ld_mod, c0, a.k, hv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float factor = bf16r(__fadd_rn(1.0f, __bfloat162float(sv[i])));
+        const float p = bf16r(__fmul_rn(v[j][i], factor));
+        const float t = bf16r(__fadd_rn(p, __bfloat162float(hv[i])));
+        v[j][i] = (c0 + i < a.k) ? t : 0.f;
+      }
+    }
+  }
+  if (a.smooth != nullptr) {
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j) {
+      const int chunk = threadIdx.x + j * blockDim.x;
+      const int c0 = chunk * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (chunk < nchunks && c0 + i < a.k)
+          v[j][i] = bf16r(__fdiv_rn(v[j][i], __ldg(a.smooth + c0 + i)));
+    }
+  }
+  if constexpr (kOut == 16) {
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j) {
+      const int chunk = threadIdx.x + j * blockDim.x;
+      // Every lane takes part in the pairwise shuffle; stores are guarded.
+      store_nvfp4_chunk(v[j], row, chunk < nchunks ? chunk : nchunks, a.k,
+                        a.q, a.scales);
+    }
+  } else {
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m = fmaxf(m, fabsf(v[j][i]));
+  m = block_max(m, red);
+  const float s = row_scale<kOut>(m);
+  if (threadIdx.x == 0)
+    reinterpret_cast<float *>(a.scales)[row] = s;
+  uint8_t *qrow = a.q + row * (kOut == 8 ? a.kpad : a.kpad / 2);
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j) {
+    const int chunk = threadIdx.x + j * blockDim.x;
+    if (chunk < nchunks)
+      store_codes<kOut>(v[j], s, qrow, chunk * 8);
+  }
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+// Threads per row: enough 8-wide chunks per thread to cover Kpad with at most
+// kCpt chunks each, a multiple of 32, at most 1024.
+static inline int pick_threads(int nchunks, int cpt) {
+  int t = (nchunks + cpt - 1) / cpt;
+  t = (t + 31) / 32 * 32;
+  return t < 32 ? 32 : t;
+}
+
+template <int kBits, int kCpt>
+static cudaError_t launch_quant(const QuantArgs &a, int64_t rows, bool vec,
+                                cudaStream_t st) {
+  const int threads = pick_threads(a.kpad / 8, kCpt);
+  if (vec)
+    quant_rows_kernel<kBits, kCpt, true><<<dim3(unsigned(rows)), threads, 0, st>>>(a);
+  else
+    quant_rows_kernel<kBits, kCpt, false><<<dim3(unsigned(rows)), threads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
+                           bool vec, cudaStream_t st) {
+  const int nchunks = a.kpad / 8;
+  // <= 256 threads with up to 4 chunks each covers Kpad <= 8192 with the row
+  // held in registers; wider rows (up to 65536) take two passes over x.
+  if (nchunks <= 256)
+    return bits == 8 ? launch_quant<8, 1>(a, rows, vec, st)
+                     : launch_quant<4, 1>(a, rows, vec, st);
+  if (nchunks <= 1024)
+    return bits == 8 ? launch_quant<8, 4>(a, rows, vec, st)
+                     : launch_quant<4, 4>(a, rows, vec, st);
+  if (vec) {
+    if (bits == 8)
+      quant_rows_stream_kernel<8, true><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
+    else
+      quant_rows_stream_kernel<4, true><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
+  } else {
+    if (bits == 8)
+      quant_rows_stream_kernel<8, false><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
+    else
+      quant_rows_stream_kernel<4, false><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+template <int kOut, int kCpt, int kNorm, bool kMod, bool kRes>
+static cudaError_t launch_norm4(const NormArgs &a, int64_t rows,
+                                cudaStream_t st) {
+  const int threads = pick_threads(a.kpad / 8, kCpt);
+  norm_quant_kernel<kOut, kCpt, kNorm, kMod, kRes>
+      <<<dim3(unsigned(rows)), threads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int kOut, int kCpt>
+static cudaError_t launch_norm3(const NormArgs &a, int64_t rows, int norm,
+                                bool mod, bool res, cudaStream_t st) {
+#define PIR2B_NORM_CASE(N, M, R)                                             \
+  if (norm == N && mod == M && res == R)                                     \
+    return launch_norm4<kOut, kCpt, N, M, R>(a, rows, st);
+  PIR2B_NORM_CASE(0, true, false)
+  PIR2B_NORM_CASE(1, false, false)
+  PIR2B_NORM_CASE(1, true, false)
+  PIR2B_NORM_CASE(2, false, false)
+  PIR2B_NORM_CASE(2, true, false)
+  PIR2B_NORM_CASE(2, true, true)
+  PIR2B_NORM_CASE(2, false, true)
+  PIR2B_NORM_CASE(0, false, false)
+  PIR2B_NORM_CASE(1, false, true)
+#undef PIR2B_NORM_CASE
+  return cudaErrorInvalidValue;
+}
+
+template <int kOut>
+static cudaError_t launch_norm2(const NormArgs &a, int64_t rows, int norm,
+                                bool mod, bool res, cudaStream_t st) {
+  const int nchunks = a.kpad / 8;
+  if (nchunks <= 256)
+    return launch_norm3<kOut, 1>(a, rows, norm, mod, res, st);
+  return launch_norm3<kOut, 4>(a, rows, norm, mod, res, st);
+}
+
+cudaError_t run_norm_quant(const NormArgs &a, int out_format, int64_t rows,
+                           int norm, bool mod, bool res, cudaStream_t st) {
+  if (out_format == 8)
+    return launch_norm2<8>(a, rows, norm, mod, res, st);
+  if (out_format == 4)
+    return launch_norm2<4>(a, rows, norm, mod, res, st);
+  return launch_norm2<16>(a, rows, norm, mod, res, st);
+}
+
+} // namespace pir2b

@@ -1,0 +1,171 @@
+"""Torch-facing wrappers of the C ABI: allocate outputs, validate, launch.
+
+Every function runs on the current CUDA stream of the input's device, never
+synchronizes and allocates only through torch's caching allocator, so all of
+them can be captured in CUDA graphs (after the library has been loaded once).
+Errors from the library are raised as ValueError (argument/alignment) or
+RuntimeError (CUDA); there is no fallback implementation.
+"""
+
+import torch
+
+from . import _lib
+
+KPAD_MULTIPLE = 128
+NPAD_MULTIPLE = 8
+
+
+def kpad(k):
+    return (k + KPAD_MULTIPLE - 1) // KPAD_MULTIPLE * KPAD_MULTIPLE
+
+
+def npad(n):
+    return (n + NPAD_MULTIPLE - 1) // NPAD_MULTIPLE * NPAD_MULTIPLE
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _rows(x):
+    """[rows, k] view and row stride of a tensor with unit last stride."""
+    k = x.shape[-1]
+    rows = x.numel() // k if k else 0
+    try:
+        matrix = x.view(rows, k)
+    except RuntimeError as error:
+        raise ValueError(
+            "Activation leading dimensions must form regularly strided rows"
+        ) from error
+    return matrix, rows, k, (matrix.stride(0) if rows > 1 else max(k, matrix.stride(0)))
+
+
+def quant_rows(x, bits, *, lut=None, up=None, smooth=None, out=None):
+    """symmetric-row-v1 activation pack of bf16 rows -> (data, scales).
+
+    mode: plain (no lut), LUT (lut only, e.g. GELU) or gated (lut and up,
+    v = bf16(lut[x] * up), e.g. SiLU(gate) * up).
+    """
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.stride(-1) != 1 or x.ndim < 2:
+        raise ValueError("Expected CUDA BF16 rows with unit feature stride")
+    matrix, rows, k, ldx = _rows(x)
+    mode = _lib.MODE_PLAIN if lut is None else (_lib.MODE_LUT if up is None else _lib.MODE_GATED)
+    ldu = 0
+    if up is not None:
+        if up.shape != x.shape or up.dtype != x.dtype or up.device != x.device or up.stride(-1) != 1:
+            raise ValueError("Invalid gated activation input")
+        _, _, _, ldu = _rows(up)
+    if lut is not None and (lut.numel() != 65536 or lut.dtype != torch.bfloat16 or not lut.is_contiguous()):
+        raise ValueError("Invalid activation lookup table")
+    pad = kpad(k)
+    if out is None:
+        data = torch.empty(
+            (rows, pad if bits == 8 else pad // 2),
+            device=x.device,
+            dtype=torch.int8 if bits == 8 else torch.uint8,
+        )
+        scales = torch.empty(rows, device=x.device, dtype=torch.float32)
+    else:
+        data, scales = out
+    status = _lib.lib().pir2b_quant_rows(
+        x.data_ptr(), ldx, _ptr(up), ldu, _ptr(lut), _ptr(smooth), mode, bits,
+        rows, k, data.data_ptr(), scales.data_ptr(), _stream(x.device),
+    )
+    _lib.check(status, "pir2b_quant_rows")
+    return data, scales
+
+
+def norm_quant_rows(
+    x,
+    out_format,
+    *,
+    norm=_lib.NORM_NONE,
+    eps=0.0,
+    gamma=None,
+    scale=None,
+    shift=None,
+    tokens=1,
+    y=None,
+    gate=None,
+    smooth=None,
+):
+    """Fused [residual +] [RMS|LN norm] [+ AdaLN] [/ smooth] -> pack.
+
+    x, y: contiguous bf16 [rows, k]; scale/shift/gate: bf16 rows indexed by
+    row // tokens with a shared row stride.  Returns (data, scales, residual)
+    where residual is the bf16 x + bf16(y * gate) when y is given.
+    """
+    if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
+        raise ValueError("Fused producers need contiguous CUDA BF16 input")
+    k = x.shape[-1]
+    rows = x.numel() // k
+    ld_mod = 0
+    for t in (scale, shift, gate):
+        if t is not None:
+            if t.dtype != torch.bfloat16 or t.device != x.device or t.stride(-1) != 1:
+                raise ValueError("Modulation operands must be CUDA BF16 with unit stride")
+            ld_mod = t.stride(-2) if t.ndim >= 2 and t.shape[-2] > 1 else k
+    if scale is not None and shift is not None and scale.stride(-2) != shift.stride(-2) and scale.shape[-2] > 1:
+        raise ValueError("Scale and shift must share a row stride")
+    residual = None
+    if y is not None:
+        if y.shape != x.shape or not y.is_contiguous() or y.dtype != x.dtype:
+            raise ValueError("Residual operand must match the contiguous BF16 input")
+        residual = torch.empty_like(x)
+    if out_format == _lib.OUT_NVFP4:
+        data = torch.empty((rows, k // 2), device=x.device, dtype=torch.uint8)
+        scales = torch.empty(
+            (-(-rows // 128) * 128, -(-(k // 16) // 4) * 4), device=x.device, dtype=torch.uint8
+        )
+    else:
+        pad = kpad(k)
+        data = torch.empty(
+            (rows, pad if out_format == 8 else pad // 2),
+            device=x.device,
+            dtype=torch.int8 if out_format == 8 else torch.uint8,
+        )
+        scales = torch.empty(rows, device=x.device, dtype=torch.float32)
+    status = _lib.lib().pir2b_norm_quant_rows(
+        x.data_ptr(), _ptr(y), _ptr(gate), _ptr(residual), _ptr(gamma), _ptr(scale),
+        _ptr(shift), ld_mod, tokens, _ptr(smooth), norm, float(eps), out_format,
+        rows, k, data.data_ptr(), scales.data_ptr(), _stream(x.device),
+    )
+    _lib.check(status, "pir2b_norm_quant_rows")
+    return data, scales, residual
+
+
+def gemm(a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, n_store=None, out=None, tactic=-1):
+    """Quantized GEMM + dequant epilogue -> bf16 [m, n_store] (or into `out`).
+
+    bias_mode defaults to piR2's `gemm` semantics: add the bias, or +0 when
+    the bias is None.  Pass _lib.BIAS_NONE for `gemm_biasless` without bias.
+    """
+    m = a.shape[0]
+    n_pad = w.shape[0]
+    k_pad = a.shape[1] * (2 if bits == 4 else 1)
+    if n_store is None:
+        n_store = n_pad
+    if bias_mode is None:
+        bias_mode = _lib.BIAS_ADD if bias is not None else _lib.BIAS_ZERO
+    if out is None:
+        out = torch.empty((m, n_store), device=a.device, dtype=torch.bfloat16)
+    ldo = out.stride(0) if out.ndim == 2 else n_store
+    if out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError("GEMM output must be BF16 with unit column stride")
+    status = _lib.lib().pir2b_gemm(
+        a.data_ptr(), sa.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias), bias_mode,
+        _ptr(out_lut), bits, m, n_pad, k_pad, out.data_ptr(), ldo, n_store, int(tactic),
+        _stream(a.device),
+    )
+    _lib.check(status, "pir2b_gemm")
+    return out
+
+
+def pack_nvfp4(x):
+    """NVFP4 pack of contiguous bf16 rows -> (packed [rows, k/2], swizzled sf)."""
+    data, scales, _ = norm_quant_rows(x.reshape(-1, x.shape[-1]).contiguous(), _lib.OUT_NVFP4)
+    return data, scales

@@ -1,0 +1,240 @@
+"""Generates tests/golden/golden.npz from the piR2 reference itself.
+
+Run in a container that has the reference checkout (not on the GPU box):
+    PIR2_REFERENCE=/path/to/piR2 python tests/golden/make_golden.py
+
+What it runs, unmodified, from the reference:
+  * the Triton activation quantizer `_prepare`
+    (coexecution/kernels/ampere_ada/integer.py:27-94), called with the
+    arguments of `prepare` (coexecution/optimization/backends/integer/
+    linear.py:51-90) and of `prepare_activation` (integer.py:107-173);
+  * the AdaLN / LayerNorm / residual producers `_prepare_modulation`,
+    `_prepare_norm_modulation`, `_prepare_residual_norm_modulation`
+    (coexecution/kernels/ampere_ada/modulation.py:123-219);
+  * the RMSNorm tail `_rms_tail_pack` (coexecution/kernels/ampere_ada/
+    producers.py:19-53);
+  * `channel_scales` (coexecution/optimization/backends/thor/smoothquant.py:
+    27-45), which is plain CPU torch;
+  * the explicit torch formula of the bitwise Linear test
+    (tests/gpu/test_quantization_gpu.py:37-44).
+
+The Triton kernels run under Triton's CPU interpreter (TRITON_INTERPRET=1).
+Two interpreter emulation gaps are closed first, so that the CPU run has the
+GPU's arithmetic: fp32 -> bf16 casts are made round-to-nearest-even (the
+interpreter truncates), and `libdevice.nearbyint` / `libdevice.rsqrt` are
+mapped to numpy (`rint`, and 1/sqrt).  Nothing in the reference is edited.
+"""
+
+import os
+import sys
+
+os.environ["TRITON_INTERPRET"] = "1"
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import triton  # noqa: E402
+import triton.language as tl  # noqa: E402
+from triton.runtime import interpreter as _interp  # noqa: E402
+
+REFERENCE = os.environ.get("PIR2_REFERENCE", "/root/reference")
+OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden.npz")
+
+_original_convert = _interp._convert_float
+
+
+def _convert_float(data, src, dst, rounding_mode):
+    if src == tl.float32 and dst == tl.bfloat16:
+        t = torch.from_numpy(np.ascontiguousarray(data).view(np.float32).copy())
+        return t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    if src == tl.bfloat16 and dst == tl.float32:
+        bits = np.ascontiguousarray(data).view(np.uint16).astype(np.uint32) << 16
+        return bits.view(np.float32)
+    return _original_convert(data, src, dst, rounding_mode)
+
+
+_interp._convert_float = _convert_float
+
+
+def _unary(fn):
+    def apply(x, _semantic=None):
+        data = x.handle.data
+        result = fn(data).astype(data.dtype)
+        return tl.tensor(_interp.TensorHandle(result, x.handle.dtype.scalar), x.type)
+
+    return apply
+
+
+class _Libdevice:
+    nearbyint = staticmethod(_unary(np.rint))
+    rsqrt = staticmethod(
+        _unary(lambda v: (1.0 / np.sqrt(v.astype(np.float64))).astype(np.float32))
+    )
+
+
+sys.path.insert(0, REFERENCE)
+from coexecution.kernels.ampere_ada import integer as ref_integer  # noqa: E402
+from coexecution.kernels.ampere_ada import modulation as ref_modulation  # noqa: E402
+from coexecution.kernels.ampere_ada import producers as ref_producers  # noqa: E402
+from coexecution.optimization.backends.thor.smoothquant import (  # noqa: E402
+    channel_scales,
+)
+
+for module in (ref_integer, ref_modulation, ref_producers):
+    module.libdevice = _Libdevice
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def gelu_lut(approximate):
+    values = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    return torch.nn.functional.gelu(values.float(), approximate=approximate).to(torch.bfloat16)
+
+
+def silu_lut():
+    values = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    return torch.nn.functional.silu(values.float()).to(torch.bfloat16)
+
+
+def run_prepare(x, bits_, lut=None, up=None, reuse=True):
+    """Reference `_prepare` with the argument list of `prepare` (REUSE=True)
+    or `prepare_activation` (REUSE=pack_reuse)."""
+    k = x.shape[-1]
+    rows = x.numel() // k
+    pad = triton.cdiv(k, 128) * 128
+    data = torch.empty(
+        (rows, pad if bits_ == 8 else pad // 2),
+        dtype=torch.int8 if bits_ == 8 else torch.uint8,
+    )
+    scales = torch.empty(rows, dtype=torch.float32)
+    mode = 0 if lut is None else 2 if up is None else 1
+    up_ = x if up is None else up
+    ref_integer._prepare[(rows,)](
+        x, up_, x if lut is None else lut, data, scales,
+        k, pad, bits_, mode, triton.next_power_of_2(pad), reuse,
+        x.view(rows, k).stride(0), up_.view(rows, k).stride(0),
+    )
+    return data.numpy().copy(), scales.numpy().copy()
+
+
+def outliers(g, rows, k, fraction=0.01, factor=20.0):
+    x = torch.randn(rows, k, generator=g)
+    cols = torch.randperm(k, generator=g)[: max(1, int(k * fraction))]
+    x[:, cols] *= factor
+    return x.to(torch.bfloat16)
+
+
+def main():
+    g = torch.Generator().manual_seed(0)
+    out = {}
+    lut_tanh = gelu_lut("tanh")
+    lut_silu = silu_lut()
+    out["lut_gelu_tanh"] = bits(lut_tanh)
+    out["lut_silu"] = bits(lut_silu)
+
+    cases = {
+        "k130": torch.randn(17, 130, generator=g).to(torch.bfloat16),
+        "k258": torch.randn(17, 258, generator=g).to(torch.bfloat16),
+        "k1": torch.randn(5, 1, generator=g).to(torch.bfloat16),
+        "k127": torch.randn(3, 127, generator=g).to(torch.bfloat16),
+        "outlier2048": outliers(g, 8, 2048),
+        "zeros": torch.zeros(2, 256, dtype=torch.bfloat16),
+    }
+    # A mixed row: exact zeros, large and tiny magnitudes, negative zero.
+    mixed = torch.randn(4, 384, generator=g) * torch.logspace(-6, 3, 384)
+    mixed[0] = 0.0
+    mixed[1, ::7] = -0.0
+    cases["mixed384"] = mixed.to(torch.bfloat16)
+    for name, x in cases.items():
+        out[f"x_{name}"] = bits(x)
+        for b in (8, 4):
+            for reuse in (True, False) if b == 4 else (True,):
+                q, s = run_prepare(x, b, reuse=reuse)
+                tag = f"{name}_b{b}" + ("" if reuse else "_noreuse")
+                out[f"q_plain_{tag}"], out[f"s_plain_{tag}"] = q, s
+
+    # LUT (GELU) and gated (SiLU*up / GELU*up) modes.
+    x = cases["k258"]
+    up = torch.randn(17, 258, generator=g).to(torch.bfloat16)
+    out["up_k258"] = bits(up)
+    for b in (8, 4):
+        out[f"q_gelu_k258_b{b}"], out[f"s_gelu_k258_b{b}"] = run_prepare(x, b, lut_tanh)
+        out[f"q_gelu_up_k258_b{b}"], out[f"s_gelu_up_k258_b{b}"] = run_prepare(x, b, lut_tanh, up)
+        out[f"q_silu_up_k258_b{b}"], out[f"s_silu_up_k258_b{b}"] = run_prepare(x, b, lut_silu, up)
+
+    # AdaLN producers on [B, T, D] = [2, 3, 64] (modulation.py:240-311).
+    bsz, tokens, k = 2, 3, 64
+    xm = torch.randn(bsz, tokens, k, generator=g).to(torch.bfloat16)
+    scale = (torch.randn(bsz, 1, k, generator=g) * 0.5).to(torch.bfloat16)
+    shift = (torch.randn(bsz, 1, k, generator=g) * 0.5).to(torch.bfloat16)
+    ym = torch.randn(bsz, tokens, k, generator=g).to(torch.bfloat16)
+    gate = torch.randn(bsz, 1, k, generator=g).to(torch.bfloat16)
+    out.update(
+        mod_x=bits(xm), mod_scale=bits(scale), mod_shift=bits(shift), mod_y=bits(ym), mod_gate=bits(gate)
+    )
+    rows, pad = bsz * tokens, 128
+    for b in (8, 4):
+        for kind in ("mod", "norm", "res"):
+            data = torch.empty((rows, pad if b == 8 else pad // 2), dtype=torch.int8 if b == 8 else torch.uint8)
+            scales = torch.empty(rows, dtype=torch.float32)
+            common = (xm, scale, shift, data, scales, k, pad, tokens, b, triton.next_power_of_2(pad))
+            if kind == "mod":
+                ref_modulation._prepare_modulation[(rows,)](*common)
+            elif kind == "norm":
+                ref_modulation._prepare_norm_modulation[(rows,)](*common, EPS=1e-6)
+            else:
+                residual = torch.empty_like(xm)
+                ref_modulation._prepare_residual_norm_modulation[(rows,)](
+                    *common, EPS=1e-6, Y=ym, GATE=gate, RESIDUAL=residual
+                )
+                out[f"res_r_b{b}"] = bits(residual)
+            out[f"{kind}_q_b{b}"], out[f"{kind}_s_b{b}"] = data.numpy().copy(), scales.numpy().copy()
+
+    # RMSNorm tail with the variance of torch's mean of squares.
+    xr = outliers(g, 6, 2048)
+    gamma = (1.0 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    variance = xr.float().pow(2).mean(-1)
+    out.update(rms_x=bits(xr), rms_gamma=bits(gamma), rms_var=variance.numpy().copy())
+    for b in (8, 4):
+        pad = 2048
+        data = torch.empty((6, pad if b == 8 else pad // 2), dtype=torch.int8 if b == 8 else torch.uint8)
+        scales = torch.empty(6, dtype=torch.float32)
+        ref_producers._rms_tail_pack[(6,)](xr, variance, gamma, data, scales, 2048, pad, 1e-6, b, 2048)
+        out[f"rms_q_b{b}"], out[f"rms_s_b{b}"] = data.numpy().copy(), scales.numpy().copy()
+
+    # SmoothQuant channel scales (config 1 shapes, reduced N for size).
+    xs = torch.randn(64, 2048, generator=g)
+    xs[:, torch.randperm(2048, generator=g)[:20]] *= 20.0
+    w = torch.randn(48, 2048, generator=g) * 0.02
+    w2 = torch.randn(24, 2048, generator=g) * 0.02
+    amax = xs.abs().amax(0)
+    out["sq_amax"] = amax.numpy().copy()
+    out["sq_w"] = w.numpy().copy()
+    out["sq_w2"] = w2.numpy().copy()
+    out["sq_scales_a05"] = channel_scales(amax, [w], 0.5).numpy().copy()
+    out["sq_scales_group_a08"] = channel_scales(amax, [w, w2], 0.8).numpy().copy()
+
+    # Explicit torch Linear formula of test_quantization_gpu.py:37-44 (K=130
+    # exercises padding), on CPU fp32.
+    torch.manual_seed(195)
+    linear = torch.nn.Linear(130, 64).to(torch.bfloat16)
+    xl = torch.randn(17, 130).to(torch.bfloat16)
+    out["lin_x"], out["lin_w"], out["lin_b"] = bits(xl), bits(linear.weight.detach()), bits(linear.bias.detach())
+    for b in (8, 4):
+        limit = 2 ** (b - 1) - 1
+        xs_ = xl.float().abs().amax(dim=-1) / limit
+        ws_ = linear.weight.float().abs().amax(dim=-1) / limit
+        qx = torch.round(xl.float() / xs_[:, None]).clamp(-limit, limit)
+        qw = torch.round(linear.weight.float() / ws_[:, None]).clamp(-limit, limit)
+        expected = ((qx @ qw.t()) * xs_[:, None] * ws_[None, :] + linear.bias.float()).to(torch.bfloat16)
+        out[f"lin_y_b{b}"] = bits(expected.detach())
+        out[f"lin_qw_b{b}"] = qw.to(torch.int8).numpy().copy()
+        out[f"lin_ws_b{b}"] = ws_.detach().numpy().copy()
+
+    np.savez_compressed(OUT, **out)
+    print(f"wrote {OUT}: {len(out)} arrays, {os.path.getsize(OUT)} bytes")
+
+
+if __name__ == "__main__":
+    main()

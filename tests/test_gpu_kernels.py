@@ -1,0 +1,237 @@
+"""Parity of the sm_100a kernels (called through the C ABI) with the oracle.
+
+Integer stages (codes, scales, int32 accumulators through the epilogue) and
+packed bytes are compared bitwise; fused norm producers within one
+quantization code (their reduction order differs from any reference order);
+NVFP4 packs bitwise against the oracle's IEEE-division restatement.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from pir2_b200 import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def bits_of(t):
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def to_dev(bits, device="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def device_lut(kind):
+    """Activation table built by torch on the device, as the reference does
+    (coexecution/kernels/common/fused.py:74-83, groot/integer.py:47-53)."""
+    values = torch.arange(65536, device="cuda", dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    if kind == "silu":
+        return torch.nn.functional.silu(values)
+    return torch.nn.functional.gelu(values, approximate=kind)
+
+
+def randn_bf16(g, *shape, outliers=False):
+    x = torch.randn(*shape, generator=g)
+    if outliers:
+        cols = torch.randperm(shape[-1], generator=g)[: max(1, shape[-1] // 100)]
+        x[..., cols] *= 20.0
+    return x.to(torch.bfloat16)
+
+
+def assert_status_clean():
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("rows,k", [(1, 2048), (17, 130), (5, 1), (3, 127), (64, 6144), (1024, 2048), (7, 12288), (2, 40000)])
+def test_quant_rows_plain_bitwise(bits, rows, k):
+    g = torch.Generator().manual_seed(rows * 131 + k)
+    x = randn_bf16(g, rows, k, outliers=True)
+    q, s = ops.quant_rows(x.cuda(), bits)
+    rq, rs = oracle.quant_rows(bits_of(x), bits)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy().view(np.uint8), rq.view(np.uint8))
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("kind", ["tanh", "none", "silu"])
+@pytest.mark.parametrize("gated", [False, True])
+def test_quant_rows_lut_modes_bitwise(bits, kind, gated):
+    g = torch.Generator().manual_seed(7)
+    x = randn_bf16(g, 17, 258)
+    up = randn_bf16(g, 17, 258)
+    lut = device_lut(kind)
+    q, s = ops.quant_rows(x.cuda(), bits, lut=lut, up=up.cuda() if gated else None)
+    rq, rs = oracle.quant_rows(bits_of(x), bits, lut_bits=bits_of(lut), up_bits=bits_of(up) if gated else None)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy().view(np.uint8), rq.view(np.uint8))
+
+
+def test_quant_rows_strided_rows_and_zero_rows():
+    g = torch.Generator().manual_seed(3)
+    base = randn_bf16(g, 6, 4096)
+    base[2] = 0
+    view = base.cuda()[:, 1024:3072]          # row stride 4096, 16-byte aligned
+    q, s = ops.quant_rows(view, 8)
+    rq, rs = oracle.quant_rows(bits_of(base[:, 1024:3072]), 8)
+    assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+    assert s[2].item() == 1.0
+    odd = base.cuda()[:, 3:1003]              # misaligned start: scalar path
+    q, s = ops.quant_rows(odd, 4)
+    rq, rs = oracle.quant_rows(bits_of(base[:, 3:1003]), 4)
+    assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+
+
+def test_quant_rows_smoothing_bitwise():
+    g = torch.Generator().manual_seed(11)
+    x = randn_bf16(g, 9, 2048, outliers=True)
+    smooth = (torch.rand(2048, generator=g) * 4 + 0.25).float()
+    q, s = ops.quant_rows(x.cuda(), 8, smooth=smooth.cuda())
+    rq, rs = oracle.quant_rows(bits_of(x), 8, smooth=smooth.numpy())
+    assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+
+
+GEMM_SHAPES = [
+    (1, 2048, 4096),
+    (16, 2048, 2048),
+    (17, 130, 64),
+    (33, 1536, 1536),
+    (64, 6144, 2048),
+    (256, 2048, 4096),
+    (300, 1024, 520),
+    (544, 2048, 4096),
+    (1024, 2048, 2048),
+    (1088, 1536, 6144),
+]
+
+
+def quantized_problem(g, m, k, n, bits, bias=True):
+    x = randn_bf16(g, m, k, outliers=True)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16) if bias else None
+    qa, sa = oracle.quant_rows(bits_of(x), bits)
+    qw, sw = oracle.quantize_weight(oracle.bf16_bits_to_f32(bits_of(w)), bits)
+    return x, w, b, qa, sa, qw, sw
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
+def test_gemm_bitwise(bits, m, k, n):
+    g = torch.Generator().manual_seed(m * 7 + k + n)
+    x, w, b, qa, sa, qw, sw = quantized_problem(g, m, k, n, bits)
+    npad = qw.shape[0]
+    bias_full = np.zeros(npad, dtype=np.uint16)
+    bias_full[:n] = bits_of(b)
+    out = ops.gemm(
+        torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(qw).cuda(),
+        torch.from_numpy(sw).cuda(), to_dev(bias_full), bits, n_store=n,
+    )
+    ua = oracle.unpack_int4(qa) if bits == 4 else qa
+    uw = oracle.unpack_int4(qw) if bits == 4 else qw
+    ref = oracle.gemm_epilogue(oracle.int_matmul(ua, uw), sa, sw, bias_full, 2)[:, :n]
+    got = bits_of(out)
+    assert got.shape == ref.shape
+    mismatch = np.argwhere(got != ref)
+    assert mismatch.size == 0, f"{len(mismatch)} mismatches, first at {mismatch[:4].tolist()}"
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("bias_mode", [_lib.BIAS_NONE, _lib.BIAS_ZERO])
+def test_gemm_bias_modes_and_negative_zero(bias_mode):
+    g = torch.Generator().manual_seed(5)
+    m, k, n = 20, 256, 64
+    _, _, _, qa, sa, qw, sw = quantized_problem(g, m, k, n, 8, bias=False)
+    qa[3] = 0                                  # exact zero row -> -0 * s stays +-0
+    sa_neg = sa.copy()
+    sa_neg[4] = -sa_neg[4]                     # negative scale produces -0 for acc == 0
+    qa[4, :] = 0
+    out = ops.gemm(
+        torch.from_numpy(qa).cuda(), torch.from_numpy(sa_neg).cuda(), torch.from_numpy(qw).cuda(),
+        torch.from_numpy(sw).cuda(), None, 8, bias_mode=bias_mode,
+    )
+    ref = oracle.gemm_epilogue(oracle.int_matmul(qa, qw), sa_neg, sw, None, bias_mode)
+    assert np.array_equal(bits_of(out), ref)
+    row4 = bits_of(out)[4]
+    assert np.all(row4 == (0x8000 if bias_mode == _lib.BIAS_NONE else 0))
+
+
+def test_gemm_output_lut_epilogue():
+    g = torch.Generator().manual_seed(9)
+    m, k, n = 17, 1536, 6144
+    _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, n, 8)
+    lut = device_lut("tanh")
+    out = ops.gemm(
+        torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(qw).cuda(),
+        torch.from_numpy(sw).cuda(), b.cuda(), 8, out_lut=lut,
+    )
+    ref = oracle.gemm_epilogue(oracle.int_matmul(qa, qw), sa, sw, bits_of(b), 2, bits_of(lut))
+    assert np.array_equal(bits_of(out), ref)
+
+
+def codes(q, bits):
+    q = q.cpu().numpy() if isinstance(q, torch.Tensor) else q
+    return oracle.unpack_int4(q).astype(np.int32) if bits == 4 else q.astype(np.int32)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_rmsnorm_producer_within_one_code(bits):
+    g = torch.Generator().manual_seed(21)
+    x = randn_bf16(g, 544, 2048, outliers=True)
+    gamma = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    q, s, _ = ops.norm_quant_rows(x.cuda(), bits, norm=_lib.NORM_RMS, eps=1e-6, gamma=gamma.cuda())
+    rq, rs = oracle.rms_norm_pack(bits_of(x), bits_of(gamma), 1e-6, bits)
+    assert np.allclose(s.cpu().numpy(), rs, rtol=2 ** -7, atol=0)
+    assert np.abs(codes(q, bits) - codes(rq, bits)).max() <= 1
+    # Most codes are identical: the difference is only reduction order.
+    assert np.mean(codes(q, bits) == codes(rq, bits)) > 0.99
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("kind", ["mod", "norm", "res"])
+def test_adaln_producers(bits, kind):
+    g = torch.Generator().manual_seed(33)
+    bsz, tokens, k = 4, 17, 1536
+    x = randn_bf16(g, bsz * tokens, k)
+    scale = (0.5 * torch.randn(bsz, k, generator=g)).to(torch.bfloat16)
+    shift = (0.5 * torch.randn(bsz, k, generator=g)).to(torch.bfloat16)
+    y = randn_bf16(g, bsz * tokens, k)
+    gate = randn_bf16(g, bsz, k)
+    kwargs = dict(scale=scale.cuda(), shift=shift.cuda(), tokens=tokens)
+    if kind == "mod":
+        q, s, _ = ops.norm_quant_rows(x.cuda(), bits, **kwargs)
+        rq, rs = oracle.modulation_pack(bits_of(x), bits_of(scale), bits_of(shift), tokens, bits)
+        assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+        return
+    if kind == "norm":
+        q, s, _ = ops.norm_quant_rows(x.cuda(), bits, norm=_lib.NORM_LN, eps=1e-6, **kwargs)
+        rq, rs = oracle.modulation_pack(bits_of(x), bits_of(scale), bits_of(shift), tokens, bits, eps=1e-6)
+    else:
+        q, s, r = ops.norm_quant_rows(
+            x.cuda(), bits, norm=_lib.NORM_LN, eps=1e-6, y=y.cuda(), gate=gate.cuda(), **kwargs
+        )
+        rq, rs, rr = oracle.residual_norm_modulation_pack(
+            bits_of(x), bits_of(y), bits_of(gate), bits_of(scale), bits_of(shift), tokens, bits, 1e-6
+        )
+        assert np.array_equal(bits_of(r), rr)
+    assert np.allclose(s.cpu().numpy(), rs, rtol=2 ** -7, atol=0)
+    assert np.abs(codes(q, bits) - codes(rq, bits)).max() <= 1
+
+
+@pytest.mark.parametrize("rows,k", [(1, 2048), (17, 1536), (300, 6144)])
+def test_nvfp4_pack_bitwise(rows, k):
+    g = torch.Generator().manual_seed(rows + k)
+    x = randn_bf16(g, rows, k, outliers=True)
+    x[0, :16] = 0
+    packed, sf = ops.pack_nvfp4(x.cuda())
+    rp, rsf = oracle.pack_nvfp4(oracle.bf16_bits_to_f32(bits_of(x)))
+    assert np.array_equal(packed.cpu().numpy(), rp)
+    sfg = sf.cpu().numpy()
+    blocks_k = (k // 16 + 3) // 4
+    rr, jj = np.meshgrid(np.arange(rows), np.arange(k // 16), indexing="ij")
+    off = oracle.nvfp4_sf_offset(rr, jj, blocks_k)
+    assert np.array_equal(sfg.reshape(-1)[off], rsf.reshape(-1)[off])
