@@ -1,0 +1,504 @@
+"""Benchmark: GR00T control-step latency (VLM prefill + 4-step DiT) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--precision w8a8|w4a4] [--batch B]
+
+One step = one GR00T-shaped control step per robot: Qwen3-shaped 16-layer VLM
+prefill over 544 tokens, then 4 Euler steps of the 16-block DiT, every
+Linear layer on the W8A8 (or W4A4) tcgen05 kernels, the whole step replayed
+from one CUDA graph.  Synthetic seeded inputs and random-init weights (no
+checkpoints or datasets exist here).  With N GPUs each rank runs its own
+robot(s) (independent instances, no collective: weak scaling); timing is
+CUDA events on the step's stream, max over ranks.  Each step streams about
+1.4 GB of packed weights, far larger than the 126 MB L2, so no L2 flush is
+needed between steps.
+
+`--impl reference` times the reference's quantized-Linear arithmetic on the
+host cores instead: piR2 has no CPU implementation of this path (its kernels
+reject CPU tensors), so this is the CPU restatement in oracle/ (numpy
+quantize + exact int GEMM + dequant epilogue, torch CPU for norms and
+attention), run on a bounded sample (one VLM layer and a two-block DiT over
+the 4 Euler steps) and scaled to the full step by layer counts.
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from types import SimpleNamespace
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "GR00T step latency ms (VLM+4-step DiT) B=1"
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+# int8 dense tensor peak measured on this pool's B200 by a kind::i8 issue-rate
+# probe (8188 MAC/clk/SM x 148 SMs at the sampled clock): 4.5 POPS.
+INT8_PEAK_TOPS = 4520.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--precision", choices=["w8a8", "w4a4"], default="w8a8")
+    p.add_argument("--batch", type=int, default=1, help="robots per GPU")
+    p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--cpu-sample-seconds", type=float, default=20.0)
+    return p.parse_args()
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            data = json.load(f)
+        return data["hbm_gbs"], "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, index):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file,
+                stderr=subprocess.DEVNULL,
+            )
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        self.file.flush()
+        self.file.seek(0)
+        mhz, max_mhz, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max_mhz, "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+class GemmTimer:
+    """Brackets every pir2b_gemm launch with CUDA events.  Used while
+    capturing a separate graph of the step: the events become event-record
+    nodes, so a replay times each GEMM on the device with no host gaps."""
+
+    def __init__(self):
+        self.records = []
+        self._start = None
+
+    def before(self, device):
+        self._start = torch.cuda.Event(enable_timing=True, external=True)
+        self._start.record(torch.cuda.current_stream(device))
+
+    def after(self, device, **shape):
+        end = torch.cuda.Event(enable_timing=True, external=True)
+        end.record(torch.cuda.current_stream(device))
+        self.records.append((self._start, end, shape))
+
+
+def gemm_bytes(s):
+    wb = s["npad"] * s["k"] * s["bits"] // 8
+    return wb + s["m"] * s["k"] * s["bits"] // 8 + 4 * s["m"] + 4 * s["npad"] + 2 * s["m"] * s["n"]
+
+
+def roofline(engine, hbm_peak, peak_kind):
+    """Times each GEMM launch of one step (a graph captured with event nodes
+    around every GEMM, replayed once warm); reports the small-M GEMMs (the
+    weight-streaming launches that dominate a B=1 step) against HBM and the
+    large-M ones against the int8 tensor peak."""
+    from pir2_b200 import ops
+
+    timer = GemmTimer()
+    graph = torch.cuda.CUDAGraph()
+    ops.launch_recorder = timer
+    try:
+        with torch.inference_mode():
+            with torch.cuda.graph(graph, stream=engine.stream):
+                engine.policy(*engine.static)
+    finally:
+        ops.launch_recorder = None
+    timer_records = list(timer.records)
+    with torch.cuda.stream(engine.stream):
+        graph.replay()
+        graph.replay()
+    engine.stream.synchronize()
+    timer.records = timer_records
+    small = {"t": 0.0, "bytes": 0.0, "n": 0}
+    large = {"t": 0.0, "ops": 0.0, "n": 0}
+    for start, end, s in timer.records:
+        ms = start.elapsed_time(end)
+        if s["m"] <= 64:
+            small["t"] += ms
+            small["bytes"] += gemm_bytes(s)
+            small["n"] += 1
+        else:
+            large["t"] += ms
+            large["ops"] += 2.0 * s["m"] * s["n"] * s["k"]
+            large["n"] += 1
+    total = small["t"] + large["t"]
+    achieved = small["bytes"] / (small["t"] * 1e-3) / 1e9 if small["t"] else 0.0
+    tops = large["ops"] / (large["t"] * 1e-3) / 1e12 if large["t"] else 0.0
+    return {
+        "_gemm_ms_small": small["t"],
+        "kernel": "gemm_i8_kernel<8> small-M (M<=64) launches",
+        "bound": "hbm",
+        "achieved": round(achieved, 1),
+        "peak": hbm_peak,
+        "unit": "GB/s",
+        "frac": round(achieved / hbm_peak, 4),
+        "peak_source": f"{peak_kind} hbm_gbs",
+        "traffic": None,
+        "launches": small["n"],
+        "avg_launch_us": round(small["t"] * 1e3 / max(small["n"], 1), 2),
+        "share_of_gemm_time": round(small["t"] / total, 3) if total else None,
+        "large_m": {
+            "bound": "tensor",
+            "launches": large["n"],
+            "achieved_tops": round(tops, 1),
+            "peak_tops": INT8_PEAK_TOPS,
+            "frac": round(tops / INT8_PEAK_TOPS, 4),
+            "peak_source": "measured int8 kind::i8 issue-rate probe",
+        },
+    }
+
+
+# ------------------------------------------------------------------ CPU arm
+def cpu_oracle_step(args, budget_s):
+    """The reference's quantized-Linear arithmetic on the host cores, on a
+    bounded sample: one VLM decoder layer (544 tokens) and a two-block DiT
+    (one cross-, one self-attention block) through the 4 Euler steps, scaled
+    to 16 layers / 16 blocks.  Returns (ms_per_step, cores, sample text)."""
+    import numpy as np
+
+    import oracle
+    from pir2_b200 import harness
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    bits = 8 if args.precision == "w8a8" else 4
+    vlm = harness.VLMConfig(layers=1, vocab=2048)
+    dit = harness.DiTConfig(layers=2)
+    policy = harness.build_policy("cpu", vlm=vlm, dit=dit)
+
+    def bits_of(t):
+        return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    for module in policy.modules():
+        if isinstance(module, torch.nn.Linear):
+            w = module.weight.detach().float().numpy()
+            qw, sw = oracle.quantize_weight(w, bits)
+            uw = oracle.unpack_int4(qw) if bits == 4 else qw
+            bias = None if module.bias is None else bits_of(module.bias)
+            n = w.shape[0]
+
+            def forward(x, uw=uw, sw=sw, bias=bias, n=n):
+                lead = x.shape[:-1]
+                rows = bits_of(x.reshape(-1, x.shape[-1]))
+                qa, sa = oracle.quant_rows(rows, bits)
+                ua = oracle.unpack_int4(qa) if bits == 4 else qa
+                acc = oracle.int_matmul(ua, uw)
+                full = None
+                if bias is not None:
+                    full = np.zeros(uw.shape[0], dtype=np.uint16)
+                    full[:n] = bias
+                y = oracle.gemm_epilogue(acc, sa, sw, full, 2 if bias is not None else 1)[:, :n]
+                return torch.from_numpy(np.ascontiguousarray(y).view(np.int16)).view(torch.bfloat16).reshape(*lead, n)
+
+            module.forward = forward
+    visual, ids, state, noise = harness.synthetic_inputs(args.batch, "cpu", vlm=vlm, dit=dit)
+    layer = policy.backbone.layers[0]
+    with torch.inference_mode():
+        h = torch.cat((visual, policy.backbone.embed_tokens(ids)), dim=1)
+        cos, sin = policy.backbone.rope(h.shape[1], h.device, h.dtype)
+        t_vlm, t_dit, reps = 0.0, 0.0, 0
+        start = time.perf_counter()
+        while reps == 0 or time.perf_counter() - start < budget_s:
+            t0 = time.perf_counter()
+            feat = layer(h, cos, sin)
+            t1 = time.perf_counter()
+            policy.action_head.get_action(feat, state, noise)
+            t2 = time.perf_counter()
+            t_vlm += t1 - t0
+            t_dit += t2 - t1
+            reps += 1
+    full_ms = 1e3 * (16 * t_vlm / reps + 8 * t_dit / reps)
+    sample = (
+        f"{reps} x (1 VLM layer over 544 tokens + 2-block DiT x 4 Euler steps), batch {args.batch}, "
+        "oracle W8A8 linears + torch CPU norms/attention, scaled x16 VLM layers / x8 DiT block pairs"
+    )
+    return full_ms, cores, sample
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    ms, cores, sample = cpu_oracle_step(args, budget_s=max(2.0, args.cpu_sample_seconds / max(args.steps, 1)))
+    line = {
+        "metric": METRIC,
+        "value": round(ms, 3),
+        "unit": "ms",
+        "impl": "reference",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8" if args.precision == "w8a8" else "int4",
+        "data": "synthetic",
+        "config": {
+            "workload": f"GR00T-shaped control step, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
+            "precision": args.precision,
+            "batch_per_gpu": args.batch,
+        },
+        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+def build_engine(args, local):
+    from pir2_b200 import harness
+    from pir2_b200.config import OptimizationConfig
+    from pir2_b200.engine import ControlStep
+    from pir2_b200.session import GrootOptimizations
+
+    device = torch.device("cuda", local)
+    policy = harness.build_policy(device)
+    config = OptimizationConfig(
+        precision=args.precision,
+        fusion=True,
+        scope="all",
+        group_conditioning=True,
+        norm_modulation_quant=True,
+        residual_norm_quant=True,
+    )
+    session = GrootOptimizations(SimpleNamespace(model=policy), config)
+    session.__enter__()
+    engine = ControlStep(policy, args.batch, device=device, graph=not args.no_graph)
+    inputs = harness.synthetic_inputs(args.batch, device)
+    engine.load(inputs)
+    engine.capture()
+    host_inputs = [t.cpu().pin_memory() for t in harness.synthetic_inputs(args.batch, "cpu", seed=2)]
+    return engine, session, host_inputs
+
+
+def run_ours(args, world, rank, local):
+    from pir2_b200 import _lib
+
+    engine, session, host_inputs = build_engine(args, local)
+    stream = engine.stream
+    for _ in range(args.warmup):
+        engine.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        # The NVTX range lets a profiler select exactly the timed steps.
+        torch.cuda.nvtx.range_push("pir2b_timed")
+        e0.record(stream)
+        for _ in range(args.steps):
+            engine.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    barrier(world)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms, world)
+    clock_summary = clocks.summary()
+
+    # End to end through the public step call: pinned host inputs -> H2D ->
+    # graph -> D2H of the actions, every step.
+    for _ in range(2):
+        engine.step(host_inputs)
+    barrier(world)
+    torch.cuda.synchronize()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        engine.step(host_inputs)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+
+    hbm, kind = peaks()
+    roof = roofline(engine, hbm, kind)
+    status = _lib.device_status()
+    roof["share_of_step"] = round(roof.pop("_gemm_ms_small", 0.0) / ms, 3) if ms else None
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu_ms, cores, sample = cpu_oracle_step(args, budget_s=args.cpu_sample_seconds)
+        cpu = {"value": round(cpu_ms, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample}
+    # Kernel launches inside one timed step (graph nodes of this library).
+    launches = count_launches(engine)
+    engine.release()
+    session.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(ms, 4),
+            "unit": "ms",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": False,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int8" if args.precision == "w8a8" else "int4",
+            "data": "synthetic",
+            "config": {
+                "workload": f"GR00T-shaped control step per GPU, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
+                "precision": args.precision,
+                "batch_per_gpu": args.batch,
+                "parallelism": f"independent robots, dp{world}, no collective",
+                "graph": not args.no_graph,
+                "l2": "each step streams ~1.4 GB of packed weights (> 126 MB L2); no flush",
+            },
+            "e2e": {
+                "value": round(e2e_ms, 4),
+                "unit": "ms",
+                "h2d_bytes_per_step": engine.h2d_bytes(),
+                "d2h_bytes_per_step": engine.d2h_bytes(),
+            },
+            "gpu_launches": launches,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clock_summary,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def count_launches(engine):
+    """Counts this library's kernel launches in one step (quant/pack, norm
+    producers and GEMMs), by wrapping the C-ABI entry points for one eager
+    step."""
+    from pir2_b200 import _lib
+
+    lib = _lib.lib()
+    names = ["pir2b_quant_rows", "pir2b_norm_quant_rows", "pir2b_gemm"]
+    counts = {n: 0 for n in names}
+    originals = {n: getattr(lib, n) for n in names}
+
+    class Counting:
+        def __init__(self, name, fn):
+            self.name, self.fn = name, fn
+
+        def __call__(self, *a):
+            counts[self.name] += 1
+            return self.fn(*a)
+
+    try:
+        for n in names:
+            setattr(lib, n, Counting(n, originals[n]))
+        with torch.inference_mode(), torch.cuda.stream(engine.stream):
+            engine.policy(*engine.static)
+        engine.stream.synchronize()
+    finally:
+        for n in names:
+            setattr(lib, n, originals[n])
+    return sum(counts.values())
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

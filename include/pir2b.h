@@ -118,15 +118,18 @@ int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
  * qw: weights int8 [npad, Kpad] / uint8 [npad, Kpad/2]; sw fp32 [npad];
  * bias: bf16 [npad] (bias_mode ADD) or NULL; out_lut: optional bf16[65536]
  * table applied to the bf16 result (fuses GELU/SiLU producers);
+ * residual: optional bf16 [m, ldr]; when given, out = bf16(f32(result) +
+ * f32(residual)) -- the residual epilogue of integer_epilogue.cu:156-327
+ * (pir2_integer_epilogue::gemm with a residual, epilogue.py:360-398);
  * out: bf16, row stride ldo, columns [0, n_store) written.
  * kpad % 128 == 0, npad % 8 == 0, n_store <= npad, m >= 1.
  * tactic: -1 selects the tile shape by heuristic; piR2's Ada tactic ids
  * 0..7 are accepted and ignored (tiles are chosen for B200). */
 int pir2b_gemm(const void *qa, const float *sa, const void *qw,
                const float *sw, const void *bias, int bias_mode,
-               const void *out_lut, int bits, int64_t m, int64_t npad,
-               int64_t kpad, void *out, int64_t ldo, int64_t n_store,
-               int tactic, void *stream);
+               const void *out_lut, const void *residual, int64_t ldr,
+               int bits, int64_t m, int64_t npad, int64_t kpad, void *out,
+               int64_t ldo, int64_t n_store, int tactic, void *stream);
 
 /* NVFP4 (E2M1 values, UE4M3 scale per 16 elements) packing of bf16 rows.
  * Replaces pack_matrix_fp4_ue_rowmajor_kernel / pack_activation_gemm_bf16 /
@@ -150,6 +153,19 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
                      const void *sfw, const void *bias, float alpha,
                      int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,
                      void *stream);
+
+/* Fused per-head RMSNorm (Qwen3 q_norm / k_norm) + rotary embedding of the
+ * q and k heads of a grouped q|k|v projection output, and the [B, H, T, D]
+ * relayout of q, k and v for attention.  BF16 pointwise fusion next to the
+ * quantized path; replaces the RoPE and RMSNorm kernels of
+ *   coexecution/fused_ops.py:34-147 (rope), :150-232 (rmsnorm).
+ * qkv: bf16 [rows = B*T, ld], q heads then k heads then v heads (head_dim
+ * 128); cos/sin: bf16 [T, 128]; outputs bf16 [B, hq|hk, T, 128]. */
+int pir2b_qk_norm_rope(const void *qkv, int64_t ld, const void *q_weight,
+                       const void *k_weight, const void *cos, const void *sin,
+                       int64_t rows, int64_t tokens, int hq, int hk,
+                       int head_dim, float eps, void *q_out, void *k_out,
+                       void *v_out, void *stream);
 
 #ifdef __cplusplus
 }

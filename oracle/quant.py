@@ -145,20 +145,31 @@ def quant_rows(x_bits, bits, *, lut_bits=None, up_bits=None, smooth=None):
     return (q if bits == 8 else pack_int4(q)), s
 
 
-def quantize_weight(w, bits):
+def quantize_weight(w, bits, *, scale_rule="cuda"):
     """Per-output-channel weight quantization and padding.
 
     Restates `IntegerLinear.from_linear` (integer.py:211-256):
-    s_n = max_k |f32(w)| / L (IEEE division; 1.0 for an all-zero row),
+    s_n = max_k |f32(w)| / L (1.0 for an all-zero row),
     q = clamp(round_half_even(w / s_n), -L, L), K zero-padded to Kpad and N to
     Npad (scales padded with 1.0), int4 nibble-packed low-first.
-    Returns (codes, scales[Npad]).
+
+    `maximum / limit` divides a CUDA tensor by a Python scalar, which PyTorch
+    evaluates on the GPU as a multiply by the fp32 reciprocal; that is the
+    reference's effective arithmetic (scale_rule "cuda", the default).  CPU
+    torch divides (scale_rule "divide").  `w / s` is a tensor-by-tensor IEEE
+    division in both.  Returns (codes, scales[Npad]).
     """
     w = np.asarray(w, dtype=F32)
     n, k = w.shape
     lim = _limit(bits)
     m = np.abs(w).max(axis=1).astype(F32)
-    s = np.where(m > 0, (m / F32(lim)).astype(F32), F32(1.0)).astype(F32)
+    if scale_rule == "cuda":
+        raw = (m * (F32(1.0) / F32(lim))).astype(F32)
+    elif scale_rule == "divide":
+        raw = (m / F32(lim)).astype(F32)
+    else:
+        raise ValueError("scale_rule must be 'cuda' or 'divide'")
+    s = np.where(m > 0, raw, F32(1.0)).astype(F32)
     q = np.clip(np.rint((w / s[:, None]).astype(F32)), -lim, lim).astype(np.int8)
     qp = np.zeros((npad_of(n), kpad_of(k)), dtype=np.int8)
     qp[:n, :k] = q
@@ -196,12 +207,12 @@ def gemm_epilogue(acc, sa, sw, bias_bits=None, bias_mode=1, out_lut_bits=None):
     return out
 
 
-def linear_w8a8(x_bits, w_f32, bias_bits, bits, *, bias_mode=None, smooth=None):
+def linear_w8a8(x_bits, w_f32, bias_bits, bits, *, bias_mode=None, smooth=None, scale_rule="cuda"):
     """Whole quantized Linear: quantize rows, quantize weights, int GEMM,
     dequant epilogue.  Returns bf16 bits [rows, n]."""
     n = np.asarray(w_f32).shape[0]
     qa, sa = quant_rows(x_bits, bits, smooth=smooth)
-    qw, sw = quantize_weight(w_f32, bits)
+    qw, sw = quantize_weight(w_f32, bits, scale_rule=scale_rule)
     if bits == 4:
         qa, qw = unpack_int4(qa), unpack_int4(qw)
     acc = int_matmul(qa, qw)

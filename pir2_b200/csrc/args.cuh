@@ -44,6 +44,8 @@ struct GemmArgs {
   const float *sw;                  // [Npad] weight channel scales
   const __nv_bfloat16 *bias;        // [Npad] or null
   const __nv_bfloat16 *out_lut;     // [65536] activation table or null
+  const __nv_bfloat16 *residual;    // [M, ldr] added after rounding, or null
+  int64_t ldr;                      // residual row stride (elements)
   __nv_bfloat16 *out;               // [M, ldo]
   int64_t ldo;                      // output row stride (elements)
   int m;                            // token rows
@@ -53,6 +55,7 @@ struct GemmArgs {
   int bn;                           // token tile (multiple of 16, <= 256)
   int stages;                       // pipeline depth
   int splits;                       // cluster size along z (1,2,4,8)
+  int tma_store;                    // 1: output tile leaves through TMA
 };
 
 cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
@@ -63,6 +66,7 @@ cudaError_t run_norm_quant(const NormArgs &a, int out_format, int64_t rows,
 template <int kBits>
 __global__ void gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w,
                                const __grid_constant__ CUtensorMap tm_a,
+                               const __grid_constant__ CUtensorMap tm_out,
                                const GemmArgs args);
 
 } // namespace pir2b

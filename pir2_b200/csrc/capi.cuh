@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/pir2b.h"
@@ -138,6 +139,27 @@ static int make_map(CUtensorMap *map, const void *base, uint64_t cols,
   return PIR2B_OK;
 }
 
+// 2-D bf16 map over the [rows, cols] output (row stride ld elements), box
+// [box_rows, 128 columns], used by the epilogue's TMA store.
+static int make_out_map(CUtensorMap *map, const void *base, uint64_t cols,
+                        uint64_t rows, uint64_t ld, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr)
+    return fail(PIR2B_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {128u, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PIR2B_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", int(r));
+  return PIR2B_OK;
+}
+
 // ------------------------------------------------------------------ GEMM plan
 struct GemmPlan {
   int bn, mtiles, splits, stages;
@@ -147,8 +169,14 @@ struct GemmPlan {
 static size_t gemm_smem(int bits, int bn, int stages) {
   const size_t stage = 16384 + size_t(bn) * 128;
   const size_t packed = bits == 4 ? ((size_t(128 + bn) * 64 + 1023) & ~size_t(1023)) : 0;
-  return 1024 + stages * (stage + packed) + (4 * stages + 1) * 8 + 16;
+  // + 1 KB of staged token scales, + barriers and the TMEM address slot.
+  return 1024 + stages * (stage + packed) + 1024 + (4 * stages + 1) * 8 + 16;
 }
+
+// Single-token-tile (small-M) GEMMs stay under ~110 KB of shared memory so
+// two CTAs fit on an SM: with programmatic dependent launch the next GEMM's
+// prologue and weight prefetch then run while this one finishes.
+constexpr int kCoResidentSmem = 110 * 1024;
 
 static int stages_for(int bits, int bn, int max_smem) {
   int s = 8;
@@ -174,7 +202,8 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
       continue;
     if (int64_t(mt - 1) * bn >= m)
       continue;  // an empty token tile
-    const int stages = stages_for(bits, bn, max_smem);
+    const int budget = (mt == 1 && bn <= 64) ? std::min(max_smem, kCoResidentSmem) : max_smem;
+    const int stages = stages_for(bits, bn, budget);
     if (size_t(stages) * (16384 + size_t(bn) * 128) < size_t(bn) * 512)
       continue;  // split-K partials must fit in the stage buffers
     for (int s = 1; s <= 8; s *= 2) {
@@ -361,9 +390,9 @@ int pir2b_pack_nvfp4(const void *x, int64_t rows, int64_t k, void *packed,
 
 int pir2b_gemm(const void *qa, const float *sa, const void *qw,
                const float *sw, const void *bias, int bias_mode,
-               const void *out_lut, int bits, int64_t m, int64_t npad,
-               int64_t kpad, void *out, int64_t ldo, int64_t n_store,
-               int tactic, void *stream) {
+               const void *out_lut, const void *residual, int64_t ldr,
+               int bits, int64_t m, int64_t npad, int64_t kpad, void *out,
+               int64_t ldo, int64_t n_store, int tactic, void *stream) {
   (void)tactic;
   if (bits != 4 && bits != 8)
     return fail(PIR2B_EINVAL, "bits must be 4 or 8, got %d", bits);
@@ -385,8 +414,11 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
   if (!aligned(qa, 16) || !aligned(qw, 16))
     return fail(PIR2B_EALIGN, "packed operands must be 16-byte aligned");
   if (!aligned(out, 2) || !aligned(sa, 4) || !aligned(sw, 4) ||
-      (bias && !aligned(bias, 2)) || (out_lut && !aligned(out_lut, 2)))
+      (bias && !aligned(bias, 2)) || (out_lut && !aligned(out_lut, 2)) ||
+      (residual && !aligned(residual, 2)))
     return fail(PIR2B_EALIGN, "scale/bias/output alignment not met");
+  if (residual != nullptr && ldr < n_store)
+    return fail(PIR2B_EINVAL, "residual row stride ldr must be >= n_store");
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
@@ -407,6 +439,8 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
                   ? static_cast<const __nv_bfloat16 *>(bias)
                   : nullptr;
   args.out_lut = static_cast<const __nv_bfloat16 *>(out_lut);
+  args.residual = static_cast<const __nv_bfloat16 *>(residual);
+  args.ldr = ldr;
   args.out = static_cast<__nv_bfloat16 *>(out);
   args.ldo = ldo;
   args.m = int(m);
@@ -416,6 +450,18 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
   args.bn = plan.bn;
   args.stages = plan.stages;
   args.splits = plan.splits;
+  // The epilogue stages the tile in shared memory and writes it with one TMA
+  // store when the output rows are 16-byte aligned; otherwise it stores
+  // directly.  Split-K tiles are reduced through cluster shared memory and
+  // stored directly.
+  args.tma_store = (plan.splits == 1 && ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  CUtensorMap tm_out;
+  memset(&tm_out, 0, sizeof(tm_out));
+  if (args.tma_store) {
+    if (int r = make_out_map(&tm_out, out, uint64_t(n_store), uint64_t(m),
+                             uint64_t(ldo), uint32_t(plan.bn)))
+      return r;
+  }
 
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
@@ -424,17 +470,61 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = unsigned(plan.splits);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = bits == 8
-                      ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, args)
-                      : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, args);
+  cfg.numAttrs = 2;
+  cudaError_t e =
+      bits == 8 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, tm_out, args)
+                : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, tm_out, args);
   return cuda_status(e, "gemm launch");
+}
+
+int pir2b_qk_norm_rope(const void *qkv, int64_t ld, const void *q_weight,
+                       const void *k_weight, const void *cos, const void *sin,
+                       int64_t rows, int64_t tokens, int hq, int hk,
+                       int head_dim, float eps, void *q_out, void *k_out,
+                       void *v_out, void *stream) {
+  if (head_dim != 128)
+    return fail(PIR2B_EINVAL, "qk_norm_rope supports head_dim 128 (got %d)", head_dim);
+  if (rows < 0 || tokens < 1 || rows % tokens != 0 || hq < 1 || hk < 1 ||
+      rows > 0x7fffffffLL / (hq + 2 * hk))
+    return fail(PIR2B_EINVAL, "qk_norm_rope: bad rows/tokens/heads");
+  if (ld < int64_t(hq + 2 * hk) * head_dim || ld % 4 != 0)
+    return fail(PIR2B_EINVAL, "qk_norm_rope: row stride too small or not a multiple of 4");
+  if (!(eps > 0.f))
+    return fail(PIR2B_EINVAL, "qk_norm_rope: epsilon must be positive");
+  const void *ptrs[] = {qkv, q_weight, k_weight, cos, sin, q_out, k_out, v_out};
+  for (const void *p : ptrs)
+    if (p == nullptr || !aligned(p, 8))
+      return fail(PIR2B_EALIGN, "qk_norm_rope operands must be non-null and 8-byte aligned");
+  if (rows == 0)
+    return PIR2B_OK;
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  QkRopeArgs a;
+  a.qkv = static_cast<const __nv_bfloat16 *>(qkv);
+  a.ld = ld;
+  a.q_w = static_cast<const __nv_bfloat16 *>(q_weight);
+  a.k_w = static_cast<const __nv_bfloat16 *>(k_weight);
+  a.cos = static_cast<const __nv_bfloat16 *>(cos);
+  a.sin = static_cast<const __nv_bfloat16 *>(sin);
+  a.q_out = static_cast<__nv_bfloat16 *>(q_out);
+  a.k_out = static_cast<__nv_bfloat16 *>(k_out);
+  a.v_out = static_cast<__nv_bfloat16 *>(v_out);
+  a.rows = int(rows);
+  a.tokens = int(tokens);
+  a.hq = hq;
+  a.hk = hk;
+  a.eps = eps;
+  return cuda_status(run_qk_norm_rope(a, rows, static_cast<cudaStream_t>(stream)),
+                     "qk_norm_rope launch");
 }
 
 int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,

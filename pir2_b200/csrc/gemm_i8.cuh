@@ -55,6 +55,18 @@ __device__ __forceinline__ __nv_bfloat16 epilogue_value(int acc, float sa,
   return o;
 }
 
+// Residual variant (coexecution/kernels/ampere_ada/epilogue.py, module
+// docstring): the bf16 GEMM result plus the bf16 residual, added in fp32 and
+// rounded to bf16 again.
+__device__ __forceinline__ __nv_bfloat16 add_residual(__nv_bfloat16 o,
+                                                      const GemmArgs &args,
+                                                      int64_t m, int c) {
+  if (args.residual == nullptr)
+    return o;
+  const float r = __bfloat162float(args.residual[m * args.ldr + c]);
+  return __float2bfloat16_rn(__fadd_rn(__bfloat162float(o), r));
+}
+
 // Unpacks a stage of low-nibble-first int4 bytes into sign-extended int8,
 // written in the 128-byte-swizzled K-major layout UMMA reads.  `src` holds
 // `rows` rows of 64 packed bytes (128 int4 values); `dst` holds `rows` rows
@@ -97,10 +109,16 @@ __device__ __forceinline__ void unpack_int4_stage(const uint8_t *src,
 // kBits == 8: operands arrive as int8 through TMA in the swizzled layout.
 // kBits == 4: operands arrive as packed int4 (64 bytes per row and K block,
 // no swizzle) and the four epilogue warps unpack them per stage.
+//
+// Launch with programmatic dependent launch: the prologue (barriers, TMEM,
+// descriptor prefetch) and the first weight tiles, which do not depend on
+// the previous kernel, overlap its tail; activation tiles and scales are
+// read only after griddepcontrol.wait.
 template <int kBits>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_a,
+                   const __grid_constant__ CUtensorMap tm_out,
                    const GemmArgs args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
@@ -116,8 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int packed_bytes = (kBits == 4) ? (kTileN + bn) * 64 : 0;
   const int packed_stride = (packed_bytes + 1023) & ~1023;
   uint8_t *packed_base = smem + stages * stage_bytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(packed_base +
-                                                stages * packed_stride);
+  float *s_sa = reinterpret_cast<float *>(packed_base + stages * packed_stride);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(s_sa + 256);
   uint64_t *full = bars;                  // TMA -> consumer
   uint64_t *empty = bars + stages;        // MMA done -> producer
   uint64_t *ready = bars + 2 * stages;    // (W4A4) unpacked -> MMA
@@ -144,6 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_a);
+    if (args.tma_store)
+      tma_prefetch_desc(&tm_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, tmem_cols);
@@ -153,20 +173,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Let the next kernel of the stream launch now: its prologue and weight
+  // prefetch overlap this kernel; it reads our output only after its own
+  // griddepcontrol.wait, which waits for this grid to complete.
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
-      const uint64_t wpolicy = policy_evict_first();
+      // Weights are streamed once when a single token tile covers M; with
+      // several token tiles other CTAs re-read them from L2.
+      const uint64_t wpolicy =
+          gridDim.y == 1 ? policy_evict_first() : policy_evict_last();
       const uint32_t tx = (kBits == 8) ? uint32_t(stage_bytes)
                                        : uint32_t((kTileN + bn) * 64);
-      for (int i = 0; i < nkb; ++i) {
+      const int kstep = kBits == 8 ? kBlockK : 64;
+      // Weight tiles of the first ring pass do not depend on the previous
+      // kernel: issue them before waiting on it.
+      const int pre = min(nkb, stages);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], tx);
+        uint8_t *dst = kBits == 8 ? smem + i * stage_bytes
+                                  : packed_base + i * packed_stride;
+        tma_load_2d_hint(dst, &tm_w, &full[i], (kb_begin + i) * kstep, n0,
+                         wpolicy);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        uint8_t *dst = kBits == 8 ? smem + i * stage_bytes + op_a_bytes
+                                  : packed_base + i * packed_stride + kTileN * 64;
+        tma_load_2d(dst, &tm_a, &full[i], (kb_begin + i) * kstep, m0);
+      }
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % stages;
         const uint32_t phase = (i / stages) & 1;
         if (!mbar_wait(&empty[s], phase ^ 1, kStatusTimeoutProducer))
           break;
         mbar_arrive_expect_tx(&full[s], tx);
-        const int kx = (kb_begin + i) * (kBits == 8 ? kBlockK : 64);
+        const int kx = (kb_begin + i) * kstep;
         if (kBits == 8) {
           uint8_t *a = smem + s * stage_bytes;
           tma_load_2d_hint(a, &tm_w, &full[s], kx, n0, wpolicy);
@@ -208,6 +252,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int et = threadIdx.x - 64;   // 0..127
+    pdl_wait();
+    // Token scales of this tile, once, while the main loop runs.
+    for (int j = et; j < bn; j += 128)
+      s_sa[j] = (m0 + j < args.m) ? __ldg(args.sa + m0 + j) : 0.f;
+    named_barrier(1, 128);
     if (kBits == 4) {
       for (int i = 0; i < nkb; ++i) {
         const int s = i % stages;
@@ -228,27 +277,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ch = quarter * 32 + lane;       // channel within the tile
     const int c = n0 + ch;
     const int valid_m = min(bn, args.m - m0);
+    const uint32_t lane_addr = tmem_base + (uint32_t(quarter * 32) << 16);
     if (have_acc) {
       if (args.splits == 1) {
-        const float sw = (c < args.n_store) ? __ldg(args.sw + c) : 0.f;
-        const float b = (args.bias_mode == 2 && c < args.n_store)
+        const bool in_range = c < args.n_store;
+        const float sw = in_range ? __ldg(args.sw + c) : 0.f;
+        const float b = (args.bias_mode == 2 && in_range)
                             ? __bfloat162float(args.bias[c])
                             : 0.f;
         const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
-        for (int j0 = 0; j0 < bn; j0 += 16) {
-          uint32_t r[16];
-          tmem_ld_16(tmem_base + (uint32_t(quarter * 32) << 16) + j0, r);
-          tmem_ld_wait();
-          if (j0 < valid_m && c < args.n_store) {
+        // Staging tile [bn tokens][128 channels] bf16 in the idle stage
+        // buffers, written out by one TMA store.
+        __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem);
+        for (int j0 = 0; j0 < bn; j0 += 32) {
+          uint32_t r[32];
+          if (j0 + 32 <= bn) {
+            tmem_ld_32(lane_addr + j0, r);
+          } else {
+            uint32_t h[16];
+            tmem_ld_16(lane_addr + j0, h);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int j = j0 + i;
-              if (j < valid_m) {
-                const float sa = __ldg(args.sa + m0 + j);
-                args.out[int64_t(m0 + j) * args.ldo + c] = epilogue_value(
-                    int(r[i]), sa, sw, b, args.bias_mode, lut);
-              }
-            }
+            for (int i = 0; i < 16; ++i)
+              r[i] = h[i];
+          }
+          const int cnt = min(32, bn - j0);
+          // Residual values of this chunk, all loads in flight together.
+          float res[32];
+          const bool with_res = args.residual != nullptr && in_range;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            res[i] = (with_res && j0 + i < valid_m)
+                         ? __bfloat162float(args.residual[int64_t(m0 + j0 + i) * args.ldr + c])
+                         : 0.f;
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i >= cnt)
+              break;
+            __nv_bfloat16 o = epilogue_value(int(r[i]), s_sa[j0 + i], sw, b,
+                                             args.bias_mode, lut);
+            if (with_res && j0 + i < valid_m)
+              o = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o), res[i]));
+            if (args.tma_store)
+              stage[(j0 + i) * kTileN + ch] = o;
+            else if (in_range && j0 + i < valid_m)
+              args.out[int64_t(m0 + j0 + i) * args.ldo + c] = o;
+          }
+        }
+        if (args.tma_store) {
+          fence_proxy_async_smem();
+          named_barrier(1, 128);
+          if (et == 0) {
+            tma_store_2d(&tm_out, stage, n0, m0);
+            tma_store_commit_and_wait();
           }
         }
       } else {
@@ -257,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int *part = reinterpret_cast<int *>(smem);
         for (int j0 = 0; j0 < bn; j0 += 16) {
           uint32_t r[16];
-          tmem_ld_16(tmem_base + (uint32_t(quarter * 32) << 16) + j0, r);
+          tmem_ld_16(lane_addr + j0, r);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -290,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc.z += v.z;
           acc.w += v.w;
         }
-        const float sa = __ldg(args.sa + m0 + j);
+        const float sa = s_sa[j];
         const int accs[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -299,8 +380,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float b = args.bias_mode == 2
                                 ? __bfloat162float(args.bias[cc])
                                 : 0.f;
-            args.out[int64_t(m0 + j) * args.ldo + cc] = epilogue_value(
-                accs[e], sa, __ldg(args.sw + cc), b, args.bias_mode, lut);
+            args.out[int64_t(m0 + j) * args.ldo + cc] = add_residual(
+                epilogue_value(accs[e], sa, __ldg(args.sw + cc), b,
+                               args.bias_mode, lut),
+                args, m0 + j, cc);
           }
         }
       }
@@ -315,8 +398,5 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem_base, tmem_cols);
   }
 }
-
-
-
 
 } // namespace pir2b

@@ -2,4 +2,5 @@
 // one definition of the device status word without relocatable device code.
 #include "quant.cuh"
 #include "gemm_i8.cuh"
+#include "pointwise.cuh"
 #include "capi.cuh"

@@ -24,9 +24,9 @@ enum DeviceStatus : int {
   kStatusTimeoutConvert = 0x104,
 };
 
-// ~2^22 polls with a nanosleep back-off: well above any legitimate wait
-// (microseconds) and well below a second.
-constexpr uint32_t kMaxPolls = 1u << 22;
+// Budget of a bounded wait, in SM clock cycles (~1 s at 1.965 GHz): far
+// above any legitimate pipeline wait (microseconds), far below a hang.
+constexpr long long kWaitCycles = 2000000000LL;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -78,15 +78,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`. Returns false (and records
-// `code`) when the poll budget runs out.
+// Bounded wait for phase `parity` of `bar`.  try_wait itself suspends the
+// thread for a short hardware-defined time, so the loop polls without
+// sleeping and checks the clock every 64 polls.  Returns false (and records
+// `code` in the status word) when the budget runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
                                           int code) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
-    if (mbar_try_wait(bar, parity))
-      return true;
-    if (i > 64)
-      __nanosleep(64);
+  if (mbar_try_wait(bar, parity))
+    return true;
+  const long long t0 = clock64();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity))
+        return true;
+    if (clock64() - t0 > kWaitCycles)
+      break;
   }
   atomicCAS(&g_device_status, 0, code);
   return false;
@@ -205,6 +212,23 @@ __device__ __forceinline__ void tmem_ld_16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+// 32 lanes x 32 bits, 32 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld_32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -226,6 +250,28 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) |
          ((m >> 4) << 24);
+}
+
+// 2-D tiled bulk tensor store from this CTA's shared memory (rows and
+// columns outside the tensor map's extent are not written).
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src,
+                                             int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], "
+      "[%1];" ::"l"(tmap),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit_and_wait() {
+  asm volatile("cp.async.bulk.commit_group;\n\t"
+               "cp.async.bulk.wait_group 0;" ::
+                   : "memory");
+}
+
+// Barrier among `count` threads (a multiple of 32) on hardware barrier `id`.
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---------------------------------------------------------------- cluster

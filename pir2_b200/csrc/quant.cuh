@@ -128,6 +128,9 @@ __device__ __forceinline__ float row_scale(float m) {
 template <int kBits, int kCpt, bool kVec>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantArgs a) {
   __shared__ float red[32];
+  // Programmatic dependent launch: inputs come from the previous kernel.
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int nchunks = a.kpad >> 3;
   const __nv_bfloat16 *xr = a.x + int64_t(row) * a.ldx;
@@ -207,6 +210,9 @@ __device__ __forceinline__ void chunk_values(const QuantArgs &a,
 template <int kBits, bool kVec>
 __global__ void __launch_bounds__(512) quant_rows_stream_kernel(const QuantArgs a) {
   __shared__ float red[32];
+  // Programmatic dependent launch: inputs come from the previous kernel.
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int nchunks = a.kpad >> 3;
   const __nv_bfloat16 *xr = a.x + int64_t(row) * a.ldx;
@@ -228,6 +234,64 @@ __global__ void __launch_bounds__(512) quant_rows_stream_kernel(const QuantArgs 
     float v[8];
     chunk_values<kBits, kVec>(a, xr, ur, chunk, v);
     store_codes<kBits>(v, s, qrow, chunk * 8);
+  }
+}
+
+// Rows split across a thread-block cluster (small M, long rows): CTA rank r
+// of the cluster owns a contiguous slice of the row's 8-element chunks,
+// reduces its block maximum, publishes it in shared memory, and every CTA
+// reads all ranks' maxima through distributed shared memory.  Same
+// arithmetic as quant_rows_kernel (the maximum is order independent).
+template <int kBits, int kCpt, bool kVec>
+__global__ void __launch_bounds__(256) quant_rows_cluster_kernel(const QuantArgs a) {
+  __shared__ float red[32];
+  __shared__ float slice_max;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int row = blockIdx.y;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t csize = gridDim.x;
+  const int nchunks = a.kpad >> 3;
+  const int per = (nchunks + int(csize) - 1) / int(csize);
+  const int c_begin = int(rank) * per;
+  const int c_end = min(nchunks, c_begin + per);
+  const __nv_bfloat16 *xr = a.x + int64_t(row) * a.ldx;
+  const __nv_bfloat16 *ur = a.up ? a.up + int64_t(row) * a.ldu : nullptr;
+  float v[kCpt][8];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j) {
+    const int chunk = c_begin + int(threadIdx.x) + j * int(blockDim.x);
+    if (chunk < c_end) {
+      chunk_values<kBits, kVec>(a, xr, ur, chunk, v[j]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[j][i] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      m = fmaxf(m, fabsf(v[j][i]));
+  }
+  m = block_max(m, red);
+  if (threadIdx.x == 0)
+    slice_max = m;
+  cluster_sync();
+  float row_max = 0.f;
+  const uint32_t addr = smem_u32(&slice_max);
+  for (uint32_t p = 0; p < csize; ++p)
+    row_max = fmaxf(row_max, __int_as_float(ld_cluster_s32(map_peer(addr, p))));
+  // No CTA may exit while a peer still reads its slice maximum.
+  cluster_sync();
+  const float s = row_scale<kBits>(row_max);
+  if (rank == 0 && threadIdx.x == 0)
+    a.scales[row] = s;
+  uint8_t *qrow = a.q + int64_t(row) * (kBits == 8 ? a.kpad : a.kpad / 2);
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j) {
+    const int chunk = c_begin + int(threadIdx.x) + j * int(blockDim.x);
+    if (chunk < c_end)
+      store_codes<kBits>(v[j], s, qrow, chunk * 8);
   }
 }
 
@@ -304,6 +368,9 @@ __device__ __forceinline__ void store_nvfp4_chunk(const float (&v)[8],
 template <int kOut, int kCpt, int kNorm, bool kMod, bool kRes>
 __global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
   __shared__ float red[32];
+  // Programmatic dependent launch: inputs come from the previous kernel.
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t row = blockIdx.x;
   const int nchunks = a.kpad >> 3;
   const int64_t cond = row / a.tokens;
@@ -461,20 +528,66 @@ static inline int pick_threads(int nchunks, int cpt) {
   return t < 32 ? 32 : t;
 }
 
+// Launches `kernel<<<rows, threads>>>(args)` with programmatic dependent
+// launch enabled, so its prologue may overlap the previous kernel's tail.
+template <typename Args>
+static cudaError_t launch_rows(void (*kernel)(Args), const Args &a,
+                               int64_t rows, int threads, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(rows), 1, 1);
+  cfg.blockDim = dim3(unsigned(threads), 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 template <int kBits, int kCpt>
 static cudaError_t launch_quant(const QuantArgs &a, int64_t rows, bool vec,
                                 cudaStream_t st) {
   const int threads = pick_threads(a.kpad / 8, kCpt);
   if (vec)
-    quant_rows_kernel<kBits, kCpt, true><<<dim3(unsigned(rows)), threads, 0, st>>>(a);
-  else
-    quant_rows_kernel<kBits, kCpt, false><<<dim3(unsigned(rows)), threads, 0, st>>>(a);
-  return cudaGetLastError();
+    return launch_rows(quant_rows_kernel<kBits, kCpt, true>, a, rows, threads, st);
+  return launch_rows(quant_rows_kernel<kBits, kCpt, false>, a, rows, threads, st);
+}
+
+template <int kBits>
+static cudaError_t launch_quant_cluster(const QuantArgs &a, int64_t rows,
+                                        int csize, bool vec, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(csize), unsigned(rows), 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(csize);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (vec)
+    return cudaLaunchKernelEx(&cfg, quant_rows_cluster_kernel<kBits, 2, true>, a);
+  return cudaLaunchKernelEx(&cfg, quant_rows_cluster_kernel<kBits, 2, false>, a);
 }
 
 cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
                            bool vec, cudaStream_t st) {
   const int nchunks = a.kpad / 8;
+  // Few long rows: spread each row over a cluster of CTAs (<= 8, each with
+  // 128 threads x 2 chunks) so the launch covers more of the 148 SMs.
+  if (rows <= 64 && nchunks > 256) {
+    int csize = (nchunks + 255) / 256;
+    csize = csize <= 2 ? 2 : (csize <= 4 ? 4 : 8);
+    if (nchunks <= csize * 256)
+      return bits == 8 ? launch_quant_cluster<8>(a, rows, csize, vec, st)
+                       : launch_quant_cluster<4>(a, rows, csize, vec, st);
+  }
   // <= 256 threads with up to 4 chunks each covers Kpad <= 8192 with the row
   // held in registers; wider rows (up to 65536) take two passes over x.
   if (nchunks <= 256)
@@ -483,27 +596,19 @@ cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
   if (nchunks <= 1024)
     return bits == 8 ? launch_quant<8, 4>(a, rows, vec, st)
                      : launch_quant<4, 4>(a, rows, vec, st);
-  if (vec) {
-    if (bits == 8)
-      quant_rows_stream_kernel<8, true><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
-    else
-      quant_rows_stream_kernel<4, true><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
-  } else {
-    if (bits == 8)
-      quant_rows_stream_kernel<8, false><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
-    else
-      quant_rows_stream_kernel<4, false><<<dim3(unsigned(rows)), 512, 0, st>>>(a);
-  }
-  return cudaGetLastError();
+  if (vec)
+    return bits == 8 ? launch_rows(quant_rows_stream_kernel<8, true>, a, rows, 512, st)
+                     : launch_rows(quant_rows_stream_kernel<4, true>, a, rows, 512, st);
+  return bits == 8 ? launch_rows(quant_rows_stream_kernel<8, false>, a, rows, 512, st)
+                   : launch_rows(quant_rows_stream_kernel<4, false>, a, rows, 512, st);
 }
 
 template <int kOut, int kCpt, int kNorm, bool kMod, bool kRes>
 static cudaError_t launch_norm4(const NormArgs &a, int64_t rows,
                                 cudaStream_t st) {
   const int threads = pick_threads(a.kpad / 8, kCpt);
-  norm_quant_kernel<kOut, kCpt, kNorm, kMod, kRes>
-      <<<dim3(unsigned(rows)), threads, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_rows(norm_quant_kernel<kOut, kCpt, kNorm, kMod, kRes>, a, rows,
+                     threads, st);
 }
 
 template <int kOut, int kCpt>

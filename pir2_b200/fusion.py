@@ -1,0 +1,111 @@
+"""Residual-add fusion for the GR00T decoder layers and DiT blocks.
+
+piR2 runs the residual epilogue as an operator candidate (residual writer of
+coexecution/kernels/ampere_ada/epilogue.py) and fuses the DiT attention
+residual with norm3 + pack (AdditionalConnections residual_quant).  This
+installer applies the residual epilogue where the residual stream meets a
+quantized projection, keeping the model's own forward code:
+
+* `Qwen3VLTextDecoderLayer`: h + o_proj(...) and h + down_proj(...) become
+  o_proj / down_proj GEMMs whose epilogue adds h;
+* DiT `BasicTransformerBlock`: x + to_out(...) and x + ff(...) likewise, and
+  norm3 (non-affine LayerNorm) + pack of the FFN input becomes the fused
+  LayerNorm producer (zero AdaLN modulation, which leaves the normalized
+  bf16 values unchanged, as piR2's residual fusion does).
+
+Results are bitwise those of the unfused quantized model: the epilogue adds
+the residual to the bf16 GEMM output in fp32 and rounds once, exactly as
+torch's bf16 addition does.
+"""
+
+import torch
+
+from .connections import packed_input
+from .modulation import prepare_norm_modulation
+
+
+class ResidualFusion:
+    def __init__(self, model, controller):
+        self.controller = controller
+        self.saved = []
+        self.layers, self.blocks = [], []
+        for name, module in model.named_modules():
+            kind = type(module).__name__
+            if kind == "Qwen3VLTextDecoderLayer" and self._quantized(module.self_attn.o_proj, module.mlp.down_proj):
+                self.layers.append(module)
+            elif kind == "BasicTransformerBlock" and self._quantized(module.attn1.to_out[0], module.ff.net[2]):
+                self.blocks.append(module)
+
+    def _quantized(self, *modules):
+        sites = {id(m): n for n, (m, _, _) in self.controller.sites.items()}
+        return all(id(m) in sites for m in modules)
+
+    def _q(self, module, bits):
+        sites = {id(m): n for n, (m, _, _) in self.controller.sites.items()}
+        return self.controller.quant[bits][sites[id(module)]]
+
+    def set(self, bits, *, norm_pack=True):
+        self.close()
+        for layer in self.layers:
+            self.saved.append((layer, "forward" in layer.__dict__, layer.__dict__.get("forward")))
+            o_q, down_q = self._q(layer.self_attn.o_proj, bits), self._q(layer.mlp.down_proj, bits)
+
+            def forward(h, cos, sin, layer=layer, o_q=o_q, down_q=down_q):
+                o_q.pending_residual(h)
+                h = layer.self_attn(layer.input_layernorm(h), cos, sin)
+                down_q.pending_residual(h)
+                return layer.mlp(layer.post_attention_layernorm(h))
+
+            layer.forward = forward
+        for block in self.blocks:
+            self.saved.append((block, "forward" in block.__dict__, block.__dict__.get("forward")))
+            out_q, down_q = self._q(block.attn1.to_out[0], bits), self._q(block.ff.net[2], bits)
+            zero = torch.zeros((1, 1, block.dim), device=block.ff.net[2].weight.device, dtype=torch.bfloat16)
+            fuse_norm = (
+                norm_pack
+                and isinstance(block.norm3, torch.nn.LayerNorm)
+                and not block.norm3.elementwise_affine
+                and self._quantized(block.ff.net[0].proj)
+            )
+
+            def forward(
+                hidden_states,
+                attention_mask=None,
+                encoder_hidden_states=None,
+                encoder_attention_mask=None,
+                temb=None,
+                block=block,
+                out_q=out_q,
+                down_q=down_q,
+                zero=zero,
+                fuse_norm=fuse_norm,
+                bits=bits,
+            ):
+                x = hidden_states
+                normalized = block.norm1(x, temb) if block.norm_type == "ada_norm" else block.norm1(x)
+                out_q.pending_residual(x)
+                x = block.attn1(
+                    normalized,
+                    encoder_hidden_states=encoder_hidden_states,
+                    attention_mask=encoder_attention_mask if encoder_hidden_states is not None else attention_mask,
+                )
+                if fuse_norm:
+                    shape = (x.shape[0], 1, x.shape[-1])
+                    packed = prepare_norm_modulation(
+                        x, zero.expand(shape), zero.expand(shape), bits, eps=block.norm3.eps
+                    )
+                    ff_in = packed_input(packed, x.shape)
+                else:
+                    ff_in = block.norm3(x)
+                down_q.pending_residual(x)
+                return block.ff(ff_in)
+
+            block.forward = forward
+
+    def close(self):
+        for module, had, forward in self.saved:
+            if had:
+                module.forward = forward
+            elif "forward" in module.__dict__:
+                del module.forward
+        self.saved = []

@@ -23,6 +23,11 @@ def npad(n):
     return (n + NPAD_MULTIPLE - 1) // NPAD_MULTIPLE * NPAD_MULTIPLE
 
 
+# Optional launch recorder used by the benchmark to time individual GEMM
+# launches with CUDA events (None in normal use).
+launch_recorder = None
+
+
 def _ptr(t):
     return None if t is None else t.data_ptr()
 
@@ -138,11 +143,13 @@ def norm_quant_rows(
     return data, scales, residual
 
 
-def gemm(a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, n_store=None, out=None, tactic=-1):
+def gemm(a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, residual=None, n_store=None, out=None, tactic=-1):
     """Quantized GEMM + dequant epilogue -> bf16 [m, n_store] (or into `out`).
 
     bias_mode defaults to piR2's `gemm` semantics: add the bias, or +0 when
     the bias is None.  Pass _lib.BIAS_NONE for `gemm_biasless` without bias.
+    `residual` (bf16 [m, >= n_store], unit column stride) is added to the
+    bf16 result in fp32 and rounded again (the residual epilogue).
     """
     m = a.shape[0]
     n_pad = w.shape[0]
@@ -156,12 +163,23 @@ def gemm(a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, n_store=None
     ldo = out.stride(0) if out.ndim == 2 else n_store
     if out.dtype != torch.bfloat16 or out.stride(-1) != 1:
         raise ValueError("GEMM output must be BF16 with unit column stride")
+    ldr = 0
+    if residual is not None:
+        residual = residual.reshape(m, -1) if residual.dim() != 2 else residual
+        if residual.dtype != torch.bfloat16 or residual.stride(-1) != 1 or residual.shape[1] < n_store:
+            raise ValueError("Residual must be BF16 [M, >= N] with unit column stride")
+        ldr = residual.stride(0) if m > 1 else residual.shape[1]
+    recorder = launch_recorder
+    if recorder is not None:
+        recorder.before(a.device)
     status = _lib.lib().pir2b_gemm(
         a.data_ptr(), sa.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias), bias_mode,
-        _ptr(out_lut), bits, m, n_pad, k_pad, out.data_ptr(), ldo, n_store, int(tactic),
-        _stream(a.device),
+        _ptr(out_lut), _ptr(residual), ldr, bits, m, n_pad, k_pad, out.data_ptr(), ldo, n_store,
+        int(tactic), _stream(a.device),
     )
     _lib.check(status, "pir2b_gemm")
+    if recorder is not None:
+        recorder.after(a.device, bits=bits, m=m, n=n_store, k=k_pad, npad=n_pad)
     return out
 
 
@@ -169,3 +187,23 @@ def pack_nvfp4(x):
     """NVFP4 pack of contiguous bf16 rows -> (packed [rows, k/2], swizzled sf)."""
     data, scales, _ = norm_quant_rows(x.reshape(-1, x.shape[-1]).contiguous(), _lib.OUT_NVFP4)
     return data, scales
+
+
+def qk_norm_rope(qkv, q_weight, k_weight, cos, sin, *, tokens, hq, hk, eps, head_dim=128):
+    """Fused q/k RMSNorm + RoPE of a grouped q|k|v projection output.
+
+    qkv: bf16 [B*T, >= (hq + 2hk) * head_dim] rows with unit column stride.
+    Returns q [B, hq, T, D], k [B, hk, T, D], v [B, hk, T, D] (contiguous).
+    """
+    matrix, rows, _, ld = _rows(qkv)
+    b = rows // tokens
+    q = torch.empty((b, hq, tokens, head_dim), device=qkv.device, dtype=torch.bfloat16)
+    k = torch.empty((b, hk, tokens, head_dim), device=qkv.device, dtype=torch.bfloat16)
+    v = torch.empty((b, hk, tokens, head_dim), device=qkv.device, dtype=torch.bfloat16)
+    status = _lib.lib().pir2b_qk_norm_rope(
+        matrix.data_ptr(), ld, q_weight.data_ptr(), k_weight.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+        rows, tokens, hq, hk, head_dim, float(eps), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        _stream(qkv.device),
+    )
+    _lib.check(status, "pir2b_qk_norm_rope")
+    return q, k, v

@@ -1,0 +1,73 @@
+"""BF16 pointwise fusion around the quantized text-attention projections.
+
+piR2 fuses Qwen3's rotary embedding and RMSNorm with Triton kernels
+(coexecution/fused_ops.py, fusion modes "rope", "rmsnorm", "rope_rms",
+"all").  `TextAttentionFusion` does the same next to the quantized path: the
+grouped q|k|v GEMM runs once, then one sm_100a kernel applies the per-head
+q_norm / k_norm, the rotary embedding and the [B, H, T, D] relayout of q, k
+and v (replacing three contiguous copies, two torch RMSNorms and two torch
+RoPE chains), then attention and the quantized o_proj run as before.
+The RoPE arithmetic is bitwise torch's; the per-head mean of squares is
+reduced in a different order than torch's (tolerance-level, like piR2's
+own fused norms).
+"""
+
+import torch.nn.functional as F
+
+from . import ops
+
+
+class TextAttentionFusion:
+    def __init__(self, model, controller):
+        self.controller = controller
+        self.saved = []
+        names = {id(m): n for n, m in model.named_modules()}
+        self.targets = []
+        for module in model.modules():
+            if type(module).__name__ != "Qwen3VLTextAttention":
+                continue
+            if module.head_dim != 128:
+                continue
+            q_name = names.get(id(module.q_proj))
+            self.targets.append((module, q_name))
+
+    def _group(self, bits, q_name):
+        for names, group in self.controller.grouped[bits]:
+            if names[0] == q_name and len(names) == 3:
+                return group
+        return None
+
+    def set(self, bits):
+        self.close()
+        for attn, q_name in self.targets:
+            group = self._group(bits, q_name)
+            if group is None:
+                continue
+            self.saved.append((attn, "forward" in attn.__dict__, attn.__dict__.get("forward")))
+
+            def forward(x, cos, sin, attn=attn, group=group):
+                b, t = x.shape[0], x.shape[1]
+                qkv = group.linear(x)
+                q, k, v = ops.qk_norm_rope(
+                    qkv.reshape(b * t, qkv.shape[-1]),
+                    attn.q_norm.weight,
+                    attn.k_norm.weight,
+                    cos,
+                    sin,
+                    tokens=t,
+                    hq=attn.heads,
+                    hk=attn.kv_heads,
+                    eps=attn.q_norm.variance_epsilon,
+                )
+                y = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+                return attn.o_proj(y.transpose(1, 2).reshape(b, t, attn.heads * attn.head_dim))
+
+            attn.forward = forward
+
+    def close(self):
+        for module, had, forward in self.saved:
+            if had:
+                module.forward = forward
+            elif "forward" in module.__dict__:
+                del module.forward
+        self.saved = []

@@ -47,7 +47,10 @@ def assert_status_clean():
 
 
 @pytest.mark.parametrize("bits", [8, 4])
-@pytest.mark.parametrize("rows,k", [(1, 2048), (17, 130), (5, 1), (3, 127), (64, 6144), (1024, 2048), (7, 12288), (2, 40000)])
+@pytest.mark.parametrize(
+    "rows,k",
+    [(1, 2048), (17, 130), (5, 1), (3, 127), (64, 6144), (1024, 2048), (7, 12288), (2, 40000), (17, 6144), (1, 4100)],
+)
 def test_quant_rows_plain_bitwise(bits, rows, k):
     g = torch.Generator().manual_seed(rows * 131 + k)
     x = randn_bf16(g, rows, k, outliers=True)
@@ -68,6 +71,19 @@ def test_quant_rows_lut_modes_bitwise(bits, kind, gated):
     lut = device_lut(kind)
     q, s = ops.quant_rows(x.cuda(), bits, lut=lut, up=up.cuda() if gated else None)
     rq, rs = oracle.quant_rows(bits_of(x), bits, lut_bits=bits_of(lut), up_bits=bits_of(up) if gated else None)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy().view(np.uint8), rq.view(np.uint8))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_quant_rows_cluster_path_lut_gated_bitwise(bits):
+    """Few long rows take the cluster-split kernel; LUT and gate included."""
+    g = torch.Generator().manual_seed(8)
+    x = randn_bf16(g, 17, 6144)
+    up = randn_bf16(g, 17, 6144)
+    lut = device_lut("silu")
+    q, s = ops.quant_rows(x.cuda(), bits, lut=lut, up=up.cuda())
+    rq, rs = oracle.quant_rows(bits_of(x), bits, lut_bits=bits_of(lut), up_bits=bits_of(up))
     assert np.array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
     assert np.array_equal(q.cpu().numpy().view(np.uint8), rq.view(np.uint8))
 
@@ -235,3 +251,56 @@ def test_nvfp4_pack_bitwise(rows, k):
     rr, jj = np.meshgrid(np.arange(rows), np.arange(k // 16), indexing="ij")
     off = oracle.nvfp4_sf_offset(rr, jj, blocks_k)
     assert np.array_equal(sfg.reshape(-1)[off], rsf.reshape(-1)[off])
+
+
+def test_qk_norm_rope_matches_torch():
+    """Fused q/k RMSNorm + RoPE vs the torch sequence it replaces: RoPE is
+    bitwise; the per-head mean of squares is reduced in another order, so a
+    rare element may differ by one bf16 ulp."""
+    g = torch.Generator().manual_seed(77)
+    b, t, hq, hk, d = 1, 544, 16, 8, 128
+    qkv = (torch.randn(b * t, (hq + 2 * hk) * d, generator=g) * 2).to(torch.bfloat16).cuda()
+    qw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16).cuda()
+    kw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16).cuda()
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    freqs = torch.outer(torch.arange(t, dtype=torch.float32), inv)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos().to(torch.bfloat16).cuda(), emb.sin().to(torch.bfloat16).cuda()
+    q, k, v = ops.qk_norm_rope(qkv, qw, kw, cos, sin, tokens=t, hq=hq, hk=hk, eps=1e-6)
+
+    def rms(x, w):
+        h = x.float()
+        h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6)
+        return w * h.to(torch.bfloat16)
+
+    def rot(x):
+        return torch.cat((-x[..., d // 2:], x[..., : d // 2]), dim=-1)
+
+    view = qkv.view(b, t, hq + 2 * hk, d)
+    rq = rms(view[:, :, :hq], qw).transpose(1, 2)
+    rk = rms(view[:, :, hq : hq + hk], kw).transpose(1, 2)
+    rq = rq * cos + rot(rq) * sin
+    rk = rk * cos + rot(rk) * sin
+    rv = view[:, :, hq + hk :].transpose(1, 2)
+    assert torch.equal(v, rv.contiguous())
+    for got, ref in ((q, rq), (k, rk)):
+        diff = (got.float() - ref.float()).abs()
+        ulp = ref.float().abs().clamp_min(1e-3) * 2 ** -7
+        assert bool((diff <= ulp).all())
+        assert float((got != ref).float().mean()) < 0.01
+
+
+def test_gemm_residual_epilogue_bitwise():
+    g = torch.Generator().manual_seed(41)
+    for m, k, n in ((17, 1536, 1536), (544, 2048, 2048), (64, 6144, 2048)):
+        _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, n, 8)
+        residual = randn_bf16(g, m, n)
+        out = ops.gemm(
+            torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(qw).cuda(),
+            torch.from_numpy(sw).cuda(), b.cuda(), 8, residual=residual.cuda(), n_store=n,
+        )
+        y = oracle.gemm_epilogue(oracle.int_matmul(qa, qw), sa, sw, bits_of(b), 2)[:, :n]
+        ref = oracle.f32_to_bf16_bits(
+            (oracle.bf16_bits_to_f32(y) + oracle.bf16_bits_to_f32(bits_of(residual))).astype(np.float32)
+        )
+        assert np.array_equal(bits_of(out), ref)

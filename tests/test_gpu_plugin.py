@@ -1,0 +1,213 @@
+"""GPU contract tests of the plugin API, ported from piR2's own GPU tests
+(tests/gpu/test_quantization_gpu.py, test_shape_tactics_gpu.py): the
+installed quantized Linear matches the explicit quantized formula bitwise
+and restores the model; grouped projections dispatch once; fused packs equal
+their unfused counterparts; graph replay equals eager.
+"""
+
+from types import SimpleNamespace
+from unittest.mock import patch
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from pir2_b200 import _lib
+from pir2_b200.connections import AdditionalConnections
+from pir2_b200.fused import prepare_gelu
+from pir2_b200.integer import prepare_activation
+from pir2_b200.linear import prepare
+from pir2_b200.projections import inventory
+from pir2_b200.transformer import TransformerINT
+
+pytestmark = pytest.mark.gpu
+
+
+def equal(actual, expected):
+    assert actual.shape == expected.shape and actual.dtype == expected.dtype
+    assert torch.equal(actual.contiguous().view(torch.uint8), expected.contiguous().view(torch.uint8))
+
+
+def bits_of(t):
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def from_bits(b, device="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+class Norm(torch.nn.Module):
+    """AdaLN fixture of piR2's tests (tests/helpers/projection_models.py:18-33)."""
+
+    def __init__(self, width):
+        super().__init__()
+        self.norm = torch.nn.LayerNorm(width, elementwise_affine=False, device="cuda", dtype=torch.bfloat16)
+        self.silu = torch.nn.SiLU()
+        self.linear = torch.nn.Linear(width, 2 * width, device="cuda", dtype=torch.bfloat16)
+
+    def forward(self, x, temb):
+        scale, shift = self.linear(self.silu(temb)).chunk(2, dim=-1)
+        if scale.ndim == 2:
+            scale, shift = scale[:, None], shift[:, None]
+        return self.norm(x) * (1 + scale) + shift
+
+
+def policy_for(blocks):
+    return SimpleNamespace(model=SimpleNamespace(action_head=SimpleNamespace(model=SimpleNamespace(transformer_blocks=blocks))))
+
+
+def torch_quantized_linear(x, weight, bias, bits):
+    """The reference's explicit formula (test_quantization_gpu.py:37-44),
+    evaluated with CUDA torch (where `tensor / scalar` multiplies by the
+    fp32 reciprocal, as the reference kernels do)."""
+    limit = 2 ** (bits - 1) - 1
+    xs = x.float().abs().amax(dim=-1) / limit
+    ws = weight.float().abs().amax(dim=-1) / limit
+    qx = torch.round(x.float() / xs[:, None]).clamp(-limit, limit)
+    qw = torch.round(weight.float() / ws[:, None]).clamp(-limit, limit)
+    acc = (qx.double() @ qw.double().t()).float()   # exact integers
+    y = acc * xs[:, None] * ws[None, :]
+    if bias is not None:
+        y = y + bias.float()
+    return y.to(torch.bfloat16)
+
+
+def test_cuda_scalar_division_is_a_reciprocal_multiply():
+    """Pins the torch behaviour the reference's weight scales rely on."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    m = torch.rand(1 << 20, device="cuda", generator=g) * 10
+    for limit in (127, 7):
+        via_div = m / limit
+        via_mul = m * (torch.tensor(1.0, device="cuda") / limit)
+        assert torch.equal(via_div, via_mul)
+        true_div = m / torch.full_like(m, limit)
+        assert not torch.equal(via_div, true_div)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("native", [False, True])
+@torch.inference_mode()
+def test_integer_linear_matches_quantized_reference_and_restores(bits, native):
+    torch.manual_seed(195)
+    linear = torch.nn.Linear(130, 64, device="cuda", dtype=torch.bfloat16).eval()
+    model = torch.nn.Sequential(linear)
+    x = torch.randn(17, 130, device="cuda", dtype=torch.bfloat16)
+    original = model(x)
+    expected = torch_quantized_linear(x, linear.weight, linear.bias, bits)
+    adapter = TransformerINT(model, {"0"}, native=native, expanded=True)
+    try:
+        adapter.set(f"w{bits}a{bits}")
+        equal(model(x), expected)
+        # And the CPU oracle agrees bitwise.
+        ref = oracle.linear_w8a8(bits_of(x), linear.weight.float().cpu().numpy(), bits_of(linear.bias), bits)
+        assert np.array_equal(bits_of(model(x)), ref)
+    finally:
+        adapter.close()
+    assert "forward" not in linear.__dict__
+    equal(model(x), original)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("tokens", [1, 41])
+@torch.inference_mode()
+def test_condition_group_reuses_pack_and_gemm_and_releases_inputs(bits, tokens):
+    dit = torch.nn.Module()
+    blocks = [torch.nn.Module(), torch.nn.Module()]
+    for block in blocks:
+        block.norm1 = Norm(64)
+    dit.transformer_blocks = torch.nn.ModuleList(blocks)
+    dit.proj_out_1 = torch.nn.Linear(64, 128, device="cuda", dtype=torch.bfloat16)
+    model = torch.nn.Module()
+    model.action_head = torch.nn.Module()
+    model.action_head.model = dit
+    sites = inventory(model, expanded=True)[0]
+    modules = [site[0] for site in sites.values()]
+    condition = torch.randn((1, 64) if tokens == 1 else (1, tokens, 64), device="cuda", dtype=torch.bfloat16)
+    adapter = TransformerINT(model, sites, native=True, expanded=True, condition_group=True)
+    try:
+        for _ in range(2):
+            expected = [adapter.quant[bits][name](condition) for name in sites]
+            adapter.set(f"w{bits}a{bits}")
+            with patch.object(adapter, "dispatch", wraps=adapter.dispatch) as dispatch:
+                actual = [module(condition) for module in modules]
+                assert dispatch.call_count == 1
+            for value, reference in zip(actual, expected):
+                equal(value, reference)
+            group = adapter.grouped[bits][0][1]
+            assert group._input is None and group._output is None
+            condition.add_(0.25)
+        modules[0](condition)
+        assert group._input is condition
+    finally:
+        adapter.close()
+    assert group._input is None and group._output is None
+    assert not group._remaining
+    assert all("forward" not in module.__dict__ for module in modules)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@torch.inference_mode()
+def test_fused_activation_pack_matches_reference(bits):
+    x = torch.randn(17, 258, device="cuda", dtype=torch.bfloat16)
+    up = torch.randn_like(x)
+    lut = prepare_gelu(x.device, x.dtype, "tanh")
+    actual = prepare(x, bits, lut, up)
+    expected = prepare_activation(x, bits, up=up, gelu="tanh", pack_reuse=True)
+    equal(actual.data, expected.data)
+    equal(actual.scales, expected.scales)
+    # ... and both equal the pack of the materialized bf16(gelu(x) * up).
+    plain = prepare_activation((torch.nn.functional.gelu(x, approximate="tanh") * up), bits)
+    equal(actual.data, plain.data)
+    equal(actual.scales, plain.scales)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("per_token", [False, True])
+@torch.inference_mode()
+def test_modulation_pack_preserves_shared_and_per_token_inputs(bits, per_token):
+    norm = Norm(64)
+    x = torch.randn(2, 3, 64, device="cuda", dtype=torch.bfloat16)
+    temb = torch.randn((2, 3, 64) if per_token else (2, 64), device="cuda", dtype=torch.bfloat16)
+    expected = prepare_activation(norm(x, temb), bits, pack_reuse=True)
+    adapter = AdditionalConnections(policy_for([SimpleNamespace(norm1=norm)]), None, {})
+    try:
+        adapter.set(f"w{bits}a{bits}")
+        actual = norm(x, temb).for_bits(bits)
+        equal(actual.data, expected.data)
+        equal(actual.scales, expected.scales)
+        assert actual.shape == expected.shape
+    finally:
+        adapter.close()
+    assert "forward" not in norm.__dict__
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@torch.inference_mode()
+def test_graph_replay_equals_eager(bits):
+    torch.manual_seed(3)
+    linear = torch.nn.Linear(1536, 6144, device="cuda", dtype=torch.bfloat16).eval()
+    model = torch.nn.Sequential(linear)
+    adapter = TransformerINT(model, {"0"}, native=True, expanded=True)
+    try:
+        adapter.set(f"w{bits}a{bits}")
+        for rows in (41, 153, 17):
+            x = torch.randn(rows, 1536, device="cuda", dtype=torch.bfloat16)
+            eager = model(x)
+            graph = torch.cuda.CUDAGraph()
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(graph, stream=stream):
+                    out = model(x)
+            eager2 = model(x)
+            graph.replay()
+            torch.cuda.synchronize()
+            equal(out, eager)
+            equal(eager2, eager)
+            x.add_(0.5)
+            graph.replay()
+            torch.cuda.synchronize()
+            equal(out, model(x))
+    finally:
+        adapter.close()
+    assert _lib.device_status() == 0

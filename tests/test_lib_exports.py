@@ -41,7 +41,7 @@ def test_argument_errors_are_reported_without_touching_the_device():
     status = lib.pir2b_quant_rows(None, 0, None, 0, None, None, 0, 3, 1, 8, None, None, None)
     assert status == _lib.EINVAL
     assert b"bits" in lib.pir2b_last_error()
-    status = lib.pir2b_gemm(None, None, None, None, None, 0, None, 8, 1, 12, 128, None, 12, 12, -1, None)
+    status = lib.pir2b_gemm(None, None, None, None, None, 0, None, None, 0, 8, 1, 12, 128, None, 12, 12, -1, None)
     assert status == _lib.EINVAL
     with pytest.raises(ValueError, match="npad"):
         _lib.check(status, "pir2b_gemm")

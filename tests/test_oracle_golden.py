@@ -100,8 +100,9 @@ def test_channel_scales_match_reference():
 
 @pytest.mark.parametrize("bits", [8, 4])
 def test_weight_quant_matches_reference_formula(bits):
+    # The golden formula ran on CPU torch, which divides by L.
     w = oracle.bf16_bits_to_f32(GOLDEN["lin_w"])
-    q, s = oracle.quantize_weight(w, bits)
+    q, s = oracle.quantize_weight(w, bits, scale_rule="divide")
     codes = oracle.unpack_int4(q) if bits == 4 else q
     assert np.array_equal(codes[:64, :130], GOLDEN[f"lin_qw_b{bits}"])
     assert np.array_equal(s[:64].view(np.uint32), GOLDEN[f"lin_ws_b{bits}"].view(np.uint32))
@@ -116,9 +117,12 @@ def test_linear_matches_reference_bitwise_formula(bits):
     constant 1/L (integer.py:71, integer_dispatch.cu:237; pinned bitwise by
     the Triton vectors above).  The two scales can differ by one ulp, so the
     formula is compared on the rows where they coincide, which must then be
-    bitwise equal; every differing row must be one of the others."""
+    bitwise equal; every differing row must be one of the others.  (The
+    formula ran on CPU torch, where `tensor / scalar` divides; on CUDA torch
+    it multiplies by the reciprocal, which makes the formula and the kernels
+    agree on every row there.)"""
     w = oracle.bf16_bits_to_f32(GOLDEN["lin_w"])
-    y = oracle.linear_w8a8(GOLDEN["lin_x"], w, GOLDEN["lin_b"], bits)
+    y = oracle.linear_w8a8(GOLDEN["lin_x"], w, GOLDEN["lin_b"], bits, scale_rule="divide")
     ref = GOLDEN[f"lin_y_b{bits}"]
     x = oracle.bf16_bits_to_f32(GOLDEN["lin_x"])
     limit = np.float32(2 ** (bits - 1) - 1)
