@@ -53,6 +53,12 @@ def parse():
     p.add_argument("--batch", type=int, default=1, help="robots per GPU")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--cpu-sample-seconds", type=float, default=20.0)
+    p.add_argument(
+        "--kernel",
+        metavar="M,K,N",
+        help="time one quantized GEMM shape alone (for kernel profiling), not the step",
+    )
+    p.add_argument("--kernel-weights-mb", type=float, default=600.0, help="rotating weight copies for --kernel")
     return p.parse_args()
 
 
@@ -80,11 +86,13 @@ def barrier(world):
 
 
 def max_over_ranks(value, world):
+    """Maximum of a per-rank scalar (NCCL on GPUs, gloo on CPU ranks)."""
     if world == 1:
         return value
     import torch.distributed as dist
 
-    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -415,6 +423,7 @@ def run_ours(args, world, rank, local):
         cpu = {"value": round(cpu_ms, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample}
     # Kernel launches inside one timed step (graph nodes of this library).
     launches = count_launches(engine)
+    phases = phase_breakdown(engine)
     engine.release()
     session.close()
     if rank == 0:
@@ -446,12 +455,46 @@ def run_ours(args, world, rank, local):
                 "d2h_bytes_per_step": engine.d2h_bytes(),
             },
             "gpu_launches": launches,
+            "phases": phases,
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clock_summary,
             "device_status": status,
         }
         print(json.dumps(line), flush=True)
+
+
+def phase_breakdown(engine, reps=50):
+    """Device time of the VLM prefill and of the 4-step action head, each
+    replayed from its own graph (diagnostic split of the step)."""
+    policy = engine.policy
+    visual, ids, state, noise = engine.static
+    results = {}
+    with torch.inference_mode():
+        features = policy.backbone(visual, ids)
+        phases = {
+            "vlm_prefill_ms": lambda: policy.backbone(visual, ids),
+            "action_head_ms": lambda: policy.action_head.get_action(features, state, noise),
+        }
+        for name, fn in phases.items():
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(engine.stream):
+                fn()
+            engine.stream.synchronize()
+            with torch.cuda.graph(graph, stream=engine.stream):
+                fn()
+            with torch.cuda.stream(engine.stream):
+                for _ in range(3):
+                    graph.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(engine.stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(engine.stream)
+            engine.stream.synchronize()
+            results[name] = round(e0.elapsed_time(e1) / reps, 4)
+            del graph
+    return results
 
 
 def count_launches(engine):
@@ -485,8 +528,54 @@ def count_launches(engine):
     return sum(counts.values())
 
 
+def run_kernel(args):
+    """Times one quantized GEMM shape (activation pack excluded): rotating
+    weight copies totalling ~--kernel-weights-mb keep each launch's weights
+    out of L2.  Prints one JSON line with the per-launch time and rooflines."""
+    from pir2_b200 import ops
+
+    m, k, n = (int(v) for v in args.kernel.split(","))
+    bits = 8 if args.precision == "w8a8" else 4
+    kp, npd = ops.kpad(k), ops.npad(n)
+    wbytes = npd * kp * bits // 8
+    copies = max(1, min(64, int(args.kernel_weights_mb * 1e6 // wbytes)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    cols = kp if bits == 8 else kp // 2
+    dtype = torch.int8 if bits == 8 else torch.uint8
+    lo, hi = (-127, 128) if bits == 8 else (0, 256)
+    weights = [torch.randint(lo, hi, (npd, cols), device="cuda", dtype=dtype, generator=g) for _ in range(copies)]
+    qa = torch.randint(lo, hi, (m, cols), device="cuda", dtype=dtype, generator=g)
+    sa = torch.rand(m, device="cuda", generator=g)
+    sw = torch.rand(npd, device="cuda", generator=g)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    iters = max(args.steps, copies)
+    for i in range(args.warmup):
+        ops.gemm(qa, sa, weights[i % copies], sw, None, bits, n_store=n, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        ops.gemm(qa, sa, weights[i % copies], sw, None, bits, n_store=n, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    algo = wbytes + m * cols + 4 * m + 4 * npd + 2 * m * n
+    hbm, _ = peaks()
+    print(json.dumps({
+        "kernel": f"gemm_i8_kernel<{bits}>", "m": m, "k": k, "n": n, "us_per_launch": round(us, 3),
+        "algorithmic_bytes": algo, "GBs": round(algo / us / 1e3, 1), "hbm_frac": round(algo / us / 1e3 / hbm, 4),
+        "TOPS": round(2 * m * n * k / us / 1e6, 1), "int8_frac": round(2 * m * n * k / us / 1e6 / INT8_PEAK_TOPS, 4),
+        "weight_copies": copies, "launches": iters,
+        "note": "eager launches back to back; small shapes are host-launch bound",
+    }), flush=True)
+
+
 def main():
     args = parse()
+    if args.kernel:
+        torch.cuda.set_device(0)
+        run_kernel(args)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

@@ -140,15 +140,16 @@ static int make_map(CUtensorMap *map, const void *base, uint64_t cols,
 }
 
 // 2-D bf16 map over the [rows, cols] output (row stride ld elements), box
-// [box_rows, 128 columns], used by the epilogue's TMA store.
+// [box_rows, box_cols], used by the epilogue's TMA store.
 static int make_out_map(CUtensorMap *map, const void *base, uint64_t cols,
-                        uint64_t rows, uint64_t ld, uint32_t box_rows) {
+                        uint64_t rows, uint64_t ld, uint32_t box_rows,
+                        uint32_t box_cols) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr)
     return fail(PIR2B_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {ld * 2};
-  const cuuint32_t box[2] = {128u, box_rows};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                   const_cast<void *>(base), dims, strides, box, estr,
@@ -186,17 +187,27 @@ static int stages_for(int bits, int bn, int max_smem) {
 }
 
 // Picks the token tile, number of token tiles and the split-K cluster size
-// with a small cost model: per-CTA cycles ~ (K blocks / split) *
-// (fixed weight-tile cost + per-token cost) + epilogue, times the number of
-// waves over the SMs.
+// with a small cost model in SM cycles:
+//  * a 128 x BN x 128 K block costs max(347, 2 BN) MMA cycles (measured
+//    kind::i8 issue rate: N <= 128 has a fixed ~87-cycle MMA, full rate is
+//    8192 MAC/clk/SM);
+//  * its operands (16 KB of weights + 128 BN bytes) arrive at the CTA's share
+//    of HBM (~3400 B/clk for weights streamed once, single token tile) or of
+//    L2 (~9000 B/clk when several token tiles re-read the weights);
+//  * each CTA pays ~3000 cycles of launch, prologue and epilogue, +1500 for
+//    the cluster reduction of split-K;
+//  * CTAs under ~113 KB of shared memory run two per SM.
 static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
                           int sms, int max_smem) {
   const int ntiles = int((npad + 127) / 128);
   const int num_kb = int(kpad / 128);
-  GemmPlan best{16, 1, 1, 2, 0};
+  GemmPlan best{0, 0, 0, 0, 0};   // smem == 0 marks "no plan"
   double best_cost = 1e30;
+  // One token tile up to 256 tokens (weights streamed once); larger M also
+  // tries 1-3 extra tiles to balance the waves.
   const int mt0 = int((m + 255) / 256);
-  for (int mt = mt0; mt <= mt0 + 3; ++mt) {
+  const int mt1 = m <= 256 ? mt0 : mt0 + 3;
+  for (int mt = mt0; mt <= mt1; ++mt) {
     int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
     if (bn > 256 || bn < 16)
       continue;
@@ -204,20 +215,35 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
       continue;  // an empty token tile
     const int budget = (mt == 1 && bn <= 64) ? std::min(max_smem, kCoResidentSmem) : max_smem;
     const int stages = stages_for(bits, bn, budget);
-    if (size_t(stages) * (16384 + size_t(bn) * 128) < size_t(bn) * 512)
-      continue;  // split-K partials must fit in the stage buffers
+    const size_t smem = gemm_smem(bits, bn, stages);
+    if (smem > size_t(max_smem))
+      continue;
+    // Split-K reuses the stage buffers for the int32 partial tile and the
+    // rank's bf16 staging slice.
+    const bool split_fits =
+        size_t(stages) * (16384 + size_t(bn) * 128) >= size_t(bn) * (512 + 128);
+    const int per_sm = smem <= 113 * 1024 ? 2 : 1;
+    const double scale = bits == 4 ? 0.5 : 1.0;
+    const double w_bytes = 16384.0 * scale;     // weight tile per K block
+    const double a_bytes = 128.0 * bn * scale;  // token tile per K block
     for (int s = 1; s <= 8; s *= 2) {
-      if (s > num_kb)
+      if (s > num_kb || (s > 1 && !split_fits))
         break;
       const int ctas = ntiles * mt * s;
-      const int waves = (ctas + sms - 1) / sms;
+      const int slots = sms * per_sm;
+      const int waves = (ctas + slots - 1) / slots;
+      const int active = std::min(ctas, slots);
+      // Weights come from HBM once (single token tile) or from L2; token
+      // tiles are L2-resident.  Per-SM fill rate is capped at 128 B/clk.
+      const double w_bw = std::min(128.0, (mt == 1 ? 3400.0 : 9000.0) / active);
+      const double a_bw = std::min(128.0, 9000.0 / active);
       const double kb = double(num_kb) / s;
-      const double per_cta = kb * (700.0 + 6.0 * bn) + 1500.0 +
-                             (s > 1 ? 2.0 * bn * 128 / 32 : 0.0);
+      const double per_kb = std::max(std::max(347.0, 2.0 * bn), w_bytes / w_bw + a_bytes / a_bw);
+      const double per_cta = kb * per_kb + 3000.0 + (s > 1 ? 1500.0 : 0.0);
       const double cost = waves * per_cta;
       if (cost < best_cost * 0.999) {
         best_cost = cost;
-        best = GemmPlan{bn, mt, s, stages, gemm_smem(bits, bn, stages)};
+        best = GemmPlan{bn, mt, s, stages, smem};
       }
     }
   }
@@ -423,6 +449,10 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
   if (int r = device_info(&dev))
     return r;
   const GemmPlan plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem);
+  if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
+      plan.smem > size_t(dev->max_smem))
+    return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",
+                (long long)m, (long long)npad, (long long)kpad);
   const uint64_t row_bytes = bits == 8 ? uint64_t(kpad) : uint64_t(kpad / 2);
   const uint32_t box_cols = bits == 8 ? 128u : 64u;
   CUtensorMap tm_w, tm_a;
@@ -450,16 +480,16 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
   args.bn = plan.bn;
   args.stages = plan.stages;
   args.splits = plan.splits;
-  // The epilogue stages the tile in shared memory and writes it with one TMA
-  // store when the output rows are 16-byte aligned; otherwise it stores
-  // directly.  Split-K tiles are reduced through cluster shared memory and
-  // stored directly.
-  args.tma_store = (plan.splits == 1 && ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  // The epilogue stages the tile (or, with split-K, each cluster rank's
+  // channel slice) in shared memory and writes it with one TMA store when
+  // the output rows are 16-byte aligned; otherwise it stores directly.
+  args.tma_store = (ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
   CUtensorMap tm_out;
   memset(&tm_out, 0, sizeof(tm_out));
   if (args.tma_store) {
     if (int r = make_out_map(&tm_out, out, uint64_t(n_store), uint64_t(m),
-                             uint64_t(ldo), uint32_t(plan.bn)))
+                             uint64_t(ldo), uint32_t(plan.bn),
+                             uint32_t(128 / plan.splits)))
       return r;
   }
 
@@ -539,13 +569,15 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
 // Plan introspection for tests and the benchmark (not part of the public
 // header's contract; exported for diagnostics).
 int pir2b_gemm_plan(int bits, int64_t m, int64_t npad, int64_t kpad,
-                    int sms, int *bn, int *mtiles, int *splits, int *stages) {
+                    int sms, int *bn, int *mtiles, int *splits, int *stages,
+                    int64_t *smem) {
   const GemmPlan p = plan_gemm(bits, m, npad, kpad, sms, 232448);
   *bn = p.bn;
   *mtiles = p.mtiles;
   *splits = p.splits;
   *stages = p.stages;
-  return PIR2B_OK;
+  *smem = int64_t(p.smem);
+  return p.smem == 0 ? fail(PIR2B_EINVAL, "no GEMM tile plan") : PIR2B_OK;
 }
 
 } // extern "C"

@@ -115,7 +115,7 @@ __device__ __forceinline__ void unpack_int4_stage(const uint8_t *src,
 // the previous kernel, overlap its tail; activation tiles and scales are
 // read only after griddepcontrol.wait.
 template <int kBits>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_a,
                    const __grid_constant__ CUtensorMap tm_out,
@@ -289,39 +289,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Staging tile [bn tokens][128 channels] bf16 in the idle stage
         // buffers, written out by one TMA store.
         __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem);
-        for (int j0 = 0; j0 < bn; j0 += 32) {
-          uint32_t r[32];
-          if (j0 + 32 <= bn) {
-            tmem_ld_32(lane_addr + j0, r);
-          } else {
-            uint32_t h[16];
-            tmem_ld_16(lane_addr + j0, h);
+        const int bias_mode = args.bias_mode;
+        const bool tma = args.tma_store != 0;
+        const bool with_res = args.residual != nullptr;
+        for (int j0 = 0; j0 < bn; j0 += 16) {
+          // 16 token columns per step: bn is a multiple of 16.
+          uint32_t r[16];
+          tmem_ld_16(lane_addr + j0, r);
+          float res[16];
+          if (with_res) {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              r[i] = h[i];
+              res[i] = (in_range && j0 + i < valid_m)
+                           ? __bfloat162float(args.residual[int64_t(m0 + j0 + i) * args.ldr + c])
+                           : 0.f;
           }
-          const int cnt = min(32, bn - j0);
-          // Residual values of this chunk, all loads in flight together.
-          float res[32];
-          const bool with_res = args.residual != nullptr && in_range;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            res[i] = (with_res && j0 + i < valid_m)
-                         ? __bfloat162float(args.residual[int64_t(m0 + j0 + i) * args.ldr + c])
-                         : 0.f;
           tmem_ld_wait();
+          __nv_bfloat16 o[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (i >= cnt)
-              break;
-            __nv_bfloat16 o = epilogue_value(int(r[i]), s_sa[j0 + i], sw, b,
-                                             args.bias_mode, lut);
-            if (with_res && j0 + i < valid_m)
-              o = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o), res[i]));
-            if (args.tma_store)
-              stage[(j0 + i) * kTileN + ch] = o;
-            else if (in_range && j0 + i < valid_m)
-              args.out[int64_t(m0 + j0 + i) * args.ldo + c] = o;
+          for (int i = 0; i < 16; ++i)
+            o[i] = epilogue_value(int(r[i]), s_sa[j0 + i], sw, b, bias_mode, lut);
+          if (with_res) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              o[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o[i]), res[i]));
+          }
+          if (tma) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              stage[(j0 + i) * kTileN + ch] = o[i];
+          } else if (in_range) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (j0 + i < valid_m)
+                args.out[int64_t(m0 + j0 + i) * args.ldo + c] = o[i];
           }
         }
         if (args.tma_store) {
@@ -352,39 +353,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every thread of every CTA in the cluster takes part in both barriers.
     cluster_sync();
     if (warp >= 2) {
+      // Rank r reduces and writes channels [r*slice, (r+1)*slice) of the
+      // tile: each thread owns one channel (scale and bias loaded once) and
+      // walks the tokens; lanes read consecutive channels of every peer's
+      // partial tile through distributed shared memory.
       const int et = threadIdx.x - 64;
       const uint32_t rank = cluster_ctarank();
-      const int slice = kTileN / args.splits;        // channels per rank
-      const int quads = slice / 4;
+      const int splits = args.splits;
+      const int slice = kTileN / splits;              // 64, 32 or 16 channels
+      const int cl = et % slice;
+      const int cq = int(rank) * slice + cl;          // channel within the tile
+      const int cc = n0 + cq;
+      const int tstride = 128 / slice;
       const int valid_m = min(bn, args.m - m0);
-      const uint32_t part_addr = smem_u32(smem);
+      const bool in_range = cc < args.n_store;
+      const float sw = in_range ? __ldg(args.sw + cc) : 0.f;
+      const float b = (args.bias_mode == 2 && in_range) ? __bfloat162float(args.bias[cc]) : 0.f;
       const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
-      for (int idx = et; idx < valid_m * quads; idx += 128) {
-        const int j = idx / quads;
-        const int cq = rank * slice + (idx % quads) * 4;
-        int4 acc = make_int4(0, 0, 0, 0);
-        const uint32_t off = part_addr + uint32_t((j * kTileN + cq) * 4);
-        for (int p = 0; p < args.splits; ++p) {
-          const int4 v = ld_cluster_v4(map_peer(off, uint32_t(p)));
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
-        }
-        const float sa = s_sa[j];
-        const int accs[4] = {acc.x, acc.y, acc.z, acc.w};
+      const uint32_t part_addr = smem_u32(smem);
+      uint32_t peer_base[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int cc = n0 + cq + e;
-          if (cc < args.n_store) {
-            const float b = args.bias_mode == 2
-                                ? __bfloat162float(args.bias[cc])
-                                : 0.f;
-            args.out[int64_t(m0 + j) * args.ldo + cc] = add_residual(
-                epilogue_value(accs[e], sa, __ldg(args.sw + cc), b,
-                               args.bias_mode, lut),
-                args, m0 + j, cc);
-          }
+      for (int p = 0; p < 8; ++p)
+        peer_base[p] = p < splits ? map_peer(part_addr, uint32_t(p)) : 0u;
+      // Staging tile [bn][slice] bf16 after the partial sums.
+      __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem + size_t(bn) * kTileN * 4);
+      const bool tma = args.tma_store != 0;
+      for (int j = et / slice; j < (tma ? bn : valid_m); j += tstride) {
+        const uint32_t off = uint32_t((j * kTileN + cq) * 4);
+        int acc = 0;
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          if (p < splits)
+            acc += ld_cluster_s32(peer_base[p] + off);
+        __nv_bfloat16 o = epilogue_value(acc, s_sa[j], sw, b, args.bias_mode, lut);
+        if (args.residual != nullptr && in_range && j < valid_m)
+          o = add_residual(o, args, m0 + j, cc);
+        if (tma)
+          stage[j * slice + cl] = o;
+        else if (in_range)
+          args.out[int64_t(m0 + j) * args.ldo + cc] = o;
+      }
+      if (tma) {
+        fence_proxy_async_smem();
+        named_barrier(1, 128);
+        if (et == 0) {
+          tma_store_2d(&tm_out, stage, n0 + int(rank) * slice, m0);
+          tma_store_commit_and_wait();
         }
       }
     }
