@@ -49,7 +49,7 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--precision", choices=["w8a8", "w4a4"], default="w8a8")
+    p.add_argument("--precision", choices=["w8a8", "w4a4", "fp4"], default="w8a8")
     p.add_argument("--batch", type=int, default=1, help="robots per GPU")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--cpu-sample-seconds", type=float, default=20.0)
@@ -261,6 +261,7 @@ def cpu_oracle_step(args, budget_s):
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
+    fp4 = args.precision == "fp4"
     bits = 8 if args.precision == "w8a8" else 4
     vlm = harness.VLMConfig(layers=1, vocab=2048)
     dit = harness.DiTConfig(layers=2)
@@ -270,7 +271,22 @@ def cpu_oracle_step(args, budget_s):
         return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)
 
     for module in policy.modules():
-        if isinstance(module, torch.nn.Linear):
+        if isinstance(module, torch.nn.Linear) and fp4:
+            if module.in_features % 256 or module.out_features % 32:
+                continue  # stays bf16, as in the GPU path
+            pw, sw4 = oracle.pack_nvfp4(module.weight.detach().float().numpy())
+            bias4 = None if module.bias is None else bits_of(module.bias)
+            n4, k4 = module.out_features, module.in_features
+
+            def forward4(x, pw=pw, sw4=sw4, bias4=bias4, n4=n4, k4=k4):
+                lead = x.shape[:-1]
+                rows = x.reshape(-1, k4).float().numpy()
+                pa, sa = oracle.pack_nvfp4(rows)
+                y = oracle.nvfp4_gemm(pa, sa, pw, sw4, rows.shape[0], n4, k4, bias4)
+                return torch.from_numpy(np.ascontiguousarray(y).view(np.int16)).view(torch.bfloat16).reshape(*lead, n4)
+
+            module.forward = forward4
+        elif isinstance(module, torch.nn.Linear):
             w = module.weight.detach().float().numpy()
             qw, sw = oracle.quantize_weight(w, bits)
             uw = oracle.unpack_int4(qw) if bits == 4 else qw
@@ -331,7 +347,7 @@ def run_reference(args, world, rank):
         "higher_is_better": False,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "int8" if args.precision == "w8a8" else "int4",
+        "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1"}[args.precision],
         "data": "synthetic",
         "config": {
             "workload": f"GR00T-shaped control step, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
@@ -353,14 +369,17 @@ def build_engine(args, local):
 
     device = torch.device("cuda", local)
     policy = harness.build_policy(device)
-    config = OptimizationConfig(
-        precision=args.precision,
-        fusion=True,
-        scope="all",
-        group_conditioning=True,
-        norm_modulation_quant=True,
-        residual_norm_quant=True,
-    )
+    if args.precision == "fp4":
+        config = OptimizationConfig(precision="fp4", scope="all")
+    else:
+        config = OptimizationConfig(
+            precision=args.precision,
+            fusion=True,
+            scope="all",
+            group_conditioning=True,
+            norm_modulation_quant=True,
+            residual_norm_quant=True,
+        )
     session = GrootOptimizations(SimpleNamespace(model=policy), config)
     session.__enter__()
     engine = ControlStep(policy, args.batch, device=device, graph=not args.no_graph)
@@ -438,7 +457,7 @@ def run_ours(args, world, rank, local):
             "higher_is_better": False,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "int8" if args.precision == "w8a8" else "int4",
+            "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1"}[args.precision],
             "data": "synthetic",
             "config": {
                 "workload": f"GR00T-shaped control step per GPU, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",

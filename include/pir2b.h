@@ -148,7 +148,9 @@ int pir2b_pack_nvfp4(const void *x, int64_t rows, int64_t k, void *packed,
  * Replaces linear_forward_packed_gemm_bf16_tactic
  *   coexecution/kernels/blackwell/csrc/fp4_cutlass_linear.cu:1751-1847.
  * qa [m, k/2] + sfa (swizzled, rows padded to 128); qw [n, k/2] + sfw;
- * bias bf16 [n] or NULL; out bf16 [m, ldo]. k % 64 == 0, n % 32 == 0. */
+ * bias bf16 [n] or NULL; out bf16 [m, ldo]; out = bf16(alpha * acc + bias).
+ * k % 256 == 0 (one K block = 256 values + 16 factors per row; piR2 accepts
+ * k % 32 == 0), operands 16-byte aligned. */
 int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
                      const void *sfw, const void *bias, float alpha,
                      int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,

@@ -85,6 +85,10 @@ static int device_info(DeviceInfo **out) {
       e = cudaFuncSetAttribute(gemm_i8_kernel<4>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                d.max_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp4_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               d.max_smem);
     if (e != cudaSuccess)
       return cuda_status(e, "cudaFuncSetAttribute");
     d.attrs_set = true;
@@ -561,9 +565,75 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
                      const void *sfw, const void *bias, float alpha,
                      int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,
                      void *stream) {
-  (void)qa; (void)sfa; (void)qw; (void)sfw; (void)bias; (void)alpha;
-  (void)m; (void)n; (void)k; (void)out; (void)ldo; (void)stream;
-  return fail(PIR2B_EINVAL, "pir2b_gemm_nvfp4: NVFP4 GEMM kernel not built");
+  if (m < 1 || n < 1 || m > 0x7fffffffLL || n > 0x7fffffffLL)
+    return fail(PIR2B_EINVAL, "NVFP4 GEMM needs m >= 1 and n >= 1");
+  if (k < 256 || k % 256 != 0 || k > (1LL << 20))
+    return fail(PIR2B_EINVAL,
+                "NVFP4 GEMM needs k %% 256 == 0 (k=%lld): one K block is 256 "
+                "E2M1 values with 16 UE4M3 factors per row",
+                (long long)k);
+  if (ldo < n)
+    return fail(PIR2B_EINVAL, "ldo must be >= n");
+  if (qa == nullptr || sfa == nullptr || qw == nullptr || sfw == nullptr ||
+      out == nullptr)
+    return fail(PIR2B_EINVAL, "NVFP4 GEMM operands must be non-null");
+  const void *p16[] = {qa, sfa, qw, sfw};
+  for (const void *p : p16)
+    if (!aligned(p, 16))
+      return fail(PIR2B_EALIGN, "NVFP4 operands and factors must be 16-byte aligned");
+  if (!aligned(out, 2) || (bias && !aligned(bias, 2)))
+    return fail(PIR2B_EALIGN, "output/bias alignment not met");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  // Token tiles start on 128-row factor atoms: one tile of <= 128 tokens, or
+  // tiles of 128.
+  const int bn = m <= 128 ? int((m + 15) / 16 * 16) : 128;
+  const int mtiles = int((m + 127) / 128);
+  const size_t stage = size_t(kFp4WeightTile) + size_t(bn) * kFp4BlockBytes + 2 * kSfStageBytes;
+  int stages = 8;
+  auto smem_of = [&](int s) { return 1024 + s * stage + (2 * s + 1) * 8 + 16; };
+  while (stages > 2 && smem_of(stages) > size_t(dev->max_smem))
+    --stages;
+  const uint64_t row_bytes = uint64_t(k / 2);
+  CUtensorMap tm_w, tm_a, tm_out;
+  memset(&tm_out, 0, sizeof(tm_out));
+  if (int r = make_map(&tm_w, qw, row_bytes, uint64_t(n), row_bytes, 128u, 128u, true))
+    return r;
+  if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, 128u, uint32_t(bn), true))
+    return r;
+  Fp4GemmArgs args;
+  args.sfw = static_cast<const uint8_t *>(sfw);
+  args.sfa = static_cast<const uint8_t *>(sfa);
+  args.bias = static_cast<const __nv_bfloat16 *>(bias);
+  args.out = static_cast<__nv_bfloat16 *>(out);
+  args.ldo = ldo;
+  args.m = int(m);
+  args.n = int(n);
+  args.num_kb = int(k / 256);
+  args.blocks_k = int((k / 16 + 3) / 4);
+  args.bn = bn;
+  args.stages = stages;
+  args.alpha = alpha;
+  args.tma_store = (ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  if (args.tma_store) {
+    if (int r = make_out_map(&tm_out, out, uint64_t(n), uint64_t(m), uint64_t(ldo),
+                             uint32_t(bn), 128u))
+      return r;
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(unsigned((n + 127) / 128), unsigned(mtiles), 1);
+  cfg.blockDim = dim3(kFp4Threads, 1, 1);
+  cfg.dynamicSmemBytes = smem_of(stages);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, gemm_fp4_kernel, tm_w, tm_a, tm_out, args),
+                     "gemm_nvfp4 launch");
 }
 
 // Plan introspection for tests and the benchmark (not part of the public

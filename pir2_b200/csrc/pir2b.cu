@@ -2,5 +2,6 @@
 // one definition of the device status word without relocatable device code.
 #include "quant.cuh"
 #include "gemm_i8.cuh"
+#include "gemm_fp4.cuh"
 #include "pointwise.cuh"
 #include "capi.cuh"

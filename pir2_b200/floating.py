@@ -1,0 +1,216 @@
+"""NVFP4 Linear layers and producers on the B200 kernels.
+
+Mirrors the FP4 half of coexecution/optimization/backends/thor/linear.py
+(`FloatingLinear`, :30-190) and packing.py (`FloatingPacked`, the fused
+norm/smoothing producers, :15-448): weights are packed once as E2M1 with
+UE4M3 factors per 16 elements (the CUTLASS 128x4 swizzled factor layout,
+`sfa_offset`), activations are packed per call (optionally fused with
+LayerNorm / RMSNorm / AdaLN / residual / SmoothQuant division), and the GEMM
+runs on tcgen05 kind::mxf4nvf4 with fp32 accumulation and bf16 output.
+
+This build supports precision "fp4"; FP8 is not part of it.  A K block of
+the B200 kernel is 256 values, so in_features must be a multiple of 256
+(piR2 requires 32); out_features must be a multiple of 32 as in piR2.
+"""
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, ops
+
+
+@dataclass
+class FloatingPacked:
+    data: torch.Tensor
+    scale: torch.Tensor
+    shape: tuple
+    precision: str
+    smoothing_scale: torch.Tensor | None = None
+
+
+def _check_smoothing_metadata(scale, value):
+    if scale is not None and (
+        scale.shape != (value.shape[-1],)
+        or scale.dtype != torch.float32
+        or scale.device != value.device
+        or not scale.is_contiguous()
+        or scale.requires_grad
+    ):
+        raise ValueError("SmoothQuant requires contiguous immutable FP32 channel scales")
+
+
+def _require_fp4(precision):
+    if precision != "fp4":
+        raise ValueError("This B200 build implements the fp4 floating precision only")
+
+
+def _producer_rows(x):
+    if not x.is_cuda or x.dtype != torch.bfloat16 or x.numel() == 0 or x.requires_grad:
+        raise ValueError("Floating producer requires nonempty CUDA BF16 inference")
+    k = x.shape[-1]
+    if k % 32 or k > 8192:
+        raise ValueError("Floating producer requires K % 32 == 0 and K <= 8192")
+    return x.reshape(-1, k).contiguous(), k
+
+
+def prepare_smoothed(matrix, precision, smoothing_scale):
+    """bf16(x / s) fused into the FP4 pack (packing.py:314-349)."""
+    _require_fp4(precision)
+    _check_smoothing_metadata(smoothing_scale, matrix)
+    if smoothing_scale is None or matrix.ndim != 2 or not matrix.is_contiguous():
+        raise ValueError("Smoothed packing needs a contiguous matrix and channel scales")
+    rows, _ = _producer_rows(matrix)
+    data, scale, _ = ops.norm_quant_rows(rows, _lib.OUT_NVFP4, smooth=smoothing_scale)
+    return FloatingPacked(data, scale, tuple(matrix.shape), precision, smoothing_scale)
+
+
+def prepare_rmsnorm_packed(x, weight, precision, *, eps, smoothing_scale=None):
+    """RMSNorm [+ SmoothQuant] to FP4 (packing.py:395-448)."""
+    _require_fp4(precision)
+    _check_smoothing_metadata(smoothing_scale, x)
+    if not x.is_contiguous() or weight.shape != (x.shape[-1],) or not math.isfinite(eps) or eps <= 0:
+        raise ValueError("RMSNorm packing requires contiguous BF16 and positive epsilon")
+    rows, _ = _producer_rows(x)
+    data, scale, _ = ops.norm_quant_rows(
+        rows, _lib.OUT_NVFP4, norm=_lib.NORM_RMS, eps=eps, gamma=weight, smooth=smoothing_scale
+    )
+    return FloatingPacked(data, scale, tuple(x.shape), precision, smoothing_scale)
+
+
+def prepare_norm(x, precision, *, eps, scale=None, shift=None, residual=None, smoothing_scale=None):
+    """LayerNorm [+ AdaLN] [+ residual] [+ SmoothQuant] to FP4
+    (packing.py:234-297).  Returns (packed, bf16 residual sum or None)."""
+    _require_fp4(precision)
+    _check_smoothing_metadata(smoothing_scale, x)
+    if x.ndim != 3 or not x.is_contiguous() or not math.isfinite(eps) or eps <= 0:
+        raise ValueError("Norm packing requires contiguous B,T,D and positive epsilon")
+    if (scale is None) != (shift is None):
+        raise ValueError("Modulation requires both scale and shift")
+    b, t, k = x.shape
+    tokens = 1
+    if scale is not None:
+        if scale.shape != shift.shape or scale.shape not in (x.shape, (b, k)):
+            raise ValueError("Modulation must match BF16 B,D or per-token B,T,D")
+        tokens = t if scale.ndim == 2 else 1
+        scale, shift = scale.reshape(-1, k).contiguous(), shift.reshape(-1, k).contiguous()
+    y = None
+    if residual is not None:
+        if residual.shape != x.shape or not residual.is_contiguous():
+            raise ValueError("Residual must match contiguous BF16 input")
+        y = residual.reshape(-1, k)
+    rows, _ = _producer_rows(x)
+    data, sf, summed = ops.norm_quant_rows(
+        rows, _lib.OUT_NVFP4, norm=_lib.NORM_LN, eps=eps, scale=scale, shift=shift, tokens=tokens,
+        y=y, smooth=smoothing_scale,
+    )
+    packed = FloatingPacked(data, sf, tuple(x.shape), precision, smoothing_scale)
+    return packed, (None if summed is None else summed.reshape(x.shape))
+
+
+class FloatingLinear(torch.nn.Module):
+    """Block-scaled E2M1 GEMM with packed weights (thor/linear.py:30-190)."""
+
+    def __init__(self, linear, name, precision="fp4", *, fast_fp8=False, fp4_swap_ab=False, smoothing_scale=None):
+        super().__init__()
+        _require_fp4(precision)
+        if fast_fp8:
+            raise ValueError("Fast FP8 quantization requires precision=fp8")
+        if (
+            not linear.weight.is_cuda
+            or linear.weight.dtype != torch.bfloat16
+            or linear.in_features % 256
+            or linear.out_features % 32
+        ):
+            raise ValueError("fp4 requires CUDA BF16 weights, in_features % 256 == 0 and out_features % 32 == 0")
+        if torch.cuda.get_device_capability(linear.weight.device) != (10, 0):
+            raise ValueError("The B200 FP4 adapter runs on sm_100 devices")
+        self.name = name
+        self.precision = precision
+        self.fp4_swap_ab = fp4_swap_ab   # the tcgen05 kernel has no separate swap-AB variant
+        self.in_features = linear.in_features
+        self.out_features = linear.out_features
+        weight_input = linear.weight.detach().contiguous()
+        if smoothing_scale is not None:
+            _check_smoothing_metadata(smoothing_scale, weight_input)
+            if not torch.isfinite(smoothing_scale).all() or not (smoothing_scale > 0).all():
+                raise ValueError("SmoothQuant scales must be finite and positive")
+            weight_input = (weight_input.float() * smoothing_scale).to(torch.bfloat16)
+            if not torch.isfinite(weight_input).all():
+                raise ValueError("SmoothQuant overflowed BF16 weights")
+        self.register_buffer("smoothing_scale", smoothing_scale)
+        packed, scale = ops.pack_nvfp4(weight_input)
+        self.register_buffer("packed_weight", packed)
+        self.register_buffer("weight_scale", scale)
+        self.register_buffer(
+            "metadata", torch.tensor([self.out_features, self.in_features], dtype=torch.int64)
+        )
+        self.register_buffer("bias", None if linear.bias is None else linear.bias.detach())
+
+    def pack_input(self, value):
+        if isinstance(value, FloatingPacked):
+            if (
+                value.precision != self.precision
+                or value.shape[-1] != self.in_features
+                or value.data.device != self.packed_weight.device
+                or value.smoothing_scale is not self.smoothing_scale
+            ):
+                raise ValueError("Floating packed input does not match its consumer")
+            return value.data, value.scale
+        if (
+            value.dtype != torch.bfloat16
+            or value.device != self.packed_weight.device
+            or value.ndim < 1
+            or value.shape[-1] != self.in_features
+            or value.numel() == 0
+            or value.requires_grad
+        ):
+            raise ValueError("Floating quantization requires nonempty CUDA BF16 inference activations")
+        matrix = value.reshape(-1, self.in_features).contiguous()
+        if self.smoothing_scale is not None:
+            packed = prepare_smoothed(matrix, self.precision, self.smoothing_scale)
+            return packed.data, packed.scale
+        return ops.pack_nvfp4(matrix)
+
+    def forward_packed(self, packed, scale, leading_shape):
+        result = ops.gemm_nvfp4(packed, scale, self.packed_weight, self.weight_scale, self.bias, n=self.out_features)
+        return result.reshape(*leading_shape, self.out_features)
+
+    def forward(self, value):
+        packed, scale = self.pack_input(value)
+        shape = value.shape[:-1] if not isinstance(value, FloatingPacked) else value.shape[:-1]
+        return self.forward_packed(packed, scale, shape)
+
+
+class FloatingProjections:
+    """Reversible installation of FloatingLinear on the executed sites that
+    meet the FP4 alignment (others stay bf16, as piR2's alignment checks
+    exclude them)."""
+
+    def __init__(self, model, executed, *, smoothing=None):
+        self.sites = {}
+        self.skipped = []
+        modules = dict(model.named_modules())
+        for name in executed:
+            module = modules[name]
+            if module.in_features % 256 or module.out_features % 32:
+                self.skipped.append(name)
+                continue
+            scale = None if smoothing is None else smoothing.get(name)
+            self.sites[name] = (module, FloatingLinear(module, name, "fp4", smoothing_scale=scale))
+        self.saved = []
+
+    def set(self):
+        self.close()
+        for module, linear in self.sites.values():
+            self.saved.append((module, "forward" in module.__dict__, module.__dict__.get("forward")))
+            module.forward = linear.forward
+
+    def close(self):
+        for module, had, forward in self.saved:
+            if had:
+                module.forward = forward
+            elif "forward" in module.__dict__:
+                del module.forward
+        self.saved = []

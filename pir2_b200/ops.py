@@ -207,3 +207,23 @@ def qk_norm_rope(qkv, q_weight, k_weight, cos, sin, *, tokens, hq, hk, eps, head
     )
     _lib.check(status, "pir2b_qk_norm_rope")
     return q, k, v
+
+
+def gemm_nvfp4(a_packed, a_sf, w_packed, w_sf, bias=None, *, n, alpha=1.0, out=None):
+    """NVFP4 GEMM: bf16(alpha * sum (a * sfa)(w * sfw) [+ bias]) -> [m, n].
+
+    a_packed: uint8 [m, k/2], a_sf: swizzled UE4M3 factors (rows padded to
+    128); w_packed: uint8 [n, k/2], w_sf likewise (the layouts of pack_nvfp4).
+    """
+    m = a_packed.shape[0]
+    k = a_packed.shape[1] * 2
+    if w_packed.shape[1] * 2 != k or w_packed.shape[0] < n:
+        raise ValueError("NVFP4 operand shapes do not match")
+    if out is None:
+        out = torch.empty((m, n), device=a_packed.device, dtype=torch.bfloat16)
+    status = _lib.lib().pir2b_gemm_nvfp4(
+        a_packed.data_ptr(), a_sf.data_ptr(), w_packed.data_ptr(), w_sf.data_ptr(), _ptr(bias),
+        float(alpha), m, n, k, out.data_ptr(), out.stride(0), _stream(a_packed.device),
+    )
+    _lib.check(status, "pir2b_gemm_nvfp4")
+    return out
