@@ -254,59 +254,16 @@ def cpu_oracle_step(args, budget_s):
     bounded sample: one VLM decoder layer (544 tokens) and a two-block DiT
     (one cross-, one self-attention block) through the 4 Euler steps, scaled
     to 16 layers / 16 blocks.  Returns (ms_per_step, cores, sample text)."""
-    import numpy as np
-
-    import oracle
+    from oracle.model import install_oracle_linears
     from pir2_b200 import harness
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    fp4 = args.precision == "fp4"
-    bits = 8 if args.precision == "w8a8" else 4
     vlm = harness.VLMConfig(layers=1, vocab=2048)
     dit = harness.DiTConfig(layers=2)
     policy = harness.build_policy("cpu", vlm=vlm, dit=dit)
 
-    def bits_of(t):
-        return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)
-
-    for module in policy.modules():
-        if isinstance(module, torch.nn.Linear) and fp4:
-            if module.in_features % 256 or module.out_features % 32:
-                continue  # stays bf16, as in the GPU path
-            pw, sw4 = oracle.pack_nvfp4(module.weight.detach().float().numpy())
-            bias4 = None if module.bias is None else bits_of(module.bias)
-            n4, k4 = module.out_features, module.in_features
-
-            def forward4(x, pw=pw, sw4=sw4, bias4=bias4, n4=n4, k4=k4):
-                lead = x.shape[:-1]
-                rows = x.reshape(-1, k4).float().numpy()
-                pa, sa = oracle.pack_nvfp4(rows)
-                y = oracle.nvfp4_gemm(pa, sa, pw, sw4, rows.shape[0], n4, k4, bias4)
-                return torch.from_numpy(np.ascontiguousarray(y).view(np.int16)).view(torch.bfloat16).reshape(*lead, n4)
-
-            module.forward = forward4
-        elif isinstance(module, torch.nn.Linear):
-            w = module.weight.detach().float().numpy()
-            qw, sw = oracle.quantize_weight(w, bits)
-            uw = oracle.unpack_int4(qw) if bits == 4 else qw
-            bias = None if module.bias is None else bits_of(module.bias)
-            n = w.shape[0]
-
-            def forward(x, uw=uw, sw=sw, bias=bias, n=n):
-                lead = x.shape[:-1]
-                rows = bits_of(x.reshape(-1, x.shape[-1]))
-                qa, sa = oracle.quant_rows(rows, bits)
-                ua = oracle.unpack_int4(qa) if bits == 4 else qa
-                acc = oracle.int_matmul(ua, uw)
-                full = None
-                if bias is not None:
-                    full = np.zeros(uw.shape[0], dtype=np.uint16)
-                    full[:n] = bias
-                y = oracle.gemm_epilogue(acc, sa, sw, full, 2 if bias is not None else 1)[:, :n]
-                return torch.from_numpy(np.ascontiguousarray(y).view(np.int16)).view(torch.bfloat16).reshape(*lead, n)
-
-            module.forward = forward
+    install_oracle_linears(policy, args.precision)
     visual, ids, state, noise = harness.synthetic_inputs(args.batch, "cpu", vlm=vlm, dit=dit)
     layer = policy.backbone.layers[0]
     with torch.inference_mode():
@@ -326,7 +283,7 @@ def cpu_oracle_step(args, budget_s):
     full_ms = 1e3 * (16 * t_vlm / reps + 8 * t_dit / reps)
     sample = (
         f"{reps} x (1 VLM layer over 544 tokens + 2-block DiT x 4 Euler steps), batch {args.batch}, "
-        "oracle W8A8 linears + torch CPU norms/attention, scaled x16 VLM layers / x8 DiT block pairs"
+        f"oracle {args.precision.upper()} linears + torch CPU norms/attention, scaled x16 VLM layers / x8 DiT block pairs"
     )
     return full_ms, cores, sample
 
@@ -517,13 +474,22 @@ def phase_breakdown(engine, reps=50):
 
 
 def count_launches(engine):
-    """Counts this library's kernel launches in one step (quant/pack, norm
-    producers and GEMMs), by wrapping the C-ABI entry points for one eager
-    step."""
+    """Counts this library's kernel launches in one step (packs, norm
+    producers, GEMMs, attention, q/k norm + RoPE, NVFP4), by wrapping the
+    C-ABI entry points for one eager step (each launches one kernel for the
+    shapes of the step)."""
     from pir2_b200 import _lib
 
     lib = _lib.lib()
-    names = ["pir2b_quant_rows", "pir2b_norm_quant_rows", "pir2b_gemm"]
+    names = [
+        "pir2b_quant_rows",
+        "pir2b_norm_quant_rows",
+        "pir2b_gemm",
+        "pir2b_qk_norm_rope",
+        "pir2b_attention_rows",
+        "pir2b_pack_nvfp4",
+        "pir2b_gemm_nvfp4",
+    ]
     counts = {n: 0 for n in names}
     originals = {n: getattr(lib, n) for n in names}
 

@@ -89,6 +89,10 @@ static int device_info(DeviceInfo **out) {
       e = cudaFuncSetAttribute(gemm_fp4_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                d.max_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_rows_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               d.max_smem);
     if (e != cudaSuccess)
       return cuda_status(e, "cudaFuncSetAttribute");
     d.attrs_set = true;
@@ -559,6 +563,48 @@ int pir2b_qk_norm_rope(const void *qkv, int64_t ld, const void *q_weight,
   a.eps = eps;
   return cuda_status(run_qk_norm_rope(a, rows, static_cast<cudaStream_t>(stream)),
                      "qk_norm_rope launch");
+}
+
+int pir2b_attention_rows(const void *q, int64_t ldq, const void *k,
+                         int64_t ldk, const void *v, int64_t ldv, void *out,
+                         int64_t ldo, int64_t batch, int64_t tq, int64_t skv,
+                         int heads, int head_dim, float scale, void *stream) {
+  if (batch < 1 || tq < 1 || skv < 1 || heads < 1 || head_dim < 8 ||
+      head_dim > 128 || head_dim % 8 != 0 || skv > (int64_t(1) << 20) ||
+      tq > (int64_t(1) << 30) || batch > 65535 || heads > 65535)
+    return fail(PIR2B_EINVAL,
+                "attention_rows: need batch, T, S >= 1 and head_dim %% 8 == 0, <= 128");
+  const int64_t width = int64_t(heads) * head_dim;
+  if (ldq < width || ldk < width || ldv < width || ldo < width ||
+      ldk % 8 != 0 || ldv % 8 != 0)
+    return fail(PIR2B_EINVAL, "attention_rows: row strides too small or K/V strides not %% 8");
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(PIR2B_EINVAL, "attention_rows operands must be non-null");
+  if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 2) || !aligned(out, 2))
+    return fail(PIR2B_EALIGN, "attention_rows: K/V must be 16-byte aligned");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  const int chunks = attention_chunks(int(skv));
+  const int chunk = int((skv + chunks - 1) / chunks);
+  if (attention_smem(chunk, head_dim, chunks) > size_t(dev->max_smem))
+    return fail(PIR2B_EINVAL, "attention_rows: S too long for shared memory");
+  AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16 *>(q);
+  a.ldq = ldq;
+  a.k = static_cast<const __nv_bfloat16 *>(k);
+  a.ldk = ldk;
+  a.v = static_cast<const __nv_bfloat16 *>(v);
+  a.ldv = ldv;
+  a.out = static_cast<__nv_bfloat16 *>(out);
+  a.ldo = ldo;
+  a.T = int(tq);
+  a.S = int(skv);
+  a.H = heads;
+  a.D = head_dim;
+  a.scale = scale;
+  return cuda_status(run_attention_rows(a, int(batch), static_cast<cudaStream_t>(stream)),
+                     "attention_rows launch");
 }
 
 int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,

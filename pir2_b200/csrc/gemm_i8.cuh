@@ -354,23 +354,29 @@ __global__ void __launch_bounds__(kThreads, 2)
     cluster_sync();
     if (warp >= 2) {
       // Rank r reduces and writes channels [r*slice, (r+1)*slice) of the
-      // tile: each thread owns one channel (scale and bias loaded once) and
-      // walks the tokens; lanes read consecutive channels of every peer's
-      // partial tile through distributed shared memory.
+      // tile.  Each thread owns four consecutive channels (scales and bias
+      // loaded once) and walks the tokens; one 16-byte distributed-shared-
+      // memory load per peer and token fetches the four partial sums.
       const int et = threadIdx.x - 64;
       const uint32_t rank = cluster_ctarank();
       const int splits = args.splits;
       const int slice = kTileN / splits;              // 64, 32 or 16 channels
-      const int cl = et % slice;
-      const int cq = int(rank) * slice + cl;          // channel within the tile
+      const int tpt = slice / 4;                      // threads per token
+      const int cl = (et % tpt) * 4;
+      const int cq = int(rank) * slice + cl;          // first channel in the tile
       const int cc = n0 + cq;
-      const int tstride = 128 / slice;
+      const int tstride = 128 / tpt;
       const int valid_m = min(bn, args.m - m0);
-      const bool in_range = cc < args.n_store;
-      const float sw = in_range ? __ldg(args.sw + cc) : 0.f;
-      const float b = (args.bias_mode == 2 && in_range) ? __bfloat162float(args.bias[cc]) : 0.f;
+      float sw[4], b[4];
+      bool in_range[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        in_range[i] = cc + i < args.n_store;
+        sw[i] = in_range[i] ? __ldg(args.sw + cc + i) : 0.f;
+        b[i] = (args.bias_mode == 2 && in_range[i]) ? __bfloat162float(args.bias[cc + i]) : 0.f;
+      }
       const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
-      const uint32_t part_addr = smem_u32(smem);
+      const uint32_t part_addr = smem_u32(smem) + uint32_t(cq * 4);
       uint32_t peer_base[8];
 #pragma unroll
       for (int p = 0; p < 8; ++p)
@@ -378,20 +384,40 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Staging tile [bn][slice] bf16 after the partial sums.
       __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem + size_t(bn) * kTileN * 4);
       const bool tma = args.tma_store != 0;
-      for (int j = et / slice; j < (tma ? bn : valid_m); j += tstride) {
-        const uint32_t off = uint32_t((j * kTileN + cq) * 4);
-        int acc = 0;
+      const int jend = tma ? bn : valid_m;
+      for (int j = et / tpt; j < jend; j += tstride) {
+        const uint32_t off = uint32_t(j * kTileN * 4);
+        int4 v[8];
 #pragma unroll
         for (int p = 0; p < 8; ++p)
           if (p < splits)
-            acc += ld_cluster_s32(peer_base[p] + off);
-        __nv_bfloat16 o = epilogue_value(acc, s_sa[j], sw, b, args.bias_mode, lut);
-        if (args.residual != nullptr && in_range && j < valid_m)
-          o = add_residual(o, args, m0 + j, cc);
-        if (tma)
-          stage[j * slice + cl] = o;
-        else if (in_range)
-          args.out[int64_t(m0 + j) * args.ldo + cc] = o;
+            v[p] = ld_cluster_v4(peer_base[p] + off);
+        int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          if (p < splits) {
+            acc[0] += v[p].x;
+            acc[1] += v[p].y;
+            acc[2] += v[p].z;
+            acc[3] += v[p].w;
+          }
+        __nv_bfloat16 o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          o[i] = epilogue_value(acc[i], s_sa[j], sw[i], b[i], args.bias_mode, lut);
+          if (args.residual != nullptr && in_range[i] && j < valid_m)
+            o[i] = add_residual(o[i], args, m0 + j, cc + i);
+        }
+        if (tma) {
+          __nv_bfloat162 *d = reinterpret_cast<__nv_bfloat162 *>(stage + j * slice + cl);
+          d[0] = __halves2bfloat162(o[0], o[1]);
+          d[1] = __halves2bfloat162(o[2], o[3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (in_range[i])
+              args.out[int64_t(m0 + j) * args.ldo + cc + i] = o[i];
+        }
       }
       if (tma) {
         fence_proxy_async_smem();

@@ -4,4 +4,5 @@
 #include "gemm_i8.cuh"
 #include "gemm_fp4.cuh"
 #include "pointwise.cuh"
+#include "attention.cuh"
 #include "capi.cuh"

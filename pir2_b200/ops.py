@@ -227,3 +227,29 @@ def gemm_nvfp4(a_packed, a_sf, w_packed, w_sf, bias=None, *, n, alpha=1.0, out=N
     )
     _lib.check(status, "pir2b_gemm_nvfp4")
     return out
+
+
+def attention_rows(q, k, v, *, batch, heads, head_dim, scale=None, out=None):
+    """Unmasked attention over projection rows.
+
+    q: bf16 [batch*T, >= heads*head_dim] rows; k, v: bf16 [batch*S, ...]
+    rows (any row stride with unit column stride).  Returns bf16
+    [batch*T, heads*head_dim] rows ready for the output projection.
+    """
+    qm, qrows, _, ldq = _rows(q)
+    km, krows, _, ldk = _rows(k)
+    vm, vrows, _, ldv = _rows(v)
+    if qrows % batch or krows % batch or krows != vrows:
+        raise ValueError("attention_rows: row counts must be multiples of the batch")
+    tq, skv = qrows // batch, krows // batch
+    width = heads * head_dim
+    if out is None:
+        out = torch.empty((qrows, width), device=q.device, dtype=torch.bfloat16)
+    if scale is None:
+        scale = head_dim ** -0.5
+    status = _lib.lib().pir2b_attention_rows(
+        qm.data_ptr(), ldq, km.data_ptr(), ldk, vm.data_ptr(), ldv, out.data_ptr(), out.stride(0),
+        batch, tq, skv, heads, head_dim, float(scale), _stream(q.device),
+    )
+    _lib.check(status, "pir2b_attention_rows")
+    return out

@@ -71,3 +71,62 @@ class TextAttentionFusion:
             elif "forward" in module.__dict__:
                 del module.forward
         self.saved = []
+
+
+class DiTAttentionFusion:
+    """DiT attention on the row attention kernel.
+
+    piR2's `PreparedAttention.attend` (coexecution/groot_pointwise.py:58-92)
+    projects q, k and v, views them as [B, H, T, D], runs torch SDPA and
+    transposes the result back to [B, T, H*D] for the output projection.
+    Here the same projections feed `ops.attention_rows`, which reads the
+    projection rows in place (grouped q|k|v output, or the cached context
+    k/v) and writes [B*T, H*D] rows; masked calls keep the original forward.
+    """
+
+    def __init__(self, model):
+        self.saved = []
+        self.targets = [
+            m
+            for m in model.modules()
+            if type(m).__name__ == "Attention" and m.head_dim % 8 == 0 and m.head_dim <= 128
+        ]
+
+    @staticmethod
+    def _context_rows(kv, b):
+        # [B, H, S, D] head views of [B, S, H*D] projection rows.
+        s = kv.shape[2]
+        return kv.transpose(1, 2).reshape(b * s, kv.shape[1] * kv.shape[3])
+
+    def set(self):
+        self.close()
+        for attn in self.targets:
+            self.saved.append((attn, "forward" in attn.__dict__, attn.__dict__.get("forward")))
+            original = type(attn).forward
+
+            def forward(x, encoder_hidden_states=None, attention_mask=None, attn=attn, original=original):
+                if attention_mask is not None:
+                    return original(attn, x, encoder_hidden_states, attention_mask)
+                b, t = x.shape[0], x.shape[1]
+                width = attn.heads * attn.head_dim
+                q = attn.to_q(x)
+                if attn.is_cross_attention and attn.kv_cache is not None:
+                    k, v = (self._context_rows(z, b) for z in attn.kv_cache)
+                else:
+                    context = x if encoder_hidden_states is None else encoder_hidden_states
+                    k, v = attn.to_k(context), attn.to_v(context)
+                    k, v = k.reshape(-1, width), v.reshape(-1, width)
+                y = ops.attention_rows(
+                    q.reshape(b * t, width), k, v, batch=b, heads=attn.heads, head_dim=attn.head_dim
+                )
+                return attn.to_out[1](attn.to_out[0](y.view(b, t, width)))
+
+            attn.forward = forward
+
+    def close(self):
+        for module, had, forward in self.saved:
+            if had:
+                module.forward = forward
+            elif "forward" in module.__dict__:
+                del module.forward
+        self.saved = []

@@ -304,3 +304,53 @@ def test_gemm_residual_epilogue_bitwise():
             (oracle.bf16_bits_to_f32(y) + oracle.bf16_bits_to_f32(bits_of(residual))).astype(np.float32)
         )
         assert np.array_equal(bits_of(out), ref)
+
+
+def _sdpa_rows(q, k, v, b, heads, d):
+    """fp32 torch SDPA over [B*T, H*D] rows, result as rows."""
+    t, s = q.shape[0] // b, k.shape[0] // b
+    qh = q.float().reshape(b, t, heads, d).transpose(1, 2)
+    kh = k.float().reshape(b, s, heads, d).transpose(1, 2)
+    vh = v.float().reshape(b, s, heads, d).transpose(1, 2)
+    y = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh)
+    return y.transpose(1, 2).reshape(b * t, heads * d)
+
+
+@pytest.mark.parametrize(
+    "b,t,s,heads,d",
+    [
+        (1, 17, 17, 32, 48),      # DiT self-attention: one CTA per head
+        (1, 17, 544, 32, 48),     # DiT cross-attention: 8-CTA cluster per head
+        (2, 17, 544, 32, 48),
+        (3, 5, 33, 4, 64),
+        (1, 9, 130, 2, 128),      # 2 chunks, pitch padded
+        (1, 40, 300, 4, 48),      # query tiles of 32 across the cluster combine
+        (2, 3, 1500, 2, 40),      # odd 16-byte pitch, ragged last chunk
+    ],
+)
+def test_attention_rows_matches_fp32_sdpa(b, t, s, heads, d):
+    # Tolerance: bf16 output rounding (2^-8 relative) plus fp32 summation
+    # order; inputs are exactly representable bf16.
+    g = torch.Generator(device="cuda").manual_seed(5)
+    w = heads * d
+    q = torch.randn(b * t, w, device="cuda", generator=g).to(torch.bfloat16)
+    kv = torch.randn(b * s, 2 * w, device="cuda", generator=g).to(torch.bfloat16)
+    k, v = kv[:, :w], kv[:, w:]            # row stride 2*w, as a grouped k|v output
+    out = ops.attention_rows(q, k, v, batch=b, heads=heads, head_dim=d)
+    ref = _sdpa_rows(q, k, v, b, heads, d)
+    torch.testing.assert_close(out.float(), ref, atol=4e-3, rtol=8e-3)
+
+
+def test_attention_rows_strided_query_and_argument_errors():
+    heads, d, t = 4, 48, 7
+    w = heads * d
+    g = torch.Generator(device="cuda").manual_seed(6)
+    qkv = torch.randn(t, 3 * w, device="cuda", generator=g).to(torch.bfloat16)
+    q, k, v = qkv[:, :w], qkv[:, w:2 * w], qkv[:, 2 * w:]
+    out = ops.attention_rows(q, k, v, batch=1, heads=heads, head_dim=d)
+    torch.testing.assert_close(out.float(), _sdpa_rows(q, k, v, 1, heads, d), atol=4e-3, rtol=8e-3)
+    with pytest.raises(ValueError):
+        ops.attention_rows(q, k, v, batch=1, heads=heads, head_dim=12)   # head_dim % 8
+    long_kv = torch.zeros(20000, 2 * w, device="cuda", dtype=torch.bfloat16)   # keys exceed shared memory
+    with pytest.raises(ValueError):
+        ops.attention_rows(q, long_kv[:, :w], long_kv[:, w:], batch=1, heads=heads, head_dim=d)

@@ -90,3 +90,34 @@ def test_fp4_norm_producer_dequantizes_close_to_torch_norm(modulate, residual):
     # may move by one E2M1 step.
     assert np.mean(got == want) > 0.97
     assert np.allclose(got, want, rtol=0.34, atol=0.05)
+
+
+@torch.inference_mode()
+def test_smoothquant_profile_binds_shared_scales_into_floating_projections(tmp_path):
+    from pir2_b200 import smoothquant as sq
+    from pir2_b200.floating import FloatingLinear, FloatingProjections
+
+    torch.manual_seed(11)
+    model = torch.nn.ModuleDict(
+        {"gate": torch.nn.Linear(512, 256), "up": torch.nn.Linear(512, 256), "down": torch.nn.Linear(256, 512)}
+    ).to(device="cuda", dtype=torch.bfloat16)
+    sites = {n: (m, "Role", "text") for n, m in model.items()}
+    groups = [["gate", "up"]]
+    x = torch.randn(41, 512, device="cuda", dtype=torch.bfloat16)
+    x[:, :5] *= 20                                             # outlier channels
+    with sq.ActivationCalibration(sites, max_rows=8) as calibration:
+        h = model["gate"](x) * model["up"](x)
+        model["down"](h)
+    path = tmp_path / "profile.pt"
+    sq.write_profile(path, sites, groups, calibration, "fp4")
+    scales, evidence = sq.load_profile(path, sites, groups, "fp4")
+    assert scales["gate"] is scales["up"] and evidence["unsmoothed_linears"] == []
+    expected = FloatingLinear(model["gate"], "gate", "fp4", smoothing_scale=scales["gate"])(x)
+    original = model["gate"](x)
+    projections = FloatingProjections(model, ["gate", "up", "down"], smoothing=scales)
+    projections.set()
+    try:
+        assert torch.equal(model["gate"](x), expected)
+    finally:
+        projections.close()
+    assert torch.equal(model["gate"](x), original)

@@ -211,3 +211,30 @@ def test_graph_replay_equals_eager(bits):
     finally:
         adapter.close()
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("cross", [False, True])
+@torch.inference_mode()
+def test_dit_attention_fusion_matches_sdpa_forward_and_restores(cross):
+    from pir2_b200.harness import Attention
+    from pir2_b200.pointwise import DiTAttentionFusion
+
+    torch.manual_seed(7)
+    with torch.device("cuda"):
+        attn = Attention(1536, 32, 48, 2048 if cross else None).to(torch.bfloat16).eval()
+    x = torch.randn(2, 17, 1536, device="cuda", dtype=torch.bfloat16)
+    context = torch.randn(2, 544, 2048, device="cuda", dtype=torch.bfloat16) if cross else None
+    if cross:
+        attn.kv_cache = attn.kv(context)
+    reference = attn(x, encoder_hidden_states=context)
+    fusion = DiTAttentionFusion(torch.nn.Sequential(attn))
+    assert fusion.targets == [attn]
+    fusion.set()
+    try:
+        fused = attn(x, encoder_hidden_states=context)
+    finally:
+        fusion.close()
+    assert "forward" not in attn.__dict__
+    # Both paths run the same bf16 projections; the attention core differs
+    # only in summation order and bf16 rounding of its output.
+    torch.testing.assert_close(fused.float(), reference.float(), atol=2e-2, rtol=2e-2)

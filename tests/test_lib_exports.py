@@ -45,6 +45,11 @@ def test_argument_errors_are_reported_without_touching_the_device():
     assert status == _lib.EINVAL
     with pytest.raises(ValueError, match="npad"):
         _lib.check(status, "pir2b_gemm")
+    # head_dim % 8 != 0, then a key sequence beyond the shared-memory kernel.
+    status = lib.pir2b_attention_rows(None, 48, None, 48, None, 48, None, 48, 1, 1, 1, 4, 12, 1.0, None)
+    assert status == _lib.EINVAL and b"head_dim" in lib.pir2b_last_error()
+    status = lib.pir2b_attention_rows(None, 192, None, 192, None, 192, None, 192, 1, 1, 1 << 21, 4, 48, 1.0, None)
+    assert status == _lib.EINVAL
 
 
 def _plan(lib, bits, m, npad, kpad):
