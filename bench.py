@@ -41,6 +41,7 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # int8 dense tensor peak measured on this pool's B200 by a kind::i8 issue-rate
 # probe (8188 MAC/clk/SM x 148 SMs at the sampled clock): 4.5 POPS.
 INT8_PEAK_TOPS = 4520.0
+FP4_NOMINAL_TOPS = 9000.0
 
 
 def parse():
@@ -183,11 +184,30 @@ class GemmTimer:
 
 
 def gemm_bytes(s):
+    if s["bits"] == "fp4":
+        # E2M1 operands (half a byte per value) + one UE4M3 factor per 16.
+        return (s["n"] + s["m"]) * s["k"] * 9 // 16 + 2 * s["m"] * s["n"]
     wb = s["npad"] * s["k"] * s["bits"] // 8
     return wb + s["m"] * s["k"] * s["bits"] // 8 + 4 * s["m"] + 4 * s["npad"] + 2 * s["m"] * s["n"]
 
 
-def roofline(engine, hbm_peak, peak_kind):
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemm_i8_step_w8a8_traffic.md")
+
+
+def measured_traffic(key):
+    """DRAM bytes per launch recorded by the committed ncu capture of this
+    step (profiles/gemm_i8_step_w8a8_traffic.md), or None."""
+    try:
+        with open(TRAFFIC_PROFILE) as f:
+            for line in f:
+                if line.startswith(key + ":"):
+                    return int(line.split(":", 1)[1])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def roofline(engine, hbm_peak, peak_kind, precision):
     """Times each GEMM launch of one step (a graph captured with event nodes
     around every GEMM, replayed once warm); reports the small-M GEMMs (the
     weight-streaming launches that dominate a B=1 step) against HBM and the
@@ -226,14 +246,17 @@ def roofline(engine, hbm_peak, peak_kind):
     tops = large["ops"] / (large["t"] * 1e-3) / 1e12 if large["t"] else 0.0
     return {
         "_gemm_ms_small": small["t"],
-        "kernel": "gemm_i8_kernel<8> small-M (M<=64) launches",
+        "kernel": ("gemm_fp4_kernel" if precision == "fp4" else f"gemm_i8_kernel<{precision[1]}>")
+        + " small-M (M<=64) launches",
         "bound": "hbm",
         "achieved": round(achieved, 1),
         "peak": hbm_peak,
         "unit": "GB/s",
         "frac": round(achieved / hbm_peak, 4),
         "peak_source": f"{peak_kind} hbm_gbs",
-        "traffic": None,
+        "traffic": measured_traffic("traffic_bytes_per_launch_small_m") if precision == "w8a8" else None,
+        "traffic_unit": "DRAM bytes per launch (ncu capture of this step, profiles/gemm_i8_step_w8a8_traffic.md)",
+        "algorithmic_bytes_per_launch": round(small["bytes"] / max(small["n"], 1)),
         "launches": small["n"],
         "avg_launch_us": round(small["t"] * 1e3 / max(small["n"], 1), 2),
         "share_of_gemm_time": round(small["t"] / total, 3) if total else None,
@@ -241,9 +264,11 @@ def roofline(engine, hbm_peak, peak_kind):
             "bound": "tensor",
             "launches": large["n"],
             "achieved_tops": round(tops, 1),
-            "peak_tops": INT8_PEAK_TOPS,
-            "frac": round(tops / INT8_PEAK_TOPS, 4),
-            "peak_source": "measured int8 kind::i8 issue-rate probe",
+            "peak_tops": INT8_PEAK_TOPS if precision != "fp4" else FP4_NOMINAL_TOPS,
+            "frac": round(tops / (INT8_PEAK_TOPS if precision != "fp4" else FP4_NOMINAL_TOPS), 4),
+            "peak_source": "measured int8 kind::i8 issue-rate probe"
+            if precision != "fp4"
+            else "nominal dense FP4 (no measured FP4 peak)",
         },
     }
 
@@ -390,7 +415,7 @@ def run_ours(args, world, rank, local):
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
 
     hbm, kind = peaks()
-    roof = roofline(engine, hbm, kind)
+    roof = roofline(engine, hbm, kind, args.precision)
     status = _lib.device_status()
     roof["share_of_step"] = round(roof.pop("_gemm_ms_small", 0.0) / ms, 3) if ms else None
     cpu = None

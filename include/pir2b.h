@@ -173,9 +173,10 @@ int pir2b_qk_norm_rope(const void *qkv, int64_t ld, const void *q_weight,
  * (head h at columns h*head_dim..) and writing out[b*T + t, h*head_dim + d]
  * rows for the output projection's pack; fp32 scores and softmax, bf16 out.
  * Replaces the DiT's torch SDPA + transpose (coexecution/groot_pointwise.py:
- * 58-92) next to the quantized path.  T >= 1, head_dim % 8 == 0
- * and <= 128; S is split over a cluster of up to 8 CTAs per head, each
- * holding its keys in shared memory (S up to about 2400 at head_dim 48). */
+ * 58-92) next to the quantized path.  head_dim in {32, 48, 64, 96, 128},
+ * row strides of q/k/v multiples of 8 elements, q/k/v 16-byte aligned; S is
+ * split over a cluster of up to 8 CTAs per head, each holding its keys in
+ * shared memory (S up to about 5000 at head_dim 48). */
 int pir2b_attention_rows(const void *q, int64_t ldq, const void *k,
                          int64_t ldk, const void *v, int64_t ldv, void *out,
                          int64_t ldo, int64_t batch, int64_t tq, int64_t skv,

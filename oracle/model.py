@@ -1,4 +1,4 @@
-"""Oracle-quantized GR00T-shaped policy on the CPU (test infrastructure only).
+"""Oracle-quantized GR00T-shaped policy (test infrastructure only).
 
 Every bf16 nn.Linear of a policy gets the oracle's quantized Linear as its
 forward: for W8A8 / W4A4 the symmetric-row-v1 activation pack (quant.py
@@ -7,7 +7,8 @@ the per-channel weight quantization (`quantize_weight`, integer.py:211-256),
 the exact int32 product and the epilogue of integer_gemm.cu:37-59; for fp4
 the NVFP4 pack of both operands (thor/packing.py:24-54) and the fp64
 dequantized product.  Everything between the Linears (norms, attention,
-activations) stays plain torch on the CPU.  Linears the fp4 path cannot
+activations) stays plain torch on whatever device the policy lives on; the
+Linears compute on the host and return to that device.  Linears the fp4 path cannot
 take (K % 256 or N % 32) stay bf16, as on the GPU.
 """
 
@@ -18,15 +19,16 @@ from . import quant as oq
 
 
 def _bits_of(t):
-    return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def _from_bits(y, lead, n):
-    return torch.from_numpy(np.ascontiguousarray(y).view(np.int16)).view(torch.bfloat16).reshape(*lead, n)
+def _from_bits(y, lead, n, device):
+    t = torch.from_numpy(np.ascontiguousarray(y).view(np.int16)).view(torch.bfloat16).reshape(*lead, n)
+    return t.to(device)
 
 
 def _integer_forward(module, bits):
-    w = module.weight.detach().float().numpy()
+    w = module.weight.detach().float().cpu().numpy()
     qw, sw = oq.quantize_weight(w, bits)
     uw = oq.unpack_int4(qw) if bits == 4 else qw
     n = w.shape[0]
@@ -42,22 +44,22 @@ def _integer_forward(module, bits):
         ua = oq.unpack_int4(qa) if bits == 4 else qa
         acc = oq.int_matmul(ua, uw)
         y = oq.gemm_epilogue(acc, sa, sw, bias, 2 if bias is not None else 1)[:, :n]
-        return _from_bits(y, lead, n)
+        return _from_bits(y, lead, n, x.device)
 
     return forward
 
 
 def _nvfp4_forward(module):
-    pw, sw = oq.pack_nvfp4(module.weight.detach().float().numpy())
+    pw, sw = oq.pack_nvfp4(module.weight.detach().float().cpu().numpy())
     bias = None if module.bias is None else _bits_of(module.bias)
     n, k = module.out_features, module.in_features
 
     def forward(x):
         lead = x.shape[:-1]
-        rows = x.reshape(-1, k).float().numpy()
+        rows = x.reshape(-1, k).float().cpu().numpy()
         pa, sa = oq.pack_nvfp4(rows)
         y = oq.nvfp4_gemm(pa, sa, pw, sw, rows.shape[0], n, k, bias)
-        return _from_bits(y, lead, n)
+        return _from_bits(y, lead, n, x.device)
 
     return forward
 

@@ -1,4 +1,4 @@
-// Small-sequence attention for the DiT action head, writing the rows the
+// Small-query attention for the DiT action head, writing the rows the
 // quantized output projection packs.
 //
 // piR2 runs the DiT attention through torch SDPA (coexecution/
@@ -6,20 +6,26 @@
 // [B, T, H*D] before the integer pack of to_out.  Here one kernel reads q, k
 // and v straight from the projection outputs (row-major [rows, ld], head h at
 // columns h*D..h*D+D-1), and writes the attention output as [B*T, H*D]
-// rows: no transpose copy, and the DiT block stays a chain of this library's
-// kernels (programmatic dependent launch between them).
+// rows: no transpose copy.
 //
-// Grid (H, C, B) with a cluster of C CTAs along y: CTA c of the cluster owns
-// keys [c*chunk, (c+1)*chunk) of head h.  It copies its K and V rows into
-// shared memory with 16-byte asynchronous copies (all in flight at once),
-// then for each tile of up to 32 queries computes fp32 scores
-// s_j = scale * q.k over the chunk, p_j = exp(s_j - m) with the chunk
-// maximum m, l = sum p_j and o[d] = sum p_j v_j[d].  With C = 1 the CTA
-// writes o / l.  With C > 1 the (m, l, o) partials stay in shared memory
-// and, after a cluster barrier, rank r combines every C-th output element
-// of the tile through distributed shared memory:
-// out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, M = max_c m_c.
-// No mask (the DiT's context has no padding); D % 8 == 0, D <= 128.
+// The problem is tiny (17 queries, 17 or 544 keys, 32 heads of 48), far below
+// one 128-row tcgen05 tile, and latency-bound, so the products run on
+// warp-level bf16 MMAs (m16n8k16, fp32 accumulate) held in registers,
+// flash-attention style:
+//
+// Grid (H, C, B) with a cluster of C CTAs along y when C > 1: CTA c owns keys
+// [c*chunk, (c+1)*chunk) of head h and stages them (K and V, bf16, zero-
+// padded to a multiple of 16 keys) plus a tile of up to 64 queries in shared
+// memory with 16-byte asynchronous copies.  Each of the four warps takes 16
+// queries: for every block of up to 64 keys it forms S = q.k (fp32),
+// scales it, keeps a running row maximum m and sum l (online softmax),
+// rounds P = exp(S - m) to bf16 and accumulates O += P.V.  With C = 1 the
+// warp writes O / l.  With C > 1 the (m, l, O) partials stay in shared
+// memory and, after a cluster barrier, rank r combines every C-th output
+// element through distributed shared memory:
+// out = sum_c e^(m_c - M) O_c / sum_c e^(m_c - M) l_c, M = max_c m_c.
+// No mask (the DiT's context has no padding).  head_dim in {32, 48, 64, 96,
+// 128}.
 #pragma once
 #include "args.cuh"
 #include "ptx.cuh"
@@ -40,26 +46,25 @@ struct AttnArgs {
   float scale;
 };
 
-constexpr int kAttnThreads = 256;
-constexpr int kAttnQTile = 32;   // queries held in shared memory at a time
+constexpr int kAttnThreads = 128;
+constexpr int kAttnQTile = 64;   // queries per pass (16 per warp)
+constexpr int kAttnKBlock = 64;  // keys per online-softmax step
 
-// Shared-memory row pitch (elements) of staged K/V rows: D rounded so the
-// pitch is an odd number of 16-byte units, which keeps the 16-byte loads of
-// eight consecutive keys (one per thread) on distinct bank groups.
-__host__ __device__ inline int attn_pitch(int D) {
+// Shared-memory row pitch (elements) of staged q/K/V rows: an odd number of
+// 16-byte units, so the eight row addresses of an ldmatrix phase fall on
+// distinct bank groups.
+__host__ __device__ constexpr int attn_pitch(int D) {
   return ((D / 8) & 1) ? D : D + 8;
 }
 
-// Score rows are padded to an odd number of words.
-__host__ __device__ inline int attn_spitch(int chunk) { return chunk | 1; }
+__host__ __device__ inline int attn_chunk_pad(int chunk) { return (chunk + 15) / 16 * 16; }
 
 __host__ __device__ inline size_t attention_smem(int chunk, int D, int clusters) {
-  const size_t kv = size_t(chunk) * attn_pitch(D) * 2 * 2;
-  const size_t qs = size_t(kAttnQTile) * D * 4;
-  const size_t sc = size_t(kAttnQTile) * attn_spitch(chunk) * 4;
-  const size_t ml = size_t(kAttnQTile) * 2 * 4;
-  const size_t part = clusters > 1 ? size_t(kAttnQTile) * D * 4 : 0;
-  return kv + qs + sc + ml + part;
+  const size_t P = size_t(attn_pitch(D));
+  const size_t kv = size_t(attn_chunk_pad(chunk)) * P * 2 * 2;
+  const size_t qs = size_t(kAttnQTile) * P * 2;
+  const size_t part = clusters > 1 ? size_t(kAttnQTile) * (size_t(D) + 2) * 4 : 0;
+  return kv + qs + part;
 }
 
 __device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
@@ -77,160 +82,253 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   return v;
 }
 
-// Work is spread over all 256 threads in three phases per tile of up to 32
-// queries, each with independent accumulators for instruction-level
-// parallelism: scores (a thread owns one key and four queries), row
-// softmax (a warp per query), and P.V (a thread owns one query and a pair
-// of head dimensions).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                        uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                              uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+
+// D[16x8] += A[16x16] . B[16x8], bf16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+template <int D>
 __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  constexpr int P = attn_pitch(D);
+  constexpr int KS = D / 16;           // k16 steps over the head dimension
+  constexpr int DN = D / 8;            // n8 blocks over the head dimension
+  constexpr int NB = kAttnKBlock / 8;  // n8 blocks per key block
   const int h = blockIdx.x;
   const int b = blockIdx.z;
   const int C = gridDim.y;
-  const int c = blockIdx.y;                      // == cluster rank (cluster spans y)
+  const int c = blockIdx.y;            // == cluster rank (the cluster spans y)
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int D = a.D, P = attn_pitch(D), SP = attn_spitch(a.chunk);
+  const int g = lane >> 2, q4 = lane & 3;
   const int j0 = c * a.chunk;
   const int keys = max(0, min(a.chunk, a.S - j0));
+  const int kpad = (keys + 15) / 16 * 16;
+  const int cpad = attn_chunk_pad(a.chunk);
   __nv_bfloat16 *ks = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
-  __nv_bfloat16 *vs = ks + a.chunk * P;
-  float *qs = reinterpret_cast<float *>(vs + a.chunk * P);   // [QTile][D]
-  float *sc = qs + kAttnQTile * D;                           // [QTile][SP]
-  float *ml = sc + kAttnQTile * SP;                          // [QTile][2]
-  float *part = ml + kAttnQTile * 2;                         // [QTile][D]
+  __nv_bfloat16 *vs = ks + cpad * P;
+  __nv_bfloat16 *qs = vs + cpad * P;                                  // [QTile][P]
+  float *part = reinterpret_cast<float *>(qs + kAttnQTile * P);     // [QTile][D + 2]
 
   pdl_wait();
   pdl_launch_dependents();
-  // K and V rows of this chunk: every 16-byte copy in flight before the wait.
-  const int vecs = D / 8;
-  for (int i = tid; i < keys * vecs; i += kAttnThreads) {
+  constexpr int vecs = D / 8;
+  for (int i = tid; i < kpad * vecs; i += kAttnThreads) {
     const int j = i / vecs, d0 = (i % vecs) * 8;
-    const int64_t row = int64_t(b) * a.S + j0 + j;
-    cp_async_16(ks + j * P + d0, a.k + row * a.ldk + h * D + d0);
-    cp_async_16(vs + j * P + d0, a.v + row * a.ldv + h * D + d0);
+    if (j < keys) {
+      const int64_t row = int64_t(b) * a.S + j0 + j;
+      cp_async_16(ks + j * P + d0, a.k + row * a.ldk + h * D + d0);
+      cp_async_16(vs + j * P + d0, a.v + row * a.ldv + h * D + d0);
+    } else {   // padding keys: zero (their probabilities are exactly 0)
+      *reinterpret_cast<uint4 *>(ks + j * P + d0) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4 *>(vs + j * P + d0) = make_uint4(0, 0, 0, 0);
+    }
   }
+  const uint32_t ks_addr = smem_u32(ks), vs_addr = smem_u32(vs), qs_addr = smem_u32(qs);
 
   for (int t0 = 0; t0 < a.T; t0 += kAttnQTile) {
     const int tn = min(kAttnQTile, a.T - t0);
     const int64_t qbase = int64_t(b) * a.T + t0;
-    for (int i = tid; i < tn * D; i += kAttnThreads) {
-      const int t = i / D, d = i % D;
-      qs[i] = __bfloat162float(a.q[(qbase + t) * a.ldq + h * D + d]) * a.scale;
+    for (int i = tid; i < kAttnQTile * vecs; i += kAttnThreads) {
+      const int t = i / vecs, d0 = (i % vecs) * 8;
+      if (t < tn)
+        cp_async_16(qs + t * P + d0, a.q + (qbase + t) * a.ldq + h * D + d0);
+      else
+        *reinterpret_cast<uint4 *>(qs + t * P + d0) = make_uint4(0, 0, 0, 0);
     }
     cp_async_wait_all();
     __syncthreads();
 
-    // Scores: item = (key j, group of four queries).
-    const int groups = (tn + 3) / 4;
-    for (int i = tid; i < keys * groups; i += kAttnThreads) {
-      const int j = i % keys, t = (i / keys) * 4;
-      const __nv_bfloat16 *kr = ks + j * P;
-      const float *q0 = qs + t * D;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int d = 0; d < D; d += 8) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d);
-        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-        float kf[8];
+    const int r0 = warp * 16;          // this warp's first query of the tile
+    if (r0 < tn) {
+      float o[DN][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(k2[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
+      for (int n = 0; n < DN; ++n)
+        o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      float m_lo = -INFINITY, m_hi = -INFINITY;   // rows g and g + 8
+      float l_lo = 0.f, l_hi = 0.f;               // this thread's partial row sums
+      // q fragments for every k16 step of the head dimension.
+      uint32_t qa[KS][4];
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        const int row = r0 + (lane & 15);
+        const int col = s * 16 + (lane >> 4) * 8;
+        ldsm_x4(qs_addr + uint32_t((row * P + col) * 2), qa[s][0], qa[s][1], qa[s][2], qa[s][3]);
+      }
+      for (int kb = 0; kb < kpad; kb += kAttnKBlock) {
+        const int nbk = min(kAttnKBlock, kpad - kb) / 8;   // n8 key blocks (even)
+        float s_acc[NB][4];
+#pragma unroll
+        for (int n = 0; n < NB; ++n) {
+          s_acc[n][0] = s_acc[n][1] = s_acc[n][2] = s_acc[n][3] = 0.f;
+          if (n < nbk) {
+#pragma unroll
+            for (int s = 0; s < KS; s += 2) {
+              // K rows kb+n*8 .. +7, dims s*16 .. s*16+31: B fragments of
+              // the k16 steps s and s + 1.
+              uint32_t b0, b1, b2, b3;
+              const int row = kb + n * 8 + (lane & 7);
+              if (s + 1 < KS) {
+                const int col = s * 16 + (lane >> 3) * 8;
+                ldsm_x4(ks_addr + uint32_t((row * P + col) * 2), b0, b1, b2, b3);
+                mma_bf16_16816(s_acc[n], qa[s], b0, b1);
+                mma_bf16_16816(s_acc[n], qa[s + 1], b2, b3);
+              } else {
+                // Odd step count (D = 48): the last step alone.
+                const int col = s * 16 + ((lane >> 3) & 1) * 8;
+                ldsm_x4(ks_addr + uint32_t((row * P + col) * 2), b0, b1, b2, b3);
+                mma_bf16_16816(s_acc[n], qa[s], b0, b1);
+              }
+            }
+          }
         }
+        // Scale, mask padding keys, running maxima of rows g and g + 8.
+        float bm_lo = -INFINITY, bm_hi = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (t + u < tn) {
-            const float4 qa = *reinterpret_cast<const float4 *>(q0 + u * D + d);
-            const float4 qb = *reinterpret_cast<const float4 *>(q0 + u * D + d + 4);
-            acc[u] = fmaf(qa.x, kf[0], acc[u]);
-            acc[u] = fmaf(qa.y, kf[1], acc[u]);
-            acc[u] = fmaf(qa.z, kf[2], acc[u]);
-            acc[u] = fmaf(qa.w, kf[3], acc[u]);
-            acc[u] = fmaf(qb.x, kf[4], acc[u]);
-            acc[u] = fmaf(qb.y, kf[5], acc[u]);
-            acc[u] = fmaf(qb.z, kf[6], acc[u]);
-            acc[u] = fmaf(qb.w, kf[7], acc[u]);
+        for (int n = 0; n < NB; ++n) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = kb + n * 8 + 2 * q4 + (e & 1);
+            float v = s_acc[n][e] * a.scale;
+            if (n >= nbk || key >= keys)
+              v = -INFINITY;
+            s_acc[n][e] = v;
+          }
+          bm_lo = fmaxf(bm_lo, fmaxf(s_acc[n][0], s_acc[n][1]));
+          bm_hi = fmaxf(bm_hi, fmaxf(s_acc[n][2], s_acc[n][3]));
+        }
+        bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 1));
+        bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 2));
+        bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 1));
+        bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 2));
+        const float mn_lo = fmaxf(m_lo, bm_lo), mn_hi = fmaxf(m_hi, bm_hi);
+        const float al_lo = m_lo == -INFINITY ? 0.f : expf(m_lo - mn_lo);
+        const float al_hi = m_hi == -INFINITY ? 0.f : expf(m_hi - mn_hi);
+        m_lo = mn_lo;
+        m_hi = mn_hi;
+        l_lo *= al_lo;
+        l_hi *= al_hi;
+#pragma unroll
+        for (int n = 0; n < DN; ++n) {
+          o[n][0] *= al_lo;
+          o[n][1] *= al_lo;
+          o[n][2] *= al_hi;
+          o[n][3] *= al_hi;
+        }
+        // P = exp(S - m) as bf16 A fragments (two n8 key blocks per k16).
+        uint32_t pa[NB / 2][4];
+#pragma unroll
+        for (int n = 0; n < NB; ++n) {
+          const float p0 = expf(s_acc[n][0] - m_lo), p1 = expf(s_acc[n][1] - m_lo);
+          const float p2 = expf(s_acc[n][2] - m_hi), p3 = expf(s_acc[n][3] - m_hi);
+          l_lo += p0 + p1;
+          l_hi += p2 + p3;
+          pa[n / 2][(n & 1) * 2 + 0] = pack_bf16x2(p0, p1);
+          pa[n / 2][(n & 1) * 2 + 1] = pack_bf16x2(p2, p3);
+        }
+        // O += P . V over the block's keys.
+#pragma unroll
+        for (int kk = 0; kk < NB / 2; ++kk) {
+          if (2 * kk < nbk) {
+            const int row = kb + kk * 16 + (lane & 15);
+#pragma unroll
+            for (int n = 0; n < DN; n += 2) {
+              // V rows kk*16 .. +15 of the block, dims n*8 .. n*8+15.
+              uint32_t b0, b1, b2, b3;
+              if (n + 1 < DN) {
+                const int col = n * 8 + (lane >> 4) * 8;
+                ldsm_x4_trans(vs_addr + uint32_t((row * P + col) * 2), b0, b1, b2, b3);
+                mma_bf16_16816(o[n], pa[kk], b0, b1);
+                mma_bf16_16816(o[n + 1], pa[kk], b2, b3);
+              } else {
+                ldsm_x4_trans(vs_addr + uint32_t((row * P + n * 8) * 2), b0, b1, b2, b3);
+                mma_bf16_16816(o[n], pa[kk], b0, b1);
+              }
+            }
           }
         }
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (t + u < tn)
-          sc[(t + u) * SP + j] = acc[u];
-    }
-    __syncthreads();
-
-    // Row softmax over this chunk's keys: a warp per query.
-    for (int t = warp; t < tn; t += kAttnThreads / 32) {
-      float *row = sc + t * SP;
-      float m = -INFINITY;
-      for (int j = lane; j < keys; j += 32)
-        m = fmaxf(m, row[j]);
-      for (int o = 16; o; o >>= 1)
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      float l = 0.f;
-      for (int j = lane; j < keys; j += 32) {
-        const float e = expf(row[j] - m);
-        row[j] = e;
-        l += e;
-      }
-      for (int o = 16; o; o >>= 1)
-        l += __shfl_xor_sync(0xffffffffu, l, o);
-      if (lane == 0) {
-        ml[2 * t] = m;
-        ml[2 * t + 1] = l;
-      }
-    }
-    __syncthreads();
-
-    // P.V: item = (query t, pair of head dimensions).
-    const int pairs = D / 2;
-    for (int i = tid; i < tn * pairs; i += kAttnThreads) {
-      const int t = i / pairs, d = (i % pairs) * 2;
-      const float *prow = sc + t * SP;
-      float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-      int j = 0;
-      for (; j + 1 < keys; j += 2) {
-        const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(vs + j * P + d));
-        const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(vs + (j + 1) * P + d));
-        o0 = fmaf(prow[j], va.x, o0);
-        o1 = fmaf(prow[j], va.y, o1);
-        o2 = fmaf(prow[j + 1], vb.x, o2);
-        o3 = fmaf(prow[j + 1], vb.y, o3);
-      }
-      if (j < keys) {
-        const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(vs + j * P + d));
-        o0 = fmaf(prow[j], va.x, o0);
-        o1 = fmaf(prow[j], va.y, o1);
-      }
-      o0 += o2;
-      o1 += o3;
+      l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+      l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+      l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+      l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+      const int t_lo = r0 + g, t_hi = r0 + g + 8;
       if (C > 1) {
-        part[t * D + d] = o0;
-        part[t * D + d + 1] = o1;
+#pragma unroll
+        for (int n = 0; n < DN; ++n) {
+          const int d = n * 8 + 2 * q4;
+          part[t_lo * (D + 2) + 2 + d] = o[n][0];
+          part[t_lo * (D + 2) + 3 + d] = o[n][1];
+          part[t_hi * (D + 2) + 2 + d] = o[n][2];
+          part[t_hi * (D + 2) + 3 + d] = o[n][3];
+        }
+        if (q4 == 0) {
+          part[t_lo * (D + 2)] = m_lo;
+          part[t_lo * (D + 2) + 1] = l_lo;
+          part[t_hi * (D + 2)] = m_hi;
+          part[t_hi * (D + 2) + 1] = l_hi;
+        }
       } else {
-        const float inv = 1.0f / ml[2 * t + 1];
-        __nv_bfloat16 *dst = a.out + (qbase + t) * a.ldo + h * D + d;
-        dst[0] = __float2bfloat16_rn(o0 * inv);
-        dst[1] = __float2bfloat16_rn(o1 * inv);
+        const float i_lo = 1.0f / l_lo, i_hi = 1.0f / l_hi;
+#pragma unroll
+        for (int n = 0; n < DN; ++n) {
+          const int d = h * D + n * 8 + 2 * q4;
+          if (t_lo < tn) {
+            __nv_bfloat16 *dst = a.out + (qbase + t_lo) * a.ldo + d;
+            dst[0] = __float2bfloat16_rn(o[n][0] * i_lo);
+            dst[1] = __float2bfloat16_rn(o[n][1] * i_lo);
+          }
+          if (t_hi < tn) {
+            __nv_bfloat16 *dst = a.out + (qbase + t_hi) * a.ldo + d;
+            dst[0] = __float2bfloat16_rn(o[n][2] * i_hi);
+            dst[1] = __float2bfloat16_rn(o[n][3] * i_hi);
+          }
+        }
       }
     }
 
     if (C > 1) {
       // Partials of this tile are complete in every CTA of the cluster.
       cluster_sync();
-      const uint32_t ml_base = smem_u32(ml), part_base = smem_u32(part);
+      const uint32_t part_base = smem_u32(part);
       for (int i = c * kAttnThreads + tid; i < tn * D; i += C * kAttnThreads) {
-        const int t = i / D;
+        const int t = i / D, d = i % D;
+        const uint32_t row = part_base + uint32_t(t * (D + 2) * 4);
         float mc[8], lc[8], oc[8];
         float M = -INFINITY;
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
           if (r < C) {
-            mc[r] = ld_cluster_f32(map_peer(ml_base + uint32_t(8 * t), uint32_t(r)));
-            lc[r] = ld_cluster_f32(map_peer(ml_base + uint32_t(8 * t + 4), uint32_t(r)));
-            oc[r] = ld_cluster_f32(map_peer(part_base + uint32_t(4 * i), uint32_t(r)));
+            const uint32_t peer = map_peer(row, uint32_t(r));
+            mc[r] = ld_cluster_f32(peer);
+            lc[r] = ld_cluster_f32(peer + 4);
+            oc[r] = ld_cluster_f32(peer + uint32_t((2 + d) * 4));
           } else {
             mc[r] = -INFINITY;
             lc[r] = 0.f;
@@ -245,7 +343,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(const Attn
           L = fmaf(w, lc[r], L);
           acc = fmaf(w, oc[r], acc);
         }
-        a.out[(qbase + t) * a.ldo + h * D + (i % D)] = __float2bfloat16_rn(acc / L);
+        a.out[(qbase + t) * a.ldo + h * D + d] = __float2bfloat16_rn(acc / L);
       }
       // Peers are done reading this tile's partials before they are reused
       // (and before any CTA of the cluster exits).
@@ -265,6 +363,25 @@ static int attention_chunks(int S) {
   return c;
 }
 
+static bool attention_head_dim_supported(int D) {
+  return D == 32 || D == 48 || D == 64 || D == 96 || D == 128;
+}
+
+template <int D>
+static cudaError_t attention_set_smem(int bytes) {
+  return cudaFuncSetAttribute(attention_rows_kernel<D>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+static cudaError_t attention_set_smem_all(int bytes) {
+  cudaError_t e = attention_set_smem<32>(bytes);
+  if (e == cudaSuccess) e = attention_set_smem<48>(bytes);
+  if (e == cudaSuccess) e = attention_set_smem<64>(bytes);
+  if (e == cudaSuccess) e = attention_set_smem<96>(bytes);
+  if (e == cudaSuccess) e = attention_set_smem<128>(bytes);
+  return e;
+}
+
 cudaError_t run_attention_rows(AttnArgs a, int B, cudaStream_t st) {
   const int C = attention_chunks(a.S);
   a.chunk = (a.S + C - 1) / C;
@@ -282,7 +399,13 @@ cudaError_t run_attention_rows(AttnArgs a, int B, cudaStream_t st) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = C > 1 ? 2 : 1;      // no cluster launch for a single chunk
-  return cudaLaunchKernelEx(&cfg, attention_rows_kernel, a);
+  switch (a.D) {
+  case 32: return cudaLaunchKernelEx(&cfg, attention_rows_kernel<32>, a);
+  case 48: return cudaLaunchKernelEx(&cfg, attention_rows_kernel<48>, a);
+  case 64: return cudaLaunchKernelEx(&cfg, attention_rows_kernel<64>, a);
+  case 96: return cudaLaunchKernelEx(&cfg, attention_rows_kernel<96>, a);
+  default: return cudaLaunchKernelEx(&cfg, attention_rows_kernel<128>, a);
+  }
 }
 
 } // namespace pir2b

@@ -90,9 +90,7 @@ static int device_info(DeviceInfo **out) {
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                d.max_smem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attention_rows_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               d.max_smem);
+      e = attention_set_smem_all(d.max_smem);
     if (e != cudaSuccess)
       return cuda_status(e, "cudaFuncSetAttribute");
     d.attrs_set = true;
@@ -187,11 +185,47 @@ static size_t gemm_smem(int bits, int bn, int stages) {
 // prologue and weight prefetch then run while this one finishes.
 constexpr int kCoResidentSmem = 110 * 1024;
 
-static int stages_for(int bits, int bn, int max_smem) {
-  int s = 8;
+static int stages_for(int bits, int bn, int max_smem, int cap = 8) {
+  int s = cap;
   while (s > 2 && gemm_smem(bits, bn, s) > size_t(max_smem))
     --s;
   return s;
+}
+
+// Small M (one token tile of <= 64 tokens) is weight streaming, and the
+// measured TMA round trip under load is ~2,500 SM cycles, so a CTA moves at
+// most (stages x stage bytes) per round trip.  Weight tiles do not depend on
+// the previous kernel and are issued before griddepcontrol.wait, so the best
+// plan gives every CTA room for its whole K slice (all of its weights are in
+// flight while the producer kernel still runs) and spreads the matrix over
+// enough CTAs: the smallest split with >= 96 CTAs whose K slice fits the
+// stage ring.  Matrices with >= 148 channel tiles keep two CTAs per SM.
+static bool plan_small_m(int bits, int64_t m, int ntiles, int num_kb, int max_smem,
+                         GemmPlan *plan) {
+  const int bn = int((m + 15) / 16 * 16);
+  if (ntiles >= 148) {
+    const int stages = stages_for(bits, bn, std::min(max_smem, kCoResidentSmem));
+    *plan = GemmPlan{bn, 1, 1, stages, gemm_smem(bits, bn, stages)};
+    return true;
+  }
+  const int smax = stages_for(bits, bn, max_smem, 12);
+  int chosen = 0;
+  for (int s = 1; s <= 8 && s <= num_kb; s *= 2) {
+    const int kb_per = (num_kb + s - 1) / s;
+    chosen = s;
+    if (kb_per <= smax && ntiles * s >= 96)
+      break;
+  }
+  const int kb_per = (num_kb + chosen - 1) / chosen;
+  const int stages = std::max(2, std::min(smax, kb_per));
+  const size_t smem = gemm_smem(bits, bn, stages);
+  if (smem > size_t(max_smem))
+    return false;
+  // The split-K partial tile and staging slice live in the stage buffers.
+  if (chosen > 1 && size_t(stages) * (16384 + size_t(bn) * 128) < size_t(bn) * (512 + 128))
+    return false;
+  *plan = GemmPlan{bn, 1, chosen, stages, smem};
+  return true;
 }
 
 // Picks the token tile, number of token tiles and the split-K cluster size
@@ -210,6 +244,8 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
   const int ntiles = int((npad + 127) / 128);
   const int num_kb = int(kpad / 128);
   GemmPlan best{0, 0, 0, 0, 0};   // smem == 0 marks "no plan"
+  if (m <= 64 && plan_small_m(bits, m, ntiles, num_kb, max_smem, &best))
+    return best;
   double best_cost = 1e30;
   // One token tile up to 256 tokens (weights streamed once); larger M also
   // tries 1-3 extra tiles to balance the waves.
@@ -569,19 +605,19 @@ int pir2b_attention_rows(const void *q, int64_t ldq, const void *k,
                          int64_t ldk, const void *v, int64_t ldv, void *out,
                          int64_t ldo, int64_t batch, int64_t tq, int64_t skv,
                          int heads, int head_dim, float scale, void *stream) {
-  if (batch < 1 || tq < 1 || skv < 1 || heads < 1 || head_dim < 8 ||
-      head_dim > 128 || head_dim % 8 != 0 || skv > (int64_t(1) << 20) ||
+  if (batch < 1 || tq < 1 || skv < 1 || heads < 1 ||
+      !attention_head_dim_supported(head_dim) || skv > (int64_t(1) << 20) ||
       tq > (int64_t(1) << 30) || batch > 65535 || heads > 65535)
     return fail(PIR2B_EINVAL,
-                "attention_rows: need batch, T, S >= 1 and head_dim %% 8 == 0, <= 128");
+                "attention_rows: need batch, T, S >= 1 and head_dim in {32, 48, 64, 96, 128}");
   const int64_t width = int64_t(heads) * head_dim;
-  if (ldq < width || ldk < width || ldv < width || ldo < width ||
+  if (ldq < width || ldk < width || ldv < width || ldo < width || ldq % 8 != 0 ||
       ldk % 8 != 0 || ldv % 8 != 0)
-    return fail(PIR2B_EINVAL, "attention_rows: row strides too small or K/V strides not %% 8");
+    return fail(PIR2B_EINVAL, "attention_rows: row strides too small or q/K/V strides not %% 8");
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
     return fail(PIR2B_EINVAL, "attention_rows operands must be non-null");
-  if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 2) || !aligned(out, 2))
-    return fail(PIR2B_EALIGN, "attention_rows: K/V must be 16-byte aligned");
+  if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 16) || !aligned(out, 2))
+    return fail(PIR2B_EALIGN, "attention_rows: q/K/V must be 16-byte aligned");
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;

@@ -11,7 +11,13 @@ quantized projection, keeping the model's own forward code:
 * DiT `BasicTransformerBlock`: x + to_out(...) and x + ff(...) likewise, and
   norm3 (non-affine LayerNorm) + pack of the FFN input becomes the fused
   LayerNorm producer (zero AdaLN modulation, which leaves the normalized
-  bf16 values unchanged, as piR2's residual fusion does).
+  bf16 values unchanged, as piR2's residual fusion does);
+* the FFN's GELU moves from the down projection's pack (piR2's
+  `forward_gelu`, a LUT applied while packing) into the up projection's GEMM
+  epilogue (the same torch-built LUT applied to its bf16 output), so the down
+  projection packs plain values: the codes are identical, and the LUT
+  gathers run once per output element inside a kernel that is already
+  running.
 
 Results are bitwise those of the unfused quantized model: the epilogue adds
 the residual to the bf16 GEMM output in fp32 and rounds once, exactly as
@@ -21,6 +27,8 @@ torch's bf16 addition does.
 import torch
 
 from .connections import packed_input
+from .fused import prepare_gelu
+from .linear import prepare
 from .modulation import prepare_norm_modulation
 
 
@@ -67,6 +75,15 @@ class ResidualFusion:
                 and not block.norm3.elementwise_affine
                 and self._quantized(block.ff.net[0].proj)
             )
+            act = block.ff.net[0]
+            gelu_epilogue = (
+                type(act).__name__ == "GELU"
+                and self._quantized(act.proj)
+                and len(block.ff.net) == 3
+                and isinstance(block.ff.net[1], torch.nn.Dropout)
+            )
+            up_q = self._q(act.proj, bits) if gelu_epilogue else None
+            lut = prepare_gelu(down_q.packed_weight.device, torch.bfloat16, act.approximate) if gelu_epilogue else None
 
             def forward(
                 hidden_states,
@@ -80,6 +97,8 @@ class ResidualFusion:
                 zero=zero,
                 fuse_norm=fuse_norm,
                 bits=bits,
+                up_q=up_q,
+                lut=lut,
             ):
                 x = hidden_states
                 normalized = block.norm1(x, temb) if block.norm_type == "ada_norm" else block.norm1(x)
@@ -98,7 +117,11 @@ class ResidualFusion:
                 else:
                     ff_in = block.norm3(x)
                 down_q.pending_residual(x)
-                return block.ff(ff_in)
+                if up_q is None:
+                    return block.ff(ff_in)
+                packed = ff_in.for_bits(bits) if getattr(ff_in, "_robotics_packed_input", False) else prepare(ff_in, bits)
+                hidden = up_q.forward_packed(packed, out_lut=lut)      # gelu(up(x)), bf16
+                return self.controller.dispatch(down_q, hidden)
 
             block.forward = forward
 

@@ -221,11 +221,16 @@ def gemm_nvfp4(a_packed, a_sf, w_packed, w_sf, bias=None, *, n, alpha=1.0, out=N
         raise ValueError("NVFP4 operand shapes do not match")
     if out is None:
         out = torch.empty((m, n), device=a_packed.device, dtype=torch.bfloat16)
+    recorder = launch_recorder
+    if recorder is not None:
+        recorder.before(a_packed.device)
     status = _lib.lib().pir2b_gemm_nvfp4(
         a_packed.data_ptr(), a_sf.data_ptr(), w_packed.data_ptr(), w_sf.data_ptr(), _ptr(bias),
         float(alpha), m, n, k, out.data_ptr(), out.stride(0), _stream(a_packed.device),
     )
     _lib.check(status, "pir2b_gemm_nvfp4")
+    if recorder is not None:
+        recorder.after(a_packed.device, bits="fp4", m=m, n=n, k=k, npad=n)
     return out
 
 

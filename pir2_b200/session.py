@@ -172,10 +172,12 @@ class GrootOptimizations:
                 self.pointwise = TextAttentionFusion(model, self.controller)
                 self.stack.callback(self.pointwise.close)
                 self.pointwise.set({"w8a8": 8, "w4a4": 4}[self.config.precision])
-            # DiTAttentionFusion (pointwise.py) is built and tested but not
-            # installed: at the DiT shapes (17 queries, 17 or 544 keys, 32
-            # heads of 48) cuDNN's SDPA plus the transpose copy is faster
-            # than attention_rows_kernel (2.5 vs 6.1 us, 8.4 vs 13.2 us).
+            if self.config.fusion_mode == "all":
+                from .pointwise import DiTAttentionFusion
+
+                self.attention = DiTAttentionFusion(model.action_head.model)
+                self.stack.callback(self.attention.close)
+                self.attention.set()
             self.producers = QuantizationProducers(model, self.controller)
             if self.producers.norms:
                 self.stack.callback(self.producers.close)

@@ -1,13 +1,25 @@
-"""End-to-end action parity of a reduced GR00T-shaped policy (2 VLM layers,
-2 DiT blocks, full widths): the fused B200 path against (a) the same
-policy with every Linear replaced by the oracle's quantized Linear on the
-CPU, and (b) the unquantized bf16 policy.
+"""End-to-end parity of a reduced GR00T-shaped policy (2 VLM layers, 2 DiT
+blocks, full widths, 4 Euler steps) on the B200 path.
 
-piR2 pins no end-to-end actions; this build pins them here.  Tolerances
-(relative L2 over all actions, and max-abs) are stated per precision; the
-oracle comparison differs only by rounding in the torch parts (norms,
-attention) between CPU and GPU and in the fused producers' reduction order,
-which can move individual activation codes by one.
+The oracle policy is the same policy with every Linear replaced by the
+oracle's quantized Linear (computed on the host, returned to the GPU);
+everything between the Linears runs the same torch GPU code.  So:
+
+- with the plugin's unfused installation (TransformerINT only) the
+  actions must be bitwise identical to the oracle policy's: every integer
+  stage is exact and the activations (GELU, SiLU·up) are applied through
+  torch-built LUTs that equal torch's own results;
+- with the fused installation (norm/modulation/residual producers, q/k
+  RMSNorm + RoPE, row attention) the producers round in a different order
+  (activation codes may move by one), so actions are compared by relative L2;
+- against the unquantized bf16 policy the quantization error itself is
+  bounded (relative L2).
+
+piR2 pins no end-to-end actions; this build pins them here.  Comparing
+with a CPU oracle policy instead is not informative: CPU and GPU torch
+attention differ by ~0.4 % relative, which moves activation codes across
+rounding boundaries and changes quantized outputs by about the
+quantization noise itself.
 """
 
 import copy
@@ -26,19 +38,16 @@ pytestmark = pytest.mark.gpu
 VLM = harness.VLMConfig(layers=2, vocab=2048)
 DIT = harness.DiTConfig(layers=2)
 
-# Relative L2 bounds: (VLM features vs oracle, actions vs oracle, actions vs
-# bf16).  The flow integration amplifies single-code differences, so the
-# action bounds are looser than the feature bounds; int4 codes are 18x
-# coarser than int8 codes.
-TOLERANCE = {"w8a8": (0.02, 0.03, 0.10), "w4a4": (0.10, 0.40, 0.80), "fp4": (0.10, 0.40, 0.80)}
+# Relative-L2 bounds on the actions: (fused vs oracle policy, vs bf16).
+TOLERANCE = {"w8a8": (0.05, 0.10), "w4a4": (0.50, 0.80), "fp4": (0.10, 0.60)}
 
 
 def _rel_l2(a, b):
-    a, b = a.detach().cpu().float(), b.detach().cpu().float()
+    a, b = a.detach().float(), b.detach().float()
     return (a - b).norm().item() / b.norm().item()
 
 
-def _config(precision):
+def _fused(precision):
     if precision == "fp4":
         return OptimizationConfig(precision="fp4", scope="all")
     return OptimizationConfig(
@@ -47,33 +56,40 @@ def _config(precision):
     )
 
 
+@pytest.fixture(scope="module")
+def policies():
+    with torch.inference_mode():
+        policy = harness.build_policy("cuda", vlm=VLM, dit=DIT)
+        inputs = harness.synthetic_inputs(1, "cuda", vlm=VLM, dit=DIT)
+        bf16_actions = policy(*inputs)
+    return policy, inputs, bf16_actions
+
+
+@pytest.mark.parametrize("precision", ["w8a8", "w4a4"])
+@torch.inference_mode()
+def test_unfused_actions_equal_oracle_policy_bitwise(policies, precision):
+    policy, inputs, bf16_actions = policies
+    oracle_policy = install_oracle_linears(copy.deepcopy(policy), precision)
+    with GrootOptimizations(SimpleNamespace(model=policy), OptimizationConfig(precision=precision, scope="all")):
+        actions = policy(*inputs)
+    assert torch.equal(policy(*inputs), bf16_actions)     # restored
+    assert torch.equal(actions, oracle_policy(*inputs))
+
+
 @pytest.mark.parametrize("precision", ["w8a8", "w4a4", "fp4"])
 @torch.inference_mode()
-def test_actions_match_oracle_quantized_policy(precision):
-    policy = harness.build_policy("cuda", vlm=VLM, dit=DIT)
-    cpu_policy = copy.deepcopy(policy).to("cpu")
-    inputs = harness.synthetic_inputs(1, "cuda", vlm=VLM, dit=DIT)
-    cpu_inputs = [t.cpu() for t in inputs]
-    bf16_actions = policy(*inputs)
-    with GrootOptimizations(SimpleNamespace(model=policy), _config(precision)):
-        features = policy.backbone(*inputs[:2])
+def test_fused_actions_match_oracle_policy(policies, precision):
+    policy, inputs, bf16_actions = policies
+    oracle_policy = install_oracle_linears(copy.deepcopy(policy), precision)
+    with GrootOptimizations(SimpleNamespace(model=policy), _fused(precision)):
         actions = policy(*inputs)
-    restored = policy(*inputs)
-    platform = _rel_l2(bf16_actions, cpu_policy(*cpu_inputs))   # bf16 GPU vs bf16 CPU
-    install_oracle_linears(cpu_policy, precision)
-    oracle_features = cpu_policy.backbone(*cpu_inputs[:2])
-    oracle_actions = cpu_policy(*cpu_inputs)
-
-    assert torch.equal(restored, bf16_actions)          # the session restored the model
+    assert torch.equal(policy(*inputs), bf16_actions)     # restored
     assert torch.isfinite(actions).all()
-    rel_features = _rel_l2(features, oracle_features)
+    oracle_actions = oracle_policy(*inputs)
     rel_oracle = _rel_l2(actions, oracle_actions)
     rel_bf16 = _rel_l2(actions, bf16_actions)
-    print(
-        f"{precision}: features vs oracle {rel_features:.3e}; actions vs oracle {rel_oracle:.3e}, "
-        f"vs bf16 {rel_bf16:.3e}; bf16 GPU vs CPU {platform:.3e}"
-    )
-    tol_features, tol_actions, tol_bf16 = TOLERANCE[precision]
-    assert rel_features <= tol_features
-    assert rel_oracle <= tol_actions
+    print(f"{precision}: fused vs oracle policy {rel_oracle:.3e}, vs bf16 {rel_bf16:.3e}, "
+          f"oracle vs bf16 {_rel_l2(oracle_actions, bf16_actions):.3e}")
+    tol_oracle, tol_bf16 = TOLERANCE[precision]
+    assert rel_oracle <= tol_oracle
     assert rel_bf16 <= tol_bf16

@@ -323,9 +323,10 @@ def _sdpa_rows(q, k, v, b, heads, d):
         (1, 17, 544, 32, 48),     # DiT cross-attention: 8-CTA cluster per head
         (2, 17, 544, 32, 48),
         (3, 5, 33, 4, 64),
-        (1, 9, 130, 2, 128),      # 2 chunks, pitch padded
-        (1, 40, 300, 4, 48),      # query tiles of 32 across the cluster combine
-        (2, 3, 1500, 2, 40),      # odd 16-byte pitch, ragged last chunk
+        (1, 9, 130, 2, 128),      # 2 chunks, padded keys
+        (1, 70, 300, 4, 48),      # two query tiles of 64 across the cluster combine
+        (2, 3, 1500, 2, 32),      # 188 keys per CTA: three online-softmax blocks, ragged
+        (1, 33, 96, 3, 96),
     ],
 )
 def test_attention_rows_matches_fp32_sdpa(b, t, s, heads, d):
@@ -350,7 +351,7 @@ def test_attention_rows_strided_query_and_argument_errors():
     out = ops.attention_rows(q, k, v, batch=1, heads=heads, head_dim=d)
     torch.testing.assert_close(out.float(), _sdpa_rows(q, k, v, 1, heads, d), atol=4e-3, rtol=8e-3)
     with pytest.raises(ValueError):
-        ops.attention_rows(q, k, v, batch=1, heads=heads, head_dim=12)   # head_dim % 8
+        ops.attention_rows(q, k, v, batch=1, heads=heads, head_dim=12)   # unsupported head_dim
     long_kv = torch.zeros(20000, 2 * w, device="cuda", dtype=torch.bfloat16)   # keys exceed shared memory
     with pytest.raises(ValueError):
         ops.attention_rows(q, long_kv[:, :w], long_kv[:, w:], batch=1, heads=heads, head_dim=d)

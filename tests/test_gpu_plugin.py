@@ -227,7 +227,7 @@ def test_dit_attention_fusion_matches_sdpa_forward_and_restores(cross):
     if cross:
         attn.kv_cache = attn.kv(context)
     reference = attn(x, encoder_hidden_states=context)
-    fusion = DiTAttentionFusion(torch.nn.Sequential(attn))
+    fusion = DiTAttentionFusion(torch.nn.Sequential(attn), cross_only=False)
     assert fusion.targets == [attn]
     fusion.set()
     try:
@@ -238,3 +238,38 @@ def test_dit_attention_fusion_matches_sdpa_forward_and_restores(cross):
     # Both paths run the same bf16 projections; the attention core differs
     # only in summation order and bf16 rounding of its output.
     torch.testing.assert_close(fused.float(), reference.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@torch.inference_mode()
+def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits):
+    """Residual adds in the o-proj / down-proj epilogues and the FFN GELU in
+    the up-projection epilogue give bitwise the unfused quantized blocks."""
+    from pir2_b200.fusion import ResidualFusion
+    from pir2_b200.harness import DiTConfig, VLMConfig, build_policy
+
+    dit = DiTConfig(layers=2)
+    policy = build_policy("cuda", dit=dit, vlm=VLMConfig(layers=1, vocab=2048))
+    model = policy.action_head.model
+    names, _, _, _ = inventory(policy)
+    executed = {n for n in names if n.startswith("action_head.model.transformer_blocks")}
+    adapter = TransformerINT(policy, executed, native=True, expanded=True)
+    fusion = ResidualFusion(policy, adapter)
+    assert len(fusion.blocks) == 2
+    torch.manual_seed(5)
+    x = torch.randn(2, 17, dit.hidden, device="cuda", dtype=torch.bfloat16)
+    temb = torch.randn(2, dit.hidden, device="cuda", dtype=torch.bfloat16)
+    context = torch.randn(2, 544, dit.context, device="cuda", dtype=torch.bfloat16)
+    try:
+        adapter.set(f"w{bits}a{bits}")
+        outs = []
+        for block in model.transformer_blocks:
+            ctx = context if block.attn1.is_cross_attention else None
+            outs.append(block(x, encoder_hidden_states=ctx, temb=temb))
+        fusion.set(bits, norm_pack=False)
+        for block, ref in zip(model.transformer_blocks, outs):
+            ctx = context if block.attn1.is_cross_attention else None
+            equal(block(x, encoder_hidden_states=ctx, temb=temb), ref)
+    finally:
+        fusion.close()
+        adapter.close()

@@ -73,6 +73,6 @@ def test_gemm_planner_always_returns_a_launchable_plan():
                     assert bn % 16 == 0 and 16 <= bn <= 256
                     assert bn * mt >= m and bn * (mt - 1) < m
                     assert splits in (1, 2, 4, 8) and splits <= k // 128
-                    assert 2 <= stages <= 8 and 0 < smem <= 232448
+                    assert 2 <= stages <= 12 and 0 < smem <= 232448
                     if splits > 1:
                         assert stages * (16384 + bn * 128) >= bn * (512 + 128)
