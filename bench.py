@@ -52,6 +52,12 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--precision", choices=["w8a8", "w4a4", "fp4"], default="w8a8")
     p.add_argument("--batch", type=int, default=1, help="robots per GPU")
+    p.add_argument(
+        "--robots",
+        type=int,
+        default=None,
+        help="total robots sharded over the GPUs (batched config: B=64 -> 64/N per GPU, strong scaling)",
+    )
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--cpu-sample-seconds", type=float, default=20.0)
     p.add_argument(
@@ -437,7 +443,7 @@ def run_ours(args, world, rank, local):
             "warmup": args.warmup,
             "ms_per_step": round(ms, 4),
             "higher_is_better": False,
-            "scaling": "weak",
+            "scaling": "weak" if args.robots is None else "strong",
             "vs_baseline": None,
             "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1"}[args.precision],
             "data": "synthetic",
@@ -445,6 +451,7 @@ def run_ours(args, world, rank, local):
                 "workload": f"GR00T-shaped control step per GPU, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
                 "precision": args.precision,
                 "batch_per_gpu": args.batch,
+                "robots_total": args.batch * world,
                 "parallelism": f"independent robots, dp{world}, no collective",
                 "graph": not args.no_graph,
                 "l2": "each step streams ~1.4 GB of packed weights (> 126 MB L2); no flush",
@@ -587,6 +594,10 @@ def main():
         run_kernel(args)
         return
     world, rank, local = dist_setup(args)
+    if args.robots is not None:
+        if args.robots % world:
+            raise SystemExit(f"--robots {args.robots} does not split over {world} GPUs")
+        args.batch = args.robots // world
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)

@@ -169,6 +169,20 @@ int pir2b_qk_norm_rope(const void *qkv, int64_t ld, const void *q_weight,
                        int head_dim, float eps, void *q_out, void *k_out,
                        void *v_out, void *stream);
 
+/* W8A8 gate|up GEMM with the SwiGLU epilogue: out[m, c] =
+ * bf16(f32(silu_lut[g]) * f32(u)) for c < half_n, where g and u are the
+ * exact dequantized bf16 GEMM outputs of gate channel c and up channel c.
+ * The weight rows (and sw, bias) are interleaved in blocks of 128: rows
+ * 256j..256j+127 are gate channels 128j.., rows 256j+128..256j+255 the
+ * matching up channels.  The result equals piR2's text MLP path, which
+ * writes gate|up (coexecution/optimization/groot/integer.py:166-172) and
+ * packs bf16(SiLU(gate) * up) in the down projection's gated pack
+ * (coexecution/kernels/ampere_ada/integer.py:27-48); here the down
+ * projection packs `out` plainly.  half_n % 128 == 0, kpad % 128 == 0. */
+int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const float *sw,
+                      const void *bias, int bias_mode, const void *silu_lut, int64_t m,
+                      int64_t half_n, int64_t kpad, void *out, int64_t ldo, void *stream);
+
 /* Small-sequence attention (no mask) reading q, k, v from projection rows
  * (head h at columns h*head_dim..) and writing out[b*T + t, h*head_dim + d]
  * rows for the output projection's pack; fp32 scores and softmax, bf16 out.

@@ -56,6 +56,11 @@ struct GemmArgs {
   int stages;                       // pipeline depth
   int splits;                       // cluster size along z (1,2,4,8)
   int tma_store;                    // 1: output tile leaves through TMA
+  int wt;                           // 128-channel weight tiles per CTA (1, 2)
+  // SwiGLU epilogue (wt == 2, no split-K): weight tile 0 holds 128 gate
+  // channels and tile 1 the matching up channels; the CTA writes
+  // bf16(silu_lut[gate] * up) for those 128 output channels.
+  const __nv_bfloat16 *silu_lut;    // [65536] or null
 };
 
 cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,

@@ -171,10 +171,11 @@ static int make_out_map(CUtensorMap *map, const void *base, uint64_t cols,
 struct GemmPlan {
   int bn, mtiles, splits, stages;
   size_t smem;
+  int wt = 1;          // 128-channel weight tiles per CTA
 };
 
-static size_t gemm_smem(int bits, int bn, int stages) {
-  const size_t stage = 16384 + size_t(bn) * 128;
+static size_t gemm_smem(int bits, int bn, int stages, int wt = 1) {
+  const size_t stage = 16384 * size_t(wt) + size_t(bn) * 128;
   const size_t packed = bits == 4 ? ((size_t(128 + bn) * 64 + 1023) & ~size_t(1023)) : 0;
   // + 1 KB of staged token scales, + barriers and the TMEM address slot.
   return 1024 + stages * (stage + packed) + 1024 + (4 * stages + 1) * 8 + 16;
@@ -228,17 +229,9 @@ static bool plan_small_m(int bits, int64_t m, int ntiles, int num_kb, int max_sm
   return true;
 }
 
-// Picks the token tile, number of token tiles and the split-K cluster size
-// with a small cost model in SM cycles:
-//  * a 128 x BN x 128 K block costs max(347, 2 BN) MMA cycles (measured
-//    kind::i8 issue rate: N <= 128 has a fixed ~87-cycle MMA, full rate is
-//    8192 MAC/clk/SM);
-//  * its operands (16 KB of weights + 128 BN bytes) arrive at the CTA's share
-//    of HBM (~3400 B/clk for weights streamed once, single token tile) or of
-//    L2 (~9000 B/clk when several token tiles re-read the weights);
-//  * each CTA pays ~3000 cycles of launch, prologue and epilogue, +1500 for
-//    the cluster reduction of split-K;
-//  * CTAs under ~113 KB of shared memory run two per SM.
+// Picks the token tile, the number of token tiles, the split-K cluster size,
+// the stage count and the weight tiles per CTA (small M: plan_small_m;
+// larger M: the cost model below).
 static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
                           int sms, int max_smem) {
   const int ntiles = int((npad + 127) / 128);
@@ -246,52 +239,165 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
   GemmPlan best{0, 0, 0, 0, 0};   // smem == 0 marks "no plan"
   if (m <= 64 && plan_small_m(bits, m, ntiles, num_kb, max_smem, &best))
     return best;
+  // Larger M.  Measured on B200 (per-CTA clock traces): a K block of a CTA
+  // costs max(L / stages, MMA time) with the TMA round trip L ~ 2,700 SM
+  // cycles, the MMA time per 128-channel weight tile max(347, 2 BN) cycles
+  // (shared by the CTAs resident on an SM), plus ~4,200 cycles of prologue
+  // and pipeline fill and ~16 cycles per token column and weight tile of
+  // epilogue; a second wave adds ~6,000 cycles.  Two weight tiles per CTA
+  // (int8 only) double the MMA work per staged activation byte.  Split-K is
+  // kept for small token tiles only (its reduction costs more than it saves
+  // with BN > 64).
+  const double kRoundTrip = 2700.0;
   double best_cost = 1e30;
-  // One token tile up to 256 tokens (weights streamed once); larger M also
-  // tries 1-3 extra tiles to balance the waves.
   const int mt0 = int((m + 255) / 256);
-  const int mt1 = m <= 256 ? mt0 : mt0 + 3;
-  for (int mt = mt0; mt <= mt1; ++mt) {
-    int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
+  for (int mt = mt0; mt <= mt0 + 3; ++mt) {
+    const int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
     if (bn > 256 || bn < 16)
       continue;
     if (int64_t(mt - 1) * bn >= m)
       continue;  // an empty token tile
-    const int budget = (mt == 1 && bn <= 64) ? std::min(max_smem, kCoResidentSmem) : max_smem;
-    const int stages = stages_for(bits, bn, budget);
-    const size_t smem = gemm_smem(bits, bn, stages);
-    if (smem > size_t(max_smem))
-      continue;
-    // Split-K reuses the stage buffers for the int32 partial tile and the
-    // rank's bf16 staging slice.
-    const bool split_fits =
-        size_t(stages) * (16384 + size_t(bn) * 128) >= size_t(bn) * (512 + 128);
-    const int per_sm = smem <= 113 * 1024 ? 2 : 1;
-    const double scale = bits == 4 ? 0.5 : 1.0;
-    const double w_bytes = 16384.0 * scale;     // weight tile per K block
-    const double a_bytes = 128.0 * bn * scale;  // token tile per K block
-    for (int s = 1; s <= 8; s *= 2) {
-      if (s > num_kb || (s > 1 && !split_fits))
-        break;
-      const int ctas = ntiles * mt * s;
-      const int slots = sms * per_sm;
-      const int waves = (ctas + slots - 1) / slots;
-      const int active = std::min(ctas, slots);
-      // Weights come from HBM once (single token tile) or from L2; token
-      // tiles are L2-resident.  Per-SM fill rate is capped at 128 B/clk.
-      const double w_bw = std::min(128.0, (mt == 1 ? 3400.0 : 9000.0) / active);
-      const double a_bw = std::min(128.0, 9000.0 / active);
-      const double kb = double(num_kb) / s;
-      const double per_kb = std::max(std::max(347.0, 2.0 * bn), w_bytes / w_bw + a_bytes / a_bw);
-      const double per_cta = kb * per_kb + 3000.0 + (s > 1 ? 1500.0 : 0.0);
-      const double cost = waves * per_cta;
-      if (cost < best_cost * 0.999) {
-        best_cost = cost;
-        best = GemmPlan{bn, mt, s, stages, smem};
+    for (int wt = 1; wt <= (bits == 8 ? 2 : 1); ++wt) {
+      // Two weight tiles need at least three stages (which also keeps the
+      // CTA alone on its SM).
+      if (wt == 2 && gemm_smem(bits, bn, 3, 2) > size_t(max_smem))
+        continue;
+      int st = stages_for(bits, bn, max_smem, 8);
+      while (st > 2 && gemm_smem(bits, bn, st, wt) > size_t(max_smem))
+        --st;
+      const size_t smem = gemm_smem(bits, bn, st, wt);
+      if (smem > size_t(max_smem))
+        continue;
+      const int acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+      int per_sm = std::min(2, int(size_t(max_smem) / smem));
+      if (acc_cols * wt > 256)
+        per_sm = 1;   // the CTA holds all 512 TMEM columns
+      per_sm = std::max(per_sm, 1);
+      const bool split_fits =
+          wt == 1 && bn <= 64 &&
+          size_t(st) * (16384 + size_t(bn) * 128) >= size_t(bn) * (512 + 128);
+      const int ntw = (ntiles + wt - 1) / wt;
+      for (int s = 1; s <= 8; s *= 2) {
+        if (s > num_kb || (s > 1 && !split_fits))
+          break;
+        const int ctas = ntw * mt * s;
+        const int slots = sms * per_sm;
+        const int waves = (ctas + slots - 1) / slots;
+        const int active = std::min(per_sm, (ctas + sms - 1) / sms);
+        const double mma = double(active) * wt * std::max(347.0, 2.0 * bn);
+        const double per_kb = std::max(kRoundTrip / st, mma);
+        const double per_cta = 4200.0 + (double(num_kb) / s) * per_kb + 16.0 * wt * bn +
+                               (s > 1 ? 1500.0 : 0.0);
+        const double cost = waves * per_cta + (waves - 1) * 6000.0;
+        if (cost < best_cost * 0.999) {
+          best_cost = cost;
+          best = GemmPlan{bn, mt, s, st, smem, wt};
+        }
       }
     }
   }
   return best;
+}
+
+// Plan with two weight tiles per CTA and no split-K (the SwiGLU epilogue):
+// the token tiling of the larger-M model above, restricted to wt = 2.
+static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, int max_smem) {
+  const int ntw = int((npad + 255) / 256);
+  const int num_kb = int(kpad / 128);
+  GemmPlan best{0, 0, 0, 0, 0};
+  double best_cost = 1e30;
+  const int mt0 = int((m + 255) / 256);
+  for (int mt = mt0; mt <= mt0 + 3; ++mt) {
+    const int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
+    if (bn > 256 || bn < 16 || int64_t(mt - 1) * bn >= m)
+      continue;
+    int st = 8;
+    while (st > 3 && gemm_smem(8, bn, st, 2) > size_t(max_smem))
+      --st;
+    const size_t smem = gemm_smem(8, bn, st, 2);
+    if (smem > size_t(max_smem))
+      continue;
+    const int ctas = ntw * mt;
+    const int waves = (ctas + sms - 1) / sms;
+    const double per_kb = std::max(2700.0 / st, 2.0 * std::max(347.0, 2.0 * bn));
+    const double cost = waves * (4200.0 + num_kb * per_kb + 32.0 * bn) + (waves - 1) * 6000.0;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = GemmPlan{bn, mt, 1, st, smem, 2};
+    }
+  }
+  return best;
+}
+
+// Tensor maps, arguments and launch of one planned integer GEMM.  `n_store`
+// is the number of output columns (half the weight rows for SwiGLU).
+static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, const void *qw,
+                       const float *sw, const void *bias, int bias_mode, const void *out_lut,
+                       const void *residual, int64_t ldr, const void *silu_lut, int bits,
+                       int64_t m, int64_t npad, int64_t kpad, void *out, int64_t ldo,
+                       int64_t n_store, void *stream) {
+  const uint64_t row_bytes = bits == 8 ? uint64_t(kpad) : uint64_t(kpad / 2);
+  const uint32_t box_cols = bits == 8 ? 128u : 64u;
+  CUtensorMap tm_w, tm_a;
+  if (int r = make_map(&tm_w, qw, row_bytes, uint64_t(npad), row_bytes,
+                       box_cols, 128u, bits == 8))
+    return r;
+  if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, box_cols,
+                       uint32_t(plan.bn), bits == 8))
+    return r;
+  GemmArgs args;
+  args.sa = sa;
+  args.sw = sw;
+  args.bias = bias_mode == PIR2B_BIAS_ADD
+                  ? static_cast<const __nv_bfloat16 *>(bias)
+                  : nullptr;
+  args.out_lut = static_cast<const __nv_bfloat16 *>(out_lut);
+  args.residual = static_cast<const __nv_bfloat16 *>(residual);
+  args.ldr = ldr;
+  args.out = static_cast<__nv_bfloat16 *>(out);
+  args.ldo = ldo;
+  args.m = int(m);
+  args.n_store = int(n_store);
+  args.num_kb = int(kpad / 128);
+  args.bias_mode = bias_mode;
+  args.bn = plan.bn;
+  args.stages = plan.stages;
+  args.splits = plan.splits;
+  args.wt = plan.wt;
+  args.silu_lut = static_cast<const __nv_bfloat16 *>(silu_lut);
+  // The epilogue stages the tile (or, with split-K, each cluster rank's
+  // channel slice) in shared memory and writes it with one TMA store when
+  // the output rows are 16-byte aligned; otherwise it stores directly.
+  args.tma_store = (ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  CUtensorMap tm_out;
+  memset(&tm_out, 0, sizeof(tm_out));
+  if (args.tma_store) {
+    if (int r = make_out_map(&tm_out, out, uint64_t(n_store), uint64_t(m),
+                             uint64_t(ldo), uint32_t(plan.bn),
+                             uint32_t(128 / plan.splits)))
+      return r;
+  }
+
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(unsigned((npad + 128 * plan.wt - 1) / (128 * plan.wt)),
+                     unsigned(plan.mtiles), unsigned(plan.splits));
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = unsigned(plan.splits);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e =
+      bits == 8 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, tm_out, args)
+                : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, tm_out, args);
+  return cuda_status(e, "gemm launch");
 }
 
 } // namespace pir2b
@@ -497,66 +603,8 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
       plan.smem > size_t(dev->max_smem))
     return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",
                 (long long)m, (long long)npad, (long long)kpad);
-  const uint64_t row_bytes = bits == 8 ? uint64_t(kpad) : uint64_t(kpad / 2);
-  const uint32_t box_cols = bits == 8 ? 128u : 64u;
-  CUtensorMap tm_w, tm_a;
-  if (int r = make_map(&tm_w, qw, row_bytes, uint64_t(npad), row_bytes,
-                       box_cols, 128u, bits == 8))
-    return r;
-  if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, box_cols,
-                       uint32_t(plan.bn), bits == 8))
-    return r;
-  GemmArgs args;
-  args.sa = sa;
-  args.sw = sw;
-  args.bias = bias_mode == PIR2B_BIAS_ADD
-                  ? static_cast<const __nv_bfloat16 *>(bias)
-                  : nullptr;
-  args.out_lut = static_cast<const __nv_bfloat16 *>(out_lut);
-  args.residual = static_cast<const __nv_bfloat16 *>(residual);
-  args.ldr = ldr;
-  args.out = static_cast<__nv_bfloat16 *>(out);
-  args.ldo = ldo;
-  args.m = int(m);
-  args.n_store = int(n_store);
-  args.num_kb = int(kpad / 128);
-  args.bias_mode = bias_mode;
-  args.bn = plan.bn;
-  args.stages = plan.stages;
-  args.splits = plan.splits;
-  // The epilogue stages the tile (or, with split-K, each cluster rank's
-  // channel slice) in shared memory and writes it with one TMA store when
-  // the output rows are 16-byte aligned; otherwise it stores directly.
-  args.tma_store = (ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
-  CUtensorMap tm_out;
-  memset(&tm_out, 0, sizeof(tm_out));
-  if (args.tma_store) {
-    if (int r = make_out_map(&tm_out, out, uint64_t(n_store), uint64_t(m),
-                             uint64_t(ldo), uint32_t(plan.bn),
-                             uint32_t(128 / plan.splits)))
-      return r;
-  }
-
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(unsigned((npad + 127) / 128), unsigned(plan.mtiles),
-                     unsigned(plan.splits));
-  cfg.blockDim = dim3(192, 1, 1);
-  cfg.dynamicSmemBytes = plan.smem;
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = unsigned(plan.splits);
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  cudaError_t e =
-      bits == 8 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, tm_out, args)
-                : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, tm_out, args);
-  return cuda_status(e, "gemm launch");
+  return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, out_lut, residual, ldr, nullptr,
+                     bits, m, npad, kpad, out, ldo, n_store, stream);
 }
 
 int pir2b_qk_norm_rope(const void *qkv, int64_t ld, const void *q_weight,
@@ -718,12 +766,45 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
                      "gemm_nvfp4 launch");
 }
 
+int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const float *sw,
+                      const void *bias, int bias_mode, const void *silu_lut, int64_t m,
+                      int64_t half_n, int64_t kpad, void *out, int64_t ldo, void *stream) {
+  if (bias_mode < 0 || bias_mode > 2)
+    return fail(PIR2B_EINVAL, "bias_mode must be 0, 1 or 2");
+  if (m < 1 || m > 0x7fffffffLL || half_n < 128 || half_n % 128 != 0 ||
+      half_n > (1LL << 28) || kpad < 128 || kpad % 128 != 0 || kpad > (1LL << 20))
+    return fail(PIR2B_EINVAL,
+                "SwiGLU GEMM requires m >= 1, half_n %% 128 == 0 and kpad %% 128 == 0");
+  if (ldo < half_n)
+    return fail(PIR2B_EINVAL, "ldo must be >= half_n");
+  if (qa == nullptr || sa == nullptr || qw == nullptr || sw == nullptr || out == nullptr ||
+      silu_lut == nullptr)
+    return fail(PIR2B_EINVAL, "SwiGLU GEMM operands must be non-null");
+  if (bias_mode == PIR2B_BIAS_ADD && bias == nullptr)
+    return fail(PIR2B_EINVAL, "bias_mode ADD needs a bias vector");
+  if (!aligned(qa, 16) || !aligned(qw, 16))
+    return fail(PIR2B_EALIGN, "packed operands must be 16-byte aligned");
+  if (!aligned(out, 2) || !aligned(sa, 4) || !aligned(sw, 4) || (bias && !aligned(bias, 2)) ||
+      !aligned(silu_lut, 2))
+    return fail(PIR2B_EALIGN, "scale/bias/output alignment not met");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  const GemmPlan plan = plan_gemm_wide(m, 2 * half_n, kpad, dev->sms, dev->max_smem);
+  if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m)
+    return fail(PIR2B_EINVAL, "no SwiGLU tile plan fits m=%lld kpad=%lld", (long long)m,
+                (long long)kpad);
+  return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, nullptr, nullptr, 0, silu_lut, 8, m,
+                     2 * half_n, kpad, out, ldo, half_n, stream);
+}
+
 // Plan introspection for tests and the benchmark (not part of the public
 // header's contract; exported for diagnostics).
 int pir2b_gemm_plan(int bits, int64_t m, int64_t npad, int64_t kpad,
                     int sms, int *bn, int *mtiles, int *splits, int *stages,
-                    int64_t *smem) {
+                    int64_t *smem, int *wt) {
   const GemmPlan p = plan_gemm(bits, m, npad, kpad, sms, 232448);
+  *wt = p.wt;
   *bn = p.bn;
   *mtiles = p.mtiles;
   *splits = p.splits;

@@ -127,7 +127,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int bn = args.bn;
   const int stages = args.stages;
-  const int op_a_bytes = kWeightTileBytes;        // unpacked int8 weight tile
+  // wt = 2 (int8, no split-K): two 128-channel weight tiles share each token
+  // tile, two TMEM accumulators, twice the MMA work per staged byte.
+  const int wt = kBits == 8 ? args.wt : 1;
+  const int op_a_bytes = wt * kWeightTileBytes;   // unpacked int8 weight tile(s)
   const int op_b_bytes = bn * kBlockK;            // unpacked int8 token tile
   const int stage_bytes = op_a_bytes + op_b_bytes;
   // W4A4 keeps the packed TMA destination next to the unpacked operands.
@@ -144,13 +147,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTileN;
+  const int n0 = blockIdx.x * kTileN * wt;
   const int m0 = blockIdx.y * bn;
   const int split = blockIdx.z;
   const int kb_begin = (split * args.num_kb) / args.splits;
   const int kb_end = ((split + 1) * args.num_kb) / args.splits;
   const int nkb = kb_end - kb_begin;
-  const uint32_t tmem_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+  const uint32_t acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+  const uint32_t tmem_cols = acc_cols * uint32_t(wt);   // second accumulator at acc_cols
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -197,6 +201,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                                   : packed_base + i * packed_stride;
         tma_load_2d_hint(dst, &tm_w, &full[i], (kb_begin + i) * kstep, n0,
                          wpolicy);
+        if (wt == 2)
+          tma_load_2d_hint(dst + kWeightTileBytes, &tm_w, &full[i], (kb_begin + i) * kstep,
+                           n0 + kTileN, wpolicy);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
@@ -214,6 +221,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (kBits == 8) {
           uint8_t *a = smem + s * stage_bytes;
           tma_load_2d_hint(a, &tm_w, &full[s], kx, n0, wpolicy);
+          if (wt == 2)
+            tma_load_2d_hint(a + kWeightTileBytes, &tm_w, &full[s], kx, n0 + kTileN, wpolicy);
           tma_load_2d(a + op_a_bytes, &tm_a, &full[s], kx, m0);
         } else {
           uint8_t *p = packed_base + s * packed_stride;
@@ -242,6 +251,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           mma_i8(tmem_base, smem_desc_sw128(a_addr + k * 32),
                  smem_desc_sw128(b_addr + k * 32), idesc,
                  (i > 0 || k > 0) ? 1u : 0u);
+          if (wt == 2)
+            mma_i8(tmem_base + acc_cols, smem_desc_sw128(a_addr + kWeightTileBytes + k * 32),
+                   smem_desc_sw128(b_addr + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
         }
         mma_commit(&empty[s]);
       }
@@ -279,58 +291,101 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int valid_m = min(bn, args.m - m0);
     const uint32_t lane_addr = tmem_base + (uint32_t(quarter * 32) << 16);
     if (have_acc) {
-      if (args.splits == 1) {
-        const bool in_range = c < args.n_store;
-        const float sw = in_range ? __ldg(args.sw + c) : 0.f;
-        const float b = (args.bias_mode == 2 && in_range)
-                            ? __bfloat162float(args.bias[c])
-                            : 0.f;
-        const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
-        // Staging tile [bn tokens][128 channels] bf16 in the idle stage
-        // buffers, written out by one TMA store.
-        __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem);
+      if (args.silu_lut != nullptr && wt == 2) {
+        // SwiGLU: gate (accumulator 0) and up (accumulator 1) of the same
+        // 128 output channels meet in this thread: h = bf16(silu(g) * u)
+        // with silu(g) from the torch-built table, exactly the gated pack's
+        // value (coexecution/kernels/ampere_ada/integer.py:27-48).
+        const uint16_t *silu = reinterpret_cast<const uint16_t *>(args.silu_lut);
         const int bias_mode = args.bias_mode;
         const bool tma = args.tma_store != 0;
-        const bool with_res = args.residual != nullptr;
+        const int co = blockIdx.x * kTileN + ch;          // output channel
+        const bool in_range = co < args.n_store;
+        const float sw_g = in_range ? __ldg(args.sw + c) : 0.f;
+        const float sw_u = in_range ? __ldg(args.sw + c + kTileN) : 0.f;
+        const float b_g = (bias_mode == 2 && in_range) ? __bfloat162float(args.bias[c]) : 0.f;
+        const float b_u = (bias_mode == 2 && in_range) ? __bfloat162float(args.bias[c + kTileN]) : 0.f;
+        __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem);
         for (int j0 = 0; j0 < bn; j0 += 16) {
-          // 16 token columns per step: bn is a multiple of 16.
-          uint32_t r[16];
-          tmem_ld_16(lane_addr + j0, r);
-          float res[16];
-          if (with_res) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              res[i] = (in_range && j0 + i < valid_m)
-                           ? __bfloat162float(args.residual[int64_t(m0 + j0 + i) * args.ldr + c])
-                           : 0.f;
-          }
+          uint32_t rg[16], ru[16];
+          tmem_ld_16(lane_addr + j0, rg);
+          tmem_ld_16(lane_addr + acc_cols + j0, ru);
           tmem_ld_wait();
-          __nv_bfloat16 o[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            o[i] = epilogue_value(int(r[i]), s_sa[j0 + i], sw, b, bias_mode, lut);
-          if (with_res) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              o[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o[i]), res[i]));
-          }
-          if (tma) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              stage[(j0 + i) * kTileN + ch] = o[i];
-          } else if (in_range) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (j0 + i < valid_m)
-                args.out[int64_t(m0 + j0 + i) * args.ldo + c] = o[i];
+          for (int i = 0; i < 16; ++i) {
+            const __nv_bfloat16 g = epilogue_value(int(rg[i]), s_sa[j0 + i], sw_g, b_g, bias_mode, nullptr);
+            const __nv_bfloat16 u = epilogue_value(int(ru[i]), s_sa[j0 + i], sw_u, b_u, bias_mode, nullptr);
+            const float sg = __bfloat162float(__ushort_as_bfloat16(__ldg(silu + __bfloat16_as_ushort(g))));
+            const __nv_bfloat16 h = __float2bfloat16_rn(__fmul_rn(sg, __bfloat162float(u)));
+            if (tma)
+              stage[(j0 + i) * kTileN + ch] = h;
+            else if (in_range && j0 + i < valid_m)
+              args.out[int64_t(m0 + j0 + i) * args.ldo + co] = h;
           }
         }
-        if (args.tma_store) {
+        if (tma) {
           fence_proxy_async_smem();
           named_barrier(1, 128);
           if (et == 0) {
-            tma_store_2d(&tm_out, stage, n0, m0);
+            tma_store_2d(&tm_out, stage, blockIdx.x * kTileN, m0);
             tma_store_commit_and_wait();
+          }
+        }
+      } else if (args.splits == 1) {
+        const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
+        const int bias_mode = args.bias_mode;
+        const bool tma = args.tma_store != 0;
+        const bool with_res = args.residual != nullptr;
+        for (int w = 0; w < wt; ++w) {
+          const int cw = c + w * kTileN;            // channel of accumulator w
+          const bool in_range = cw < args.n_store;
+          const float sw = in_range ? __ldg(args.sw + cw) : 0.f;
+          const float b = (bias_mode == 2 && in_range) ? __bfloat162float(args.bias[cw]) : 0.f;
+          const uint32_t acc_addr = lane_addr + uint32_t(w) * acc_cols;
+          // Staging tile [bn tokens][128 channels] bf16 per accumulator in
+          // the idle stage buffers, written out by one TMA store each.
+          __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem) + size_t(w) * bn * kTileN;
+          for (int j0 = 0; j0 < bn; j0 += 16) {
+            // 16 token columns per step: bn is a multiple of 16.
+            uint32_t r[16];
+            tmem_ld_16(acc_addr + j0, r);
+            float res[16];
+            if (with_res) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                res[i] = (in_range && j0 + i < valid_m)
+                             ? __bfloat162float(args.residual[int64_t(m0 + j0 + i) * args.ldr + cw])
+                             : 0.f;
+            }
+            tmem_ld_wait();
+            __nv_bfloat16 o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              o[i] = epilogue_value(int(r[i]), s_sa[j0 + i], sw, b, bias_mode, lut);
+            if (with_res) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                o[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o[i]), res[i]));
+            }
+            if (tma) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                stage[(j0 + i) * kTileN + ch] = o[i];
+            } else if (in_range) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (j0 + i < valid_m)
+                  args.out[int64_t(m0 + j0 + i) * args.ldo + cw] = o[i];
+            }
+          }
+          if (tma) {
+            fence_proxy_async_smem();
+            named_barrier(1, 128);
+            // A tile that starts past the stored width has nothing to write.
+            if (et == 0 && n0 + w * kTileN < args.n_store) {
+              tma_store_2d(&tm_out, stage, n0 + w * kTileN, m0);
+              tma_store_commit_and_wait();
+            }
           }
         }
       } else {

@@ -26,8 +26,9 @@ torch's bf16 addition does.
 
 import torch
 
+from . import ops
 from .connections import packed_input
-from .fused import prepare_gelu
+from .fused import prepare_gelu, prepare_silu
 from .linear import prepare
 from .modulation import prepare_norm_modulation
 
@@ -124,6 +125,63 @@ class ResidualFusion:
                 return self.controller.dispatch(down_q, hidden)
 
             block.forward = forward
+
+    def close(self):
+        for module, had, forward in self.saved:
+            if had:
+                module.forward = forward
+            elif "forward" in module.__dict__:
+                del module.forward
+        self.saved = []
+
+
+class SwiGLUFusion:
+    """gate|up GEMM with the SwiGLU epilogue for the Qwen3 text MLPs (W8A8).
+
+    TransformerINT runs a text MLP as one gate|up group GEMM followed by the
+    down projection's gated pack bf16(SiLU(gate) * up) (piR2's
+    coexecution/optimization/groot/integer.py:166-172).  Here the gate|up
+    GEMM itself writes bf16(SiLU(gate) * up) (the same torch-built SiLU
+    table, the same rounding), half as many output bytes, and the down
+    projection packs it plainly: activation codes, and so the results, are
+    bitwise those of the unfused path.  The group's weights, scales and bias
+    are copied once into the kernel's interleaved layout (128-channel gate
+    and up blocks side by side).
+    """
+
+    def __init__(self, model, controller):
+        self.controller = controller
+        self.saved = []
+        self.sites = []
+        names = {id(m): n for n, (m, _, _) in controller.sites.items()}
+        groups = {tuple(n): g for n, g in controller.grouped[8]}
+        for mlp, down in controller.text:
+            key = (names.get(id(mlp.gate_proj)), names.get(id(mlp.up_proj)))
+            group = groups.get(key)
+            if group is None or group.sizes[0] != group.sizes[1] or group.sizes[0] % 128:
+                continue
+            half = group.sizes[0]
+            linear = group.linear
+            weight = ops.interleave_gate_up(linear.packed_weight[: 2 * half], half)
+            scale = ops.interleave_gate_up(linear.weight_scale[: 2 * half], half)
+            bias = None if linear.bias is None else ops.interleave_gate_up(linear.bias[: 2 * half], half)
+            self.sites.append((mlp, controller.quant[8][down], half, weight, scale, bias, linear._bias_mode()))
+        device = next(model.parameters()).device
+        self.silu = prepare_silu(device)
+
+    def set(self):
+        self.close()
+        for mlp, down_q, half, weight, scale, bias, bias_mode in self.sites:
+            self.saved.append((mlp, "forward" in mlp.__dict__, mlp.__dict__.get("forward")))
+
+            def forward(x, down_q=down_q, half=half, weight=weight, scale=scale, bias=bias, bias_mode=bias_mode):
+                packed = x.for_bits(8) if getattr(x, "_robotics_packed_input", False) else prepare(x, 8)
+                hidden = ops.gemm_swiglu(
+                    packed.data, packed.scales, weight, scale, bias, self.silu, half_n=half, bias_mode=bias_mode
+                )
+                return self.controller.dispatch(down_q, hidden.reshape(*packed.shape, half))
+
+            mlp.forward = forward
 
     def close(self):
         for module, had, forward in self.saved:

@@ -183,6 +183,40 @@ def gemm(a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, residual=Non
     return out
 
 
+def interleave_gate_up(t, half):
+    """Reorders the rows of a gate|up group tensor ([2*half, ...] or [2*half])
+    into 128-row blocks gate_j, up_j (the SwiGLU GEMM's weight layout)."""
+    if t.shape[0] != 2 * half or half % 128:
+        raise ValueError("gate|up interleave needs 2*half rows with half % 128 == 0")
+    g, u = t[:half], t[half:]
+    parts = torch.stack((g.reshape(half // 128, 128, *t.shape[1:]), u.reshape(half // 128, 128, *t.shape[1:])), 1)
+    return parts.reshape(t.shape).contiguous()
+
+
+def gemm_swiglu(a, sa, w, sw, bias, silu_lut, *, half_n, bias_mode=None, out=None):
+    """W8A8 gate|up GEMM writing bf16(silu(gate) * up) [m, half_n]; w, sw
+    and bias in the interleaved layout of `interleave_gate_up`."""
+    m = a.shape[0]
+    k_pad = a.shape[1]
+    if w.dtype != torch.int8 or w.shape[1] != k_pad or w.shape[0] != 2 * half_n:
+        raise ValueError("SwiGLU GEMM needs int8 weights [2*half_n, Kpad] matching the activations")
+    if bias_mode is None:
+        bias_mode = _lib.BIAS_NONE if bias is None else _lib.BIAS_ADD
+    if out is None:
+        out = torch.empty((m, half_n), device=a.device, dtype=torch.bfloat16)
+    recorder = launch_recorder
+    if recorder is not None:
+        recorder.before(a.device)
+    status = _lib.lib().pir2b_gemm_swiglu(
+        a.data_ptr(), sa.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias), bias_mode,
+        silu_lut.data_ptr(), m, half_n, k_pad, out.data_ptr(), out.stride(0), _stream(a.device),
+    )
+    _lib.check(status, "pir2b_gemm_swiglu")
+    if recorder is not None:
+        recorder.after(a.device, bits=8, m=m, n=2 * half_n, k=k_pad, npad=2 * half_n)
+    return out
+
+
 def pack_nvfp4(x):
     """NVFP4 pack of contiguous bf16 rows -> (packed [rows, k/2], swizzled sf)."""
     data, scales, _ = norm_quant_rows(x.reshape(-1, x.shape[-1]).contiguous(), _lib.OUT_NVFP4)

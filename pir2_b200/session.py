@@ -56,6 +56,7 @@ class GrootOptimizations:
         self.residual = None
         self.pointwise = None
         self.attention = None
+        self.swiglu = None
         self.floating = None
         self._active = False
         self._configuration_file_hashes = {}
@@ -166,6 +167,12 @@ class GrootOptimizations:
                 self.residual = ResidualFusion(model, self.controller)
                 self.stack.callback(self.residual.close)
                 self.residual.set({"w8a8": 8, "w4a4": 4}[self.config.precision])
+            if self.config.precision == "w8a8":
+                from .fusion import SwiGLUFusion
+
+                self.swiglu = SwiGLUFusion(model, self.controller)
+                self.stack.callback(self.swiglu.close)
+                self.swiglu.set()
             if self.config.fusion_mode in ("all", "rope_rms"):
                 from .pointwise import TextAttentionFusion
 

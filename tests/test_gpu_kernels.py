@@ -123,6 +123,11 @@ GEMM_SHAPES = [
     (544, 2048, 4096),
     (1024, 2048, 2048),
     (1088, 1536, 6144),
+    # two weight tiles per CTA: the last CTA's second tile partly or wholly
+    # beyond N (47 / 95 / 71 channel tiles)
+    (1088, 1536, 6000),
+    (544, 256, 12040),
+    (700, 512, 9000),
 ]
 
 
@@ -292,7 +297,7 @@ def test_qk_norm_rope_matches_torch():
 
 def test_gemm_residual_epilogue_bitwise():
     g = torch.Generator().manual_seed(41)
-    for m, k, n in ((17, 1536, 1536), (544, 2048, 2048), (64, 6144, 2048)):
+    for m, k, n in ((17, 1536, 1536), (544, 2048, 2048), (64, 6144, 2048), (700, 512, 9000)):
         _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, n, 8)
         residual = randn_bf16(g, m, n)
         out = ops.gemm(
@@ -355,3 +360,26 @@ def test_attention_rows_strided_query_and_argument_errors():
     long_kv = torch.zeros(20000, 2 * w, device="cuda", dtype=torch.bfloat16)   # keys exceed shared memory
     with pytest.raises(ValueError):
         ops.attention_rows(q, long_kv[:, :w], long_kv[:, w:], batch=1, heads=heads, head_dim=d)
+
+
+@pytest.mark.parametrize("m,k,half", [(544, 2048, 6144), (17, 1536, 256), (300, 256, 384)])
+def test_gemm_swiglu_bitwise(m, k, half):
+    """gate|up GEMM with the SwiGLU epilogue == the gated pack's value
+    bf16(silu_lut[gate] * up) of the two exact GEMM outputs."""
+    from pir2_b200.fused import prepare_silu
+
+    g = torch.Generator().manual_seed(m + k + half)
+    _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, 2 * half, 8)
+    lut = prepare_silu(torch.device("cuda"))
+    y = oracle.gemm_epilogue(oracle.int_matmul(qa, qw), sa, sw, bits_of(b), 2)[:, : 2 * half]
+    gate = oracle.bf16_bits_to_f32(y[:, :half])
+    up = oracle.bf16_bits_to_f32(y[:, half:])
+    silu = oracle.bf16_bits_to_f32(bits_of(lut.cpu())[y[:, :half]])
+    ref = oracle.f32_to_bf16_bits((silu * up).astype(np.float32))
+    del gate
+    cat = lambda t: ops.interleave_gate_up(t, half)   # noqa: E731
+    out = ops.gemm_swiglu(
+        torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), cat(torch.from_numpy(qw).cuda()),
+        cat(torch.from_numpy(sw).cuda()), cat(b.cuda()), lut, half_n=half,
+    )
+    assert np.array_equal(bits_of(out), ref)

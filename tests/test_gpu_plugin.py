@@ -273,3 +273,32 @@ def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits):
     finally:
         fusion.close()
         adapter.close()
+
+
+@torch.inference_mode()
+def test_swiglu_epilogue_fusion_is_bitwise():
+    """Text MLP through the SwiGLU GEMM epilogue == the unfused W8A8 MLP
+    (group GEMM + gated SiLU pack), bit for bit, and restores."""
+    from pir2_b200.fusion import SwiGLUFusion
+    from pir2_b200.harness import DiTConfig, VLMConfig, build_policy
+
+    policy = build_policy("cuda", dit=DiTConfig(layers=2), vlm=VLMConfig(layers=2, vocab=2048))
+    names = inventory(policy)[0]
+    executed = {n for n in names if n.startswith("backbone.layers")}
+    adapter = TransformerINT(policy, executed, native=True, expanded=True)
+    fusion = SwiGLUFusion(policy, adapter)
+    assert len(fusion.sites) == 2
+    torch.manual_seed(9)
+    x = torch.randn(1, 544, 2048, device="cuda", dtype=torch.bfloat16)
+    try:
+        adapter.set("w8a8")
+        mlps = [layer.mlp for layer in policy.backbone.layers]
+        refs = [mlp(x) for mlp in mlps]
+        fusion.set()
+        for mlp, ref in zip(mlps, refs):
+            equal(mlp(x), ref)
+        fusion.close()
+        equal(mlps[0](x), refs[0])
+    finally:
+        fusion.close()
+        adapter.close()

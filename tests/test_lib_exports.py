@@ -53,7 +53,7 @@ def test_argument_errors_are_reported_without_touching_the_device():
 
 
 def _plan(lib, bits, m, npad, kpad):
-    out = [ctypes.c_int() for _ in range(4)] + [ctypes.c_int64()]
+    out = [ctypes.c_int() for _ in range(4)] + [ctypes.c_int64(), ctypes.c_int()]
     status = lib.pir2b_gemm_plan(bits, m, npad, kpad, 148, *[ctypes.byref(v) for v in out])
     return status, [v.value for v in out]
 
@@ -68,11 +68,12 @@ def test_gemm_planner_always_returns_a_launchable_plan():
         for m in (1, 2, 15, 16, 17, 33, 64, 65, 128, 200, 256, 257, 300, 544, 1024, 1088, 4096):
             for k in (128, 256, 1536, 2048, 6144):
                 for n in (8, 64, 520, 1536, 2048, 4096, 6144, 12288, 52224):
-                    status, (bn, mt, splits, stages, smem) = _plan(lib, bits, m, n, k)
+                    status, (bn, mt, splits, stages, smem, wt) = _plan(lib, bits, m, n, k)
                     assert status == 0, (bits, m, k, n)
                     assert bn % 16 == 0 and 16 <= bn <= 256
                     assert bn * mt >= m and bn * (mt - 1) < m
                     assert splits in (1, 2, 4, 8) and splits <= k // 128
                     assert 2 <= stages <= 12 and 0 < smem <= 232448
+                    assert wt in (1, 2) and (wt == 1 or (bits == 8 and splits == 1 and stages >= 3))
                     if splits > 1:
                         assert stages * (16384 + bn * 128) >= bn * (512 + 128)
