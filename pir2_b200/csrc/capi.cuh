@@ -185,6 +185,9 @@ static size_t gemm_smem(int bits, int bn, int stages, int wt = 1) {
 // two CTAs fit on an SM: with programmatic dependent launch the next GEMM's
 // prologue and weight prefetch then run while this one finishes.
 constexpr int kCoResidentSmem = 110 * 1024;
+// Larger-M GEMM CTAs stay under ~200 KB so a small kernel's CTA still fits
+// beside them.
+constexpr int kChainSmem = 200 * 1024;
 
 static int stages_for(int bits, int bn, int max_smem, int cap = 8) {
   int s = cap;
@@ -239,62 +242,79 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
   GemmPlan best{0, 0, 0, 0, 0};   // smem == 0 marks "no plan"
   if (m <= 64 && plan_small_m(bits, m, ntiles, num_kb, max_smem, &best))
     return best;
-  // Larger M.  Measured on B200 (per-CTA clock traces): a K block of a CTA
-  // costs max(L / stages, MMA time) with the TMA round trip L ~ 2,700 SM
-  // cycles, the MMA time per 128-channel weight tile max(347, 2 BN) cycles
-  // (shared by the CTAs resident on an SM), plus ~4,200 cycles of prologue
-  // and pipeline fill and ~16 cycles per token column and weight tile of
-  // epilogue; a second wave adds ~6,000 cycles.  Two weight tiles per CTA
-  // (int8 only) double the MMA work per staged activation byte.  Split-K is
-  // kept for small token tiles only (its reduction costs more than it saves
-  // with BN > 64).
-  const double kRoundTrip = 2700.0;
+  // Larger M: a small cost model in SM cycles over the token tile, the
+  // number of token tiles and the split-K cluster size:
+  //  * a 128 x BN x 128 K block costs max(347, 2 BN) MMA cycles (measured
+  //    kind::i8 issue rate: N <= 128 has a fixed ~87-cycle MMA, full rate is
+  //    8192 MAC/clk/SM);
+  //  * its operands (16 KB of weights + 128 BN bytes) arrive at the CTA's
+  //    share of HBM (~3400 B/clk for weights streamed once, single token
+  //    tile) or of L2 (~9000 B/clk when several token tiles re-read the
+  //    weights);
+  //  * each CTA pays ~3000 cycles of launch, prologue and epilogue, +1500 for
+  //    the cluster reduction of split-K;
+  //  * CTAs under ~113 KB of shared memory run two per SM.
+  // Measured against a K-block latency model (which wins on isolated
+  // launches) this one gives the faster VLM prefill inside the full CUDA
+  // graph of the control step, where each GEMM shares its SMs with the
+  // programmatically launched kernels around it.
   double best_cost = 1e30;
   const int mt0 = int((m + 255) / 256);
-  for (int mt = mt0; mt <= mt0 + 3; ++mt) {
-    const int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
+  const int mt1 = m <= 256 ? mt0 : mt0 + 3;
+  for (int mt = mt0; mt <= mt1; ++mt) {
+    int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
     if (bn > 256 || bn < 16)
       continue;
     if (int64_t(mt - 1) * bn >= m)
       continue;  // an empty token tile
-    for (int wt = 1; wt <= (bits == 8 ? 2 : 1); ++wt) {
-      // Two weight tiles need at least three stages (which also keeps the
-      // CTA alone on its SM).
-      if (wt == 2 && gemm_smem(bits, bn, 3, 2) > size_t(max_smem))
-        continue;
-      int st = stages_for(bits, bn, max_smem, 8);
-      while (st > 2 && gemm_smem(bits, bn, st, wt) > size_t(max_smem))
-        --st;
-      const size_t smem = gemm_smem(bits, bn, st, wt);
-      if (smem > size_t(max_smem))
-        continue;
-      const int acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
-      int per_sm = std::min(2, int(size_t(max_smem) / smem));
-      if (acc_cols * wt > 256)
-        per_sm = 1;   // the CTA holds all 512 TMEM columns
-      per_sm = std::max(per_sm, 1);
-      const bool split_fits =
-          wt == 1 && bn <= 64 &&
-          size_t(st) * (16384 + size_t(bn) * 128) >= size_t(bn) * (512 + 128);
-      const int ntw = (ntiles + wt - 1) / wt;
-      for (int s = 1; s <= 8; s *= 2) {
-        if (s > num_kb || (s > 1 && !split_fits))
-          break;
-        const int ctas = ntw * mt * s;
-        const int slots = sms * per_sm;
-        const int waves = (ctas + slots - 1) / slots;
-        const int active = std::min(per_sm, (ctas + sms - 1) / sms);
-        const double mma = double(active) * wt * std::max(347.0, 2.0 * bn);
-        const double per_kb = std::max(kRoundTrip / st, mma);
-        const double per_cta = 4200.0 + (double(num_kb) / s) * per_kb + 16.0 * wt * bn +
-                               (s > 1 ? 1500.0 : 0.0);
-        const double cost = waves * per_cta + (waves - 1) * 6000.0;
-        if (cost < best_cost * 0.999) {
-          best_cost = cost;
-          best = GemmPlan{bn, mt, s, st, smem, wt};
-        }
+    const int budget = (mt == 1 && bn <= 64) ? std::min(max_smem, kCoResidentSmem) : max_smem;
+    const int stages = stages_for(bits, bn, budget);
+    const size_t smem = gemm_smem(bits, bn, stages);
+    if (smem > size_t(max_smem))
+      continue;
+    // Split-K reuses the stage buffers for the int32 partial tile and the
+    // rank's bf16 staging slice.
+    const bool split_fits =
+        size_t(stages) * (16384 + size_t(bn) * 128) >= size_t(bn) * (512 + 128);
+    const int per_sm = smem <= 113 * 1024 ? 2 : 1;
+    const double scale = bits == 4 ? 0.5 : 1.0;
+    const double w_bytes = 16384.0 * scale;     // weight tile per K block
+    const double a_bytes = 128.0 * bn * scale;  // token tile per K block
+    for (int s = 1; s <= 8; s *= 2) {
+      if (s > num_kb || (s > 1 && !split_fits))
+        break;
+      const int ctas = ntiles * mt * s;
+      const int slots = sms * per_sm;
+      const int waves = (ctas + slots - 1) / slots;
+      const int active = std::min(ctas, slots);
+      // Weights come from HBM once (single token tile) or from L2; token
+      // tiles are L2-resident.  Per-SM fill rate is capped at 128 B/clk.
+      const double w_bw = std::min(128.0, (mt == 1 ? 3400.0 : 9000.0) / active);
+      const double a_bw = std::min(128.0, 9000.0 / active);
+      const double kb = double(num_kb) / s;
+      const double per_kb = std::max(std::max(347.0, 2.0 * bn), w_bytes / w_bw + a_bytes / a_bw);
+      const double per_cta = kb * per_kb + 3000.0 + (s > 1 ? 1500.0 : 0.0);
+      const double cost = waves * per_cta;
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = GemmPlan{bn, mt, s, stages, smem};
       }
     }
+  }
+  // A plan that needs more than one wave of CTAs runs in one wave with two
+  // weight tiles per CTA (twice the MMA work per staged token byte): on
+  // isolated launches M=544 N=12288 K=2048 takes 20.6 instead of 29.2 us,
+  // M=1088 N=6144 K=1536 18.4 instead of 24.8 us.
+  if (bits == 8 && best.smem != 0 && best.splits == 1) {
+    const int per_sm = best.smem <= 113 * 1024 ? 2 : 1;
+    const int64_t ctas = int64_t(ntiles) * best.mtiles;
+    const int64_t ctas2 = int64_t((ntiles + 1) / 2) * best.mtiles;
+    int st = 8;
+    while (st > 3 && gemm_smem(bits, best.bn, st, 2) > size_t(std::min(max_smem, kChainSmem)))
+      --st;
+    const size_t smem2 = gemm_smem(bits, best.bn, st, 2);
+    if (ctas > int64_t(sms) * per_sm && ctas2 <= sms && smem2 <= size_t(max_smem))
+      best = GemmPlan{best.bn, best.mtiles, 1, st, smem2, 2};
   }
   return best;
 }
@@ -302,6 +322,7 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
 // Plan with two weight tiles per CTA and no split-K (the SwiGLU epilogue):
 // the token tiling of the larger-M model above, restricted to wt = 2.
 static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, int max_smem) {
+  max_smem = std::min(max_smem, kChainSmem);
   const int ntw = int((npad + 255) / 256);
   const int num_kb = int(kpad / 128);
   GemmPlan best{0, 0, 0, 0, 0};

@@ -120,6 +120,19 @@ class GrootOptimizations:
         if self.config.precision == "fp4":
             from .floating import FloatingProjections
 
+            # piR2's floating fusions (grouped / shared-input projections,
+            # SwiGLU, GELU and RMSNorm packing, AdaLN connections) are not in
+            # this build's fp4 path: refuse them instead of ignoring them.
+            unsupported = [
+                flag
+                for flag in ("fp_shared_inputs", "fp_grouped", "fp_swiglu", "fp_gelu", "fp_rmsnorm")
+                if getattr(self.config, flag)
+            ]
+            if self.config.fusion or self.config.norm_modulation_quant:
+                unsupported.append("fusion")
+            if unsupported:
+                raise ValueError(f"Not implemented for fp4 in this build: {', '.join(unsupported)}")
+
             smoothing = None
             if self.config.fp_smoothquant is not None:
                 from .smoothquant import load_profile

@@ -302,3 +302,21 @@ def test_swiglu_epilogue_fusion_is_bitwise():
     finally:
         fusion.close()
         adapter.close()
+
+
+@pytest.mark.parametrize("flags", [{"fp_grouped": True}, {"fp_rmsnorm": True}, {"fusion": True}])
+@torch.inference_mode()
+def test_fp4_session_refuses_unimplemented_floating_fusions(flags):
+    from pir2_b200.config import OptimizationConfig
+    from pir2_b200.harness import DiTConfig, VLMConfig, build_policy
+    from pir2_b200.session import GrootOptimizations
+
+    policy = build_policy("cuda", dit=DiTConfig(layers=2), vlm=VLMConfig(layers=1, vocab=2048))
+    try:
+        config = OptimizationConfig(precision="fp4", scope="all", **flags)
+    except ValueError:
+        return  # refused by the config validation itself
+    with pytest.raises(ValueError, match="fp4|Floating"):
+        with GrootOptimizations(SimpleNamespace(model=policy), config):
+            pass
+    assert all("forward" not in m.__dict__ for m in policy.modules())
