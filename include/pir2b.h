@@ -169,6 +169,31 @@ int pir2b_qk_norm_rope(const void *qkv, int64_t ld, const void *q_weight,
                        int head_dim, float eps, void *q_out, void *k_out,
                        void *v_out, void *stream);
 
+/* The W8A8 feed-forward half of a DiT block in one launch:
+ *   out = residual + down(pack(gelu(up(x))))
+ * with x the packed FFN input (int8 [m, d] codes + fp32 row scales, e.g. the
+ * norm3 pack), up weights int8 [f, d] (+ sw_up [f], bias_up [f]), the GELU
+ * table gelu_lut (torch-built, 65536 bf16), down weights int8 [d, f]
+ * (+ sw_down [d], bias_down [d]).  Bitwise equal to the four launches piR2
+ * runs for it (up GEMM, GELU pack of the down projection's input
+ * (`forward_gelu`, coexecution/optimization/groot/integer.py:161-165), down
+ * GEMM, residual add (integer_epilogue.cu:156-327)).  1 <= m <= 64,
+ * d % 128 == 0, f % 1024 == 0, f/128 + 8*d/128 CTAs must fit the SMs at
+ * once, and the whole grid must be resident at the same time (CTAs wait on
+ * one another through counters, each wait bounded at about a second: do
+ * not run other kernels concurrently on the device).  `workspace`
+ * (256-byte aligned, pir2b_dit_ffn_workspace(m, f) bytes) holds the int8
+ * codes of the intermediate activations, their row scales and three
+ * counters; it must be zero before the first call and every call leaves
+ * the counters zeroed; calls sharing a workspace must be stream-ordered. */
+int64_t pir2b_dit_ffn_workspace(int64_t m, int64_t f);
+int pir2b_dit_ffn(const void *qa, const float *sa, const void *up_w, const float *up_sw,
+                  const void *up_bias, int up_bias_mode, const void *gelu_lut,
+                  const void *down_w, const float *down_sw, const void *down_bias,
+                  int down_bias_mode, const void *residual, int64_t ldr, int64_t m, int64_t d,
+                  int64_t f, void *out, int64_t ldo, void *workspace, int64_t workspace_bytes,
+                  void *stream);
+
 /* W8A8 gate|up GEMM with the SwiGLU epilogue: out[m, c] =
  * bf16(f32(silu_lut[g]) * f32(u)) for c < half_n, where g and u are the
  * exact dequantized bf16 GEMM outputs of gate channel c and up channel c.

@@ -39,6 +39,8 @@ SIGNATURES = {
     ],
     "pir2b_pack_nvfp4": [_P, _I64, _I64, _P, _P, _P],
     "pir2b_gemm_nvfp4": [_P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _P, _I64, _P],
+    "pir2b_dit_ffn_workspace": [_I64, _I64],
+    "pir2b_dit_ffn": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
     "pir2b_gemm_swiglu": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _P, _I64, _P],
     "pir2b_attention_rows": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I, _F, _P],
     "pir2b_qk_norm_rope": [_P, _I64, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _F, _P, _P, _P, _P],
@@ -64,7 +66,7 @@ def lib():
     for name, argtypes in SIGNATURES.items():
         fn = getattr(handle, name)
         fn.argtypes = argtypes
-        fn.restype = ctypes.c_char_p if name == "pir2b_last_error" else _I
+        fn.restype = {"pir2b_last_error": ctypes.c_char_p, "pir2b_dit_ffn_workspace": _I64}.get(name, _I)
     return handle
 
 

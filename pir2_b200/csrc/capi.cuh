@@ -91,6 +91,9 @@ static int device_info(DeviceInfo **out) {
                                d.max_smem);
     if (e == cudaSuccess)
       e = attention_set_smem_all(d.max_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(dit_ffn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               d.max_smem);
     if (e != cudaSuccess)
       return cuda_status(e, "cudaFuncSetAttribute");
     d.attrs_set = true;
@@ -817,6 +820,125 @@ int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const flo
                 (long long)kpad);
   return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, nullptr, nullptr, 0, silu_lut, 8, m,
                      2 * half_n, kpad, out, ldo, half_n, stream);
+}
+
+// Workspace of pir2b_dit_ffn: [3 counters | pad to 256 B][row maxima f32
+// [m, f/128]][row scales f32 [m]] padded to 256 B, then the int8 codes of h
+// [m, f].
+static int64_t ffn_workspace_layout(int64_t m, int64_t f, int64_t *max_off, int64_t *scale_off,
+                                    int64_t *code_off) {
+  *max_off = 256;
+  *scale_off = *max_off + m * (f / 128) * 4;
+  *code_off = ((*scale_off + m * 4 + 255) / 256) * 256;
+  return *code_off + m * f;
+}
+
+int64_t pir2b_dit_ffn_workspace(int64_t m, int64_t f) {
+  if (m < 1 || f < 128)
+    return 0;
+  int64_t a, b, c;
+  return ffn_workspace_layout(m, f, &a, &b, &c);
+}
+
+int pir2b_dit_ffn(const void *qa, const float *sa, const void *up_w, const float *up_sw,
+                  const void *up_bias, int up_bias_mode, const void *gelu_lut,
+                  const void *down_w, const float *down_sw, const void *down_bias,
+                  int down_bias_mode, const void *residual, int64_t ldr, int64_t m, int64_t d,
+                  int64_t f, void *out, int64_t ldo, void *workspace, int64_t workspace_bytes,
+                  void *stream) {
+  if (m < 1 || m > 64 || d < 128 || d % 128 != 0 || d > 65536 || f < 1024 ||
+      f % (128 * kFfnSplits) != 0 || f > 8192)
+    return fail(PIR2B_EINVAL,
+                "dit_ffn: need 1 <= m <= 64, d %% 128 == 0, f %% 1024 == 0 and f <= 8192");
+  if (up_bias_mode < 0 || up_bias_mode > 2 || down_bias_mode < 0 || down_bias_mode > 2)
+    return fail(PIR2B_EINVAL, "dit_ffn: bias modes must be 0, 1 or 2");
+  if ((up_bias_mode == PIR2B_BIAS_ADD && up_bias == nullptr) ||
+      (down_bias_mode == PIR2B_BIAS_ADD && down_bias == nullptr))
+    return fail(PIR2B_EINVAL, "dit_ffn: bias mode ADD needs a bias vector");
+  if (qa == nullptr || sa == nullptr || up_w == nullptr || up_sw == nullptr ||
+      gelu_lut == nullptr || down_w == nullptr || down_sw == nullptr || residual == nullptr ||
+      out == nullptr || workspace == nullptr)
+    return fail(PIR2B_EINVAL, "dit_ffn operands must be non-null");
+  if (ldr < d || ldo < d)
+    return fail(PIR2B_EINVAL, "dit_ffn: row strides must be >= d");
+  if (!aligned(qa, 16) || !aligned(up_w, 16) || !aligned(down_w, 16) ||
+      !aligned(workspace, 256) || !aligned(out, 2) || !aligned(residual, 2))
+    return fail(PIR2B_EALIGN, "dit_ffn: operand alignment not met");
+  int64_t max_off, scale_off, code_off;
+  if (workspace_bytes < ffn_workspace_layout(m, f, &max_off, &scale_off, &code_off))
+    return fail(PIR2B_EINVAL, "dit_ffn: workspace too small");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  const int bn = int((m + 15) / 16 * 16);
+  const int up_ctas = int(f / 128);
+  const int down_kb = int(f / 128 / kFfnSplits);
+  const int ctas = up_ctas + int(d / 128) * kFfnSplits;
+  if (ctas > dev->sms)
+    return fail(PIR2B_EINVAL, "dit_ffn: %d CTAs do not fit the %d SMs at once", ctas, dev->sms);
+  if (size_t(down_kb) * kWeightTileBytes < size_t(bn) * kTileN * 4)
+    return fail(PIR2B_EINVAL, "dit_ffn: FFN width too small for the split-K partial tile");
+  const int up_kb = int(d / 128);
+  int up_stages = std::min(up_kb, 12);
+  while (up_stages > 2 && ffn_up_smem(bn, up_stages) > size_t(dev->max_smem))
+    --up_stages;
+  const size_t smem = std::max(ffn_up_smem(bn, up_stages), ffn_down_smem(bn, down_kb));
+  if (smem > size_t(dev->max_smem))
+    return fail(PIR2B_EINVAL, "dit_ffn: shared memory plan does not fit");
+  CUtensorMap tm_up, tm_act, tm_down;
+  if (int r = make_map(&tm_up, up_w, uint64_t(d), uint64_t(f), uint64_t(d), 128u, 128u, true))
+    return r;
+  if (int r = make_map(&tm_act, qa, uint64_t(d), uint64_t(m), uint64_t(d), 128u, uint32_t(bn), true))
+    return r;
+  if (int r = make_map(&tm_down, down_w, uint64_t(f), uint64_t(d), uint64_t(f), 128u, 128u, true))
+    return r;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  CUtensorMap tm_codes;
+  if (int r = make_map(&tm_codes, ws + code_off, uint64_t(f), uint64_t(m), uint64_t(f), 128u,
+                       uint32_t(bn), true))
+    return r;
+  FfnArgs a;
+  a.sa = sa;
+  a.sw_up = up_sw;
+  a.bias_up = static_cast<const __nv_bfloat16 *>(up_bias);
+  a.gelu_lut = static_cast<const __nv_bfloat16 *>(gelu_lut);
+  a.sw_down = down_sw;
+  a.bias_down = static_cast<const __nv_bfloat16 *>(down_bias);
+  a.residual = static_cast<const __nv_bfloat16 *>(residual);
+  a.ldr = ldr;
+  a.out = static_cast<__nv_bfloat16 *>(out);
+  a.ldo = ldo;
+  a.codes = reinterpret_cast<int8_t *>(ws + code_off);
+  a.scales = reinterpret_cast<float *>(ws + scale_off);
+  a.row_max = reinterpret_cast<float *>(ws + max_off);
+  a.counters = reinterpret_cast<unsigned *>(ws);
+  a.m = int(m);
+  a.d = int(d);
+  a.f = int(f);
+  a.bias_mode_up = up_bias_mode;
+  a.bias_mode_down = down_bias_mode;
+  a.bn = bn;
+  a.up_ctas = up_ctas;
+  a.up_kb = up_kb;
+  a.up_stages = up_stages;
+  a.down_kb = down_kb;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(unsigned(ctas), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kFfnSplits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cuda_status(cudaLaunchKernelEx(&cfg, dit_ffn_kernel, tm_up, tm_act, tm_down, tm_codes, a),
+                     "dit_ffn launch");
 }
 
 // Plan introspection for tests and the benchmark (not part of the public

@@ -3,6 +3,7 @@
 #include "quant.cuh"
 #include "gemm_i8.cuh"
 #include "gemm_fp4.cuh"
+#include "dit_ffn.cuh"
 #include "pointwise.cuh"
 #include "attention.cuh"
 #include "capi.cuh"

@@ -269,6 +269,17 @@ __device__ __forceinline__ void tma_store_commit_and_wait() {
                    : "memory");
 }
 
+// 16-byte asynchronous global -> shared copies (all in flight until the
+// wait).
+__device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // Barrier among `count` threads (a multiple of 32) on hardware barrier `id`.
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

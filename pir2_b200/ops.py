@@ -217,6 +217,42 @@ def gemm_swiglu(a, sa, w, sw, bias, silu_lut, *, half_n, bias_mode=None, out=Non
     return out
 
 
+_FFN_WORKSPACES = {}
+
+
+def ffn_workspace(device, m, f):
+    """Zero-initialised workspace for dit_ffn, one per (device, size) and
+    reused by every stream-ordered call (each call leaves it zeroed)."""
+    size = int(_lib.lib().pir2b_dit_ffn_workspace(m, f))
+    key = (torch.device(device), size)
+    if key not in _FFN_WORKSPACES:
+        _FFN_WORKSPACES[key] = torch.zeros(size, device=device, dtype=torch.uint8)
+    return _FFN_WORKSPACES[key]
+
+
+def dit_ffn(qa, sa, up, down, gelu_lut, residual, *, out=None):
+    """residual + down(pack(gelu(up(x)))) for a packed x [m, d] (int8 codes,
+    fp32 scales).  `up` and `down` are W8A8 IntegerLinear-like objects
+    (packed_weight, weight_scale, bias, bias mode, in/out features)."""
+    m, d = qa.shape
+    f = up.out_features
+    res = residual.reshape(m, d)
+    if res.dtype != torch.bfloat16 or res.stride(-1) != 1:
+        raise ValueError("dit_ffn residual must be bf16 rows")
+    if out is None:
+        out = torch.empty((m, d), device=qa.device, dtype=torch.bfloat16)
+    ws = ffn_workspace(qa.device, m, f)
+    status = _lib.lib().pir2b_dit_ffn(
+        qa.data_ptr(), sa.data_ptr(), up.packed_weight.data_ptr(), up.weight_scale.data_ptr(),
+        _ptr(up.bias), up._bias_mode(), gelu_lut.data_ptr(), down.packed_weight.data_ptr(),
+        down.weight_scale.data_ptr(), _ptr(down.bias), down._bias_mode(), res.data_ptr(),
+        res.stride(0), m, d, f, out.data_ptr(), out.stride(0), ws.data_ptr(), ws.numel(),
+        _stream(qa.device),
+    )
+    _lib.check(status, "pir2b_dit_ffn")
+    return out
+
+
 def pack_nvfp4(x):
     """NVFP4 pack of contiguous bf16 rows -> (packed [rows, k/2], swizzled sf)."""
     data, scales, _ = norm_quant_rows(x.reshape(-1, x.shape[-1]).contiguous(), _lib.OUT_NVFP4)

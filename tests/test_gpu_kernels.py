@@ -383,3 +383,32 @@ def test_gemm_swiglu_bitwise(m, k, half):
         cat(torch.from_numpy(sw).cuda()), cat(b.cuda()), lut, half_n=half,
     )
     assert np.array_equal(bits_of(out), ref)
+
+
+@pytest.mark.parametrize("m,d,f", [(17, 1536, 6144), (1, 1536, 6144), (40, 256, 2048), (64, 512, 2048)])
+def test_dit_ffn_equals_the_four_launch_chain(m, d, f):
+    """One-launch FFN == up GEMM (+GELU table) -> plain pack -> down GEMM
+    (+residual), bit for bit; the workspace is left zeroed for reuse."""
+    from types import SimpleNamespace
+
+    g = torch.Generator().manual_seed(m + d + f)
+    x, _, b_up, qa, sa, qw_up, sw_up = quantized_problem(g, m, d, f, 8)
+    _, _, b_dn, _, _, qw_dn, sw_dn = quantized_problem(g, m, f, d, 8)
+    lut = device_lut("tanh")
+    residual = randn_bf16(g, m, d).cuda()
+    dev = lambda a: torch.from_numpy(a).cuda()   # noqa: E731
+    up = SimpleNamespace(packed_weight=dev(qw_up), weight_scale=dev(sw_up), bias=b_up.cuda(),
+                         out_features=f, in_features=d, _bias_mode=lambda: _lib.BIAS_ADD)
+    down = SimpleNamespace(packed_weight=dev(qw_dn), weight_scale=dev(sw_dn), bias=b_dn.cuda(),
+                           out_features=d, in_features=f, _bias_mode=lambda: _lib.BIAS_ADD)
+    qa_d, sa_d = dev(qa), dev(sa)
+    for _ in range(3):                      # repeated calls reuse the workspace
+        got = ops.dit_ffn(qa_d, sa_d, up, down, lut, residual)
+    h = ops.gemm(qa_d, sa_d, up.packed_weight, up.weight_scale, up.bias, 8, out_lut=lut, n_store=f)
+    qh, sh = ops.quant_rows(h, 8)
+    ref = ops.gemm(qh, sh, down.packed_weight, down.weight_scale, down.bias, 8, residual=residual, n_store=d)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    ws = ops.ffn_workspace(torch.device("cuda"), m, f)
+    assert int(ws[:12].view(torch.int32).abs().sum()) == 0     # counters reset
+    assert_status_clean()

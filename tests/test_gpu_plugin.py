@@ -240,9 +240,9 @@ def test_dit_attention_fusion_matches_sdpa_forward_and_restores(cross):
     torch.testing.assert_close(fused.float(), reference.float(), atol=2e-2, rtol=2e-2)
 
 
-@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("bits,ffn_kernel", [(8, False), (8, True), (4, False)])
 @torch.inference_mode()
-def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits):
+def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits, ffn_kernel):
     """Residual adds in the o-proj / down-proj epilogues and the FFN GELU in
     the up-projection epilogue give bitwise the unfused quantized blocks."""
     from pir2_b200.fusion import ResidualFusion
@@ -254,7 +254,7 @@ def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits):
     names, _, _, _ = inventory(policy)
     executed = {n for n in names if n.startswith("action_head.model.transformer_blocks")}
     adapter = TransformerINT(policy, executed, native=True, expanded=True)
-    fusion = ResidualFusion(policy, adapter)
+    fusion = ResidualFusion(policy, adapter, ffn_kernel=ffn_kernel)
     assert len(fusion.blocks) == 2
     torch.manual_seed(5)
     x = torch.randn(2, 17, dit.hidden, device="cuda", dtype=torch.bfloat16)
