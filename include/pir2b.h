@@ -194,6 +194,20 @@ int pir2b_dit_ffn(const void *qa, const float *sa, const void *up_w, const float
                   int64_t f, void *out, int64_t ldo, void *workspace, int64_t workspace_bytes,
                   void *stream);
 
+/* pir2b_dit_ffn with its scratch in a static device array of this library
+ * (about 530 KB per device) instead of a caller workspace: it allocates no
+ * memory.  No counterpart in the reference.  1 <= m <= 64, f <= 8192, the
+ * other limits as pir2b_dit_ffn.  Each call clears the array's counters on
+ * `stream` first.  All calls on one device share the array: calls on
+ * different streams of the same device must not overlap (order them on one
+ * stream or synchronise between them); calls on different devices are
+ * independent. */
+int pir2b_dit_ffn_static(const void *qa, const float *sa, const void *up_w, const float *up_sw,
+                         const void *up_bias, int up_bias_mode, const void *gelu_lut,
+                         const void *down_w, const float *down_sw, const void *down_bias,
+                         int down_bias_mode, const void *residual, int64_t ldr, int64_t m,
+                         int64_t d, int64_t f, void *out, int64_t ldo, void *stream);
+
 /* W8A8 gate|up GEMM with the SwiGLU epilogue: out[m, c] =
  * bf16(f32(silu_lut[g]) * f32(u)) for c < half_n, where g and u are the
  * exact dequantized bf16 GEMM outputs of gate channel c and up channel c.

@@ -941,6 +941,44 @@ int pir2b_dit_ffn(const void *qa, const float *sa, const void *up_w, const float
                      "dit_ffn launch");
 }
 
+// pir2b_dit_ffn_static: the same launch with its scratch in a static
+// device array instead of a caller workspace, for callers that allocate
+// nothing.  Sized for the largest accepted problem (m = 64, f = 8192).
+static_assert(sizeof(int64_t) == 8, "int64_t");
+constexpr int64_t kFfnStaticM = 64, kFfnStaticF = 8192;
+constexpr int64_t kFfnStaticBytes =
+    ((256 + kFfnStaticM * (kFfnStaticF / 128) * 4 + kFfnStaticM * 4 + 255) / 256) * 256 +
+    kFfnStaticM * kFfnStaticF;
+__device__ __align__(256) uint8_t g_ffn_scratch[kFfnStaticBytes];
+
+int pir2b_dit_ffn_static(const void *qa, const float *sa, const void *up_w, const float *up_sw,
+                         const void *up_bias, int up_bias_mode, const void *gelu_lut,
+                         const void *down_w, const float *down_sw, const void *down_bias,
+                         int down_bias_mode, const void *residual, int64_t ldr, int64_t m,
+                         int64_t d, int64_t f, void *out, int64_t ldo, void *stream) {
+  if (m < 1 || m > kFfnStaticM || f < 1 || f > kFfnStaticF)
+    return fail(PIR2B_EINVAL, "dit_ffn_static: need 1 <= m <= %lld and f <= %lld",
+                (long long)kFfnStaticM, (long long)kFfnStaticF);
+  int64_t max_off, scale_off, code_off;
+  const int64_t need = ffn_workspace_layout(m, f, &max_off, &scale_off, &code_off);
+  if (need > kFfnStaticBytes)
+    return fail(PIR2B_EINVAL, "dit_ffn_static: problem exceeds the static scratch");
+  // The array's address in the current device's context.
+  void *scratch = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&scratch, g_ffn_scratch);
+  if (e != cudaSuccess || scratch == nullptr)
+    return cuda_status(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
+                       "dit_ffn_static scratch address");
+  // The three counters must start at zero (a call that timed out may have
+  // left them set); the rest of the scratch is written before it is read.
+  e = cudaMemsetAsync(scratch, 0, 16, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return cuda_status(e, "dit_ffn_static counter reset");
+  return pir2b_dit_ffn(qa, sa, up_w, up_sw, up_bias, up_bias_mode, gelu_lut, down_w, down_sw,
+                       down_bias, down_bias_mode, residual, ldr, m, d, f, out, ldo, scratch,
+                       kFfnStaticBytes, stream);
+}
+
 // Plan introspection for tests and the benchmark (not part of the public
 // header's contract; exported for diagnostics).
 int pir2b_gemm_plan(int bits, int64_t m, int64_t npad, int64_t kpad,
