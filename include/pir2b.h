@@ -235,6 +235,28 @@ int pir2b_attention_rows(const void *q, int64_t ldq, const void *k,
                          int64_t ldo, int64_t batch, int64_t tq, int64_t skv,
                          int heads, int head_dim, float scale, void *stream);
 
+/* Unpacks int4 codes (two per byte, low nibble first: the symmetric-row-v1
+ * activation pack of coexecution/kernels/ampere_ada/integer.py:79-93 and
+ * the weight packing of :234-238) into sign-extended int8 codes, one per
+ * byte.
+ * packed: [rows, k/2] bytes; out: [rows, k] int8; k a multiple of 32, both
+ * 16-byte aligned.  The int8 GEMM of unpacked codes gives the int4 GEMM's
+ * int32 sums exactly; W4A4 layers with many tokens run that way. */
+int pir2b_unpack_int4(const void *packed, int64_t rows, int64_t k, void *out, void *stream);
+
+/* Causal grouped-query attention of the VLM text layers (head_dim 128).
+ * q: bf16 [batch, hq, T, 128], k and v: bf16 [batch, hk, T, 128] (the
+ * outputs of pir2b_qk_norm_rope); out: bf16 rows out[b*T + t, h*128 + d]
+ * with row stride ldo, the o_proj input.  Replaces the torch SDPA call
+ * (is_causal, enable_gqa) and the [B, H, T, D] -> [B*T, H*D] transpose copy
+ * around the quantized o_proj of the Qwen3-VL text attention; the
+ * reference keeps transformers' "sdpa" attention there and checks for it
+ * (coexecution/optimization/groot/vlm.py:312-313).  Query head h reads kv
+ * head h / (hq / hk); key j is visible to query t when j <= t. */
+int pir2b_attention_causal(const void *q, const void *k, const void *v, int64_t batch,
+                           int64_t tokens, int hq, int hk, int head_dim, float scale, void *out,
+                           int64_t ldo, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,6 +44,8 @@ SIGNATURES = {
     "pir2b_dit_ffn_static": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I64, _P],
     "pir2b_gemm_swiglu": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _P, _I64, _P],
     "pir2b_attention_rows": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I, _F, _P],
+    "pir2b_unpack_int4": [_P, _I64, _I64, _P, _P],
+    "pir2b_attention_causal": [_P, _P, _P, _I64, _I64, _I, _I, _I, _F, _P, _I64, _P],
     "pir2b_qk_norm_rope": [_P, _I64, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _F, _P, _P, _P, _P],
 }
 

@@ -345,6 +345,218 @@ __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(const Attn
   }
 }
 
+// ------------------------------------------------------------------
+// Causal attention of the VLM text layers (head_dim 128, grouped-query):
+// q [B, HQ, T, 128], k and v [B, HK, T, 128] (the layout of
+// qk_norm_rope_kernel), output rows out[b*T + t, h*128 + d] for the o_proj
+// pack, replacing torch SDPA (is_causal, enable_gqa) and its transpose copy.
+// Grid (HQ, ceil(T / 64), B): a CTA takes 64 queries of one head, its four
+// warps 16 each; key/value blocks of 64 stream through a two-stage
+// cp.async ring (the block after the current one is in flight while the
+// current one is used); the same register-resident bf16 MMA + online
+// softmax as above, with keys after the query masked.
+struct CausalArgs {
+  const __nv_bfloat16 *q;
+  const __nv_bfloat16 *k;
+  const __nv_bfloat16 *v;
+  __nv_bfloat16 *out;
+  int64_t ldo;
+  int T, hq, hk;
+  float scale;
+};
+
+constexpr int kCausalD = 128;
+constexpr int kCausalP = kCausalD + 8;           // odd number of 16-byte units
+
+__host__ __device__ inline size_t attention_causal_smem() {
+  return size_t(kAttnQTile) * kCausalP * 2 * 5;  // q tile + two K/V stages
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attention_causal_kernel(const CausalArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  constexpr int D = kCausalD, P = kCausalP, KS = D / 16, DN = D / 8, NB = kAttnKBlock / 8;
+  const int h = blockIdx.x, b = blockIdx.z;
+  const int t0 = blockIdx.y * kAttnQTile;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q4 = lane & 3;
+  const int kvh = h / (a.hq / a.hk);
+  __nv_bfloat16 *qs = reinterpret_cast<__nv_bfloat16 *>(smem_raw);   // [64][P]
+  __nv_bfloat16 *kv = qs + kAttnQTile * P;                            // [2][K|V][64][P]
+  const __nv_bfloat16 *qg = a.q + ((int64_t(b) * a.hq + h) * a.T) * D;
+  const __nv_bfloat16 *kg = a.k + ((int64_t(b) * a.hk + kvh) * a.T) * D;
+  const __nv_bfloat16 *vg = a.v + ((int64_t(b) * a.hk + kvh) * a.T) * D;
+  constexpr int vecs = D / 8;
+  const int tn = min(kAttnQTile, a.T - t0);
+  const int nblocks = (min(a.T, t0 + kAttnQTile) + kAttnKBlock - 1) / kAttnKBlock;
+
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = tid; i < kAttnQTile * vecs; i += kAttnThreads) {
+    const int t = i / vecs, d0 = (i % vecs) * 8;
+    if (t < tn)
+      cp_async_16(qs + t * P + d0, qg + int64_t(t0 + t) * D + d0);
+    else
+      *reinterpret_cast<uint4 *>(qs + t * P + d0) = make_uint4(0, 0, 0, 0);
+  }
+  auto load_block = [&](int kb, int stage) {
+    __nv_bfloat16 *ks = kv + stage * 2 * kAttnKBlock * P;
+    __nv_bfloat16 *vs = ks + kAttnKBlock * P;
+    for (int i = tid; i < kAttnKBlock * vecs; i += kAttnThreads) {
+      const int j = i / vecs, d0 = (i % vecs) * 8;
+      const int key = kb * kAttnKBlock + j;
+      if (key < a.T) {
+        cp_async_16(ks + j * P + d0, kg + int64_t(key) * D + d0);
+        cp_async_16(vs + j * P + d0, vg + int64_t(key) * D + d0);
+      } else {
+        *reinterpret_cast<uint4 *>(ks + j * P + d0) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(vs + j * P + d0) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  load_block(0, 0);
+  cp_async_commit();                               // group: q tile + block 0
+
+  const int r0 = warp * 16;
+  const bool active = r0 < tn;
+  float o[DN][4];
+#pragma unroll
+  for (int n = 0; n < DN; ++n)
+    o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  uint32_t qa[KS][4];
+  const int t_lo = t0 + r0 + g, t_hi = t_lo + 8;    // this thread's query rows
+  for (int kb = 0; kb < nblocks; ++kb) {
+    if (kb + 1 < nblocks) {
+      load_block(kb + 1, (kb + 1) & 1);
+      cp_async_commit();
+      cp_async_wait_group<1>();
+    } else {
+      cp_async_wait_group<0>();
+    }
+    __syncthreads();
+    if (kb == 0 && active) {
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        const int row = r0 + (lane & 15);
+        const int col = s * 16 + (lane >> 4) * 8;
+        ldsm_x4(smem_u32(qs) + uint32_t((row * P + col) * 2), qa[s][0], qa[s][1], qa[s][2], qa[s][3]);
+      }
+    }
+    // A block whose keys all come after the warp's last query adds nothing.
+    if (active && kb * kAttnKBlock <= t0 + r0 + 15) {
+      const uint32_t ks_addr = smem_u32(kv + (kb & 1) * 2 * kAttnKBlock * P);
+      const uint32_t vs_addr = ks_addr + uint32_t(kAttnKBlock * P * 2);
+      float s_acc[NB][4];
+#pragma unroll
+      for (int n = 0; n < NB; ++n) {
+        s_acc[n][0] = s_acc[n][1] = s_acc[n][2] = s_acc[n][3] = 0.f;
+#pragma unroll
+        for (int s = 0; s < KS; s += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int row = n * 8 + (lane & 7);
+          const int col = s * 16 + (lane >> 3) * 8;
+          ldsm_x4(ks_addr + uint32_t((row * P + col) * 2), b0, b1, b2, b3);
+          mma_bf16_16816(s_acc[n], qa[s], b0, b1);
+          mma_bf16_16816(s_acc[n], qa[s + 1], b2, b3);
+        }
+      }
+      float bm_lo = -INFINITY, bm_hi = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < NB; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = kb * kAttnKBlock + n * 8 + 2 * q4 + (e & 1);
+          const int tq = e < 2 ? t_lo : t_hi;
+          float v = s_acc[n][e] * a.scale;
+          if (key > tq || key >= a.T)
+            v = -INFINITY;
+          s_acc[n][e] = v;
+        }
+        bm_lo = fmaxf(bm_lo, fmaxf(s_acc[n][0], s_acc[n][1]));
+        bm_hi = fmaxf(bm_hi, fmaxf(s_acc[n][2], s_acc[n][3]));
+      }
+      bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 1));
+      bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, 2));
+      bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 1));
+      bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 2));
+      const float mn_lo = fmaxf(m_lo, bm_lo), mn_hi = fmaxf(m_hi, bm_hi);
+      // Key 0 is visible to every query, so m is finite from block 0 on;
+      // the guards only keep exp(-inf - -inf) out.
+      const float al_lo = (m_lo == -INFINITY) ? 0.f : expf(m_lo - mn_lo);
+      const float al_hi = (m_hi == -INFINITY) ? 0.f : expf(m_hi - mn_hi);
+      m_lo = mn_lo;
+      m_hi = mn_hi;
+      l_lo *= al_lo;
+      l_hi *= al_hi;
+#pragma unroll
+      for (int n = 0; n < DN; ++n) {
+        o[n][0] *= al_lo;
+        o[n][1] *= al_lo;
+        o[n][2] *= al_hi;
+        o[n][3] *= al_hi;
+      }
+      uint32_t pa[NB / 2][4];
+#pragma unroll
+      for (int n = 0; n < NB; ++n) {
+        const float p0 = m_lo == -INFINITY ? 0.f : expf(s_acc[n][0] - m_lo);
+        const float p1 = m_lo == -INFINITY ? 0.f : expf(s_acc[n][1] - m_lo);
+        const float p2 = m_hi == -INFINITY ? 0.f : expf(s_acc[n][2] - m_hi);
+        const float p3 = m_hi == -INFINITY ? 0.f : expf(s_acc[n][3] - m_hi);
+        l_lo += p0 + p1;
+        l_hi += p2 + p3;
+        pa[n / 2][(n & 1) * 2 + 0] = pack_bf16x2(p0, p1);
+        pa[n / 2][(n & 1) * 2 + 1] = pack_bf16x2(p2, p3);
+      }
+#pragma unroll
+      for (int kk = 0; kk < NB / 2; ++kk) {
+        const int row = kk * 16 + (lane & 15);
+#pragma unroll
+        for (int n = 0; n < DN; n += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int col = n * 8 + (lane >> 4) * 8;
+          ldsm_x4_trans(vs_addr + uint32_t((row * P + col) * 2), b0, b1, b2, b3);
+          mma_bf16_16816(o[n], pa[kk], b0, b1);
+          mma_bf16_16816(o[n + 1], pa[kk], b2, b3);
+        }
+      }
+    }
+    __syncthreads();   // this stage is refilled by the next iteration's prefetch
+  }
+  if (!active)
+    return;
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  const float i_lo = 1.0f / l_lo, i_hi = 1.0f / l_hi;
+#pragma unroll
+  for (int n = 0; n < DN; ++n) {
+    const int d = h * D + n * 8 + 2 * q4;
+    if (t_lo < a.T) {
+      __nv_bfloat16 *dst = a.out + (int64_t(b) * a.T + t_lo) * a.ldo + d;
+      *reinterpret_cast<uint32_t *>(dst) = pack_bf16x2(o[n][0] * i_lo, o[n][1] * i_lo);
+    }
+    if (t_hi < a.T) {
+      __nv_bfloat16 *dst = a.out + (int64_t(b) * a.T + t_hi) * a.ldo + d;
+      *reinterpret_cast<uint32_t *>(dst) = pack_bf16x2(o[n][2] * i_hi, o[n][3] * i_hi);
+    }
+  }
+}
+
+cudaError_t run_attention_causal(const CausalArgs &a, int B, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(a.hq), unsigned((a.T + kAttnQTile - 1) / kAttnQTile), unsigned(B));
+  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.dynamicSmemBytes = attention_causal_smem();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_causal_kernel, a);
+}
+
 // Chunks per head: a power of two up to 8 keeping at least 64 keys per CTA,
 // so every chunk is non-empty.
 static int attention_chunks(int S) {
@@ -365,7 +577,9 @@ static cudaError_t attention_set_smem(int bytes) {
 }
 
 static cudaError_t attention_set_smem_all(int bytes) {
-  cudaError_t e = attention_set_smem<32>(bytes);
+  cudaError_t e = cudaFuncSetAttribute(attention_causal_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = attention_set_smem<32>(bytes);
   if (e == cudaSuccess) e = attention_set_smem<48>(bytes);
   if (e == cudaSuccess) e = attention_set_smem<64>(bytes);
   if (e == cudaSuccess) e = attention_set_smem<96>(bytes);

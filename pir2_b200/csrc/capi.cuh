@@ -715,6 +715,51 @@ int pir2b_attention_rows(const void *q, int64_t ldq, const void *k,
                      "attention_rows launch");
 }
 
+int pir2b_unpack_int4(const void *packed, int64_t rows, int64_t k, void *out, void *stream) {
+  if (rows < 1 || k < 32 || k % 32 != 0 || rows > (int64_t(1) << 31) || k > (int64_t(1) << 24))
+    return fail(PIR2B_EINVAL, "unpack_int4 needs rows >= 1 and k a positive multiple of 32");
+  if (packed == nullptr || out == nullptr)
+    return fail(PIR2B_EINVAL, "unpack_int4 operands must be non-null");
+  if (!aligned(packed, 16) || !aligned(out, 16))
+    return fail(PIR2B_EALIGN, "unpack_int4 buffers must be 16-byte aligned");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  return cuda_status(run_unpack_int4(packed, out, rows * k / 32, dev->sms,
+                                     static_cast<cudaStream_t>(stream)),
+                     "unpack_int4 launch");
+}
+
+int pir2b_attention_causal(const void *q, const void *k, const void *v, int64_t batch,
+                           int64_t tokens, int hq, int hk, int head_dim, float scale, void *out,
+                           int64_t ldo, void *stream) {
+  if (batch < 1 || tokens < 1 || hq < 1 || hk < 1 || hq % hk != 0 || head_dim != kCausalD ||
+      batch > 65535 || hq > 65535 || tokens > (int64_t(1) << 24))
+    return fail(PIR2B_EINVAL,
+                "attention_causal: need batch, T >= 1, hq a multiple of hk and head_dim 128");
+  if (ldo < int64_t(hq) * head_dim)
+    return fail(PIR2B_EINVAL, "attention_causal: ldo below hq * head_dim");
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(PIR2B_EINVAL, "attention_causal operands must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 4) || ldo % 2 != 0)
+    return fail(PIR2B_EALIGN, "attention_causal: q/k/v 16-byte, out 4-byte aligned, ldo even");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  CausalArgs a;
+  a.q = static_cast<const __nv_bfloat16 *>(q);
+  a.k = static_cast<const __nv_bfloat16 *>(k);
+  a.v = static_cast<const __nv_bfloat16 *>(v);
+  a.out = static_cast<__nv_bfloat16 *>(out);
+  a.ldo = ldo;
+  a.T = int(tokens);
+  a.hq = hq;
+  a.hk = hk;
+  a.scale = scale;
+  return cuda_status(run_attention_causal(a, int(batch), static_cast<cudaStream_t>(stream)),
+                     "attention_causal launch");
+}
+
 int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
                      const void *sfw, const void *bias, float alpha,
                      int64_t m, int64_t n, int64_t k, void *out, int64_t ldo,
@@ -745,7 +790,15 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
   const int bn = m <= 128 ? int((m + 15) / 16 * 16) : 128;
   const int mtiles = int((m + 127) / 128);
   const size_t stage = size_t(kFp4WeightTile) + size_t(bn) * kFp4BlockBytes + 2 * kSfStageBytes;
-  int stages = 8;
+  const int num_kb = int(k / 256);
+  const int ntiles = int((n + 127) / 128);
+  // One token tile: split K over a cluster (power of two up to 8, at least
+  // one K block per rank) until about 96 CTAs stream the weights.
+  int splits = 1;
+  while (mtiles == 1 && splits < 8 && ntiles * splits < 96 && num_kb >= 2 * splits)
+    splits *= 2;
+  const int kb_per = (num_kb + splits - 1) / splits;
+  int stages = splits > 1 ? std::max(2, std::min(8, kb_per)) : 8;
   auto smem_of = [&](int s) { return 1024 + s * stage + (2 * s + 1) * 8 + 16; };
   while (stages > 2 && smem_of(stages) > size_t(dev->max_smem))
     --stages;
@@ -764,12 +817,13 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
   args.ldo = ldo;
   args.m = int(m);
   args.n = int(n);
-  args.num_kb = int(k / 256);
+  args.num_kb = num_kb;
   args.blocks_k = int((k / 16 + 3) / 4);
   args.bn = bn;
   args.stages = stages;
   args.alpha = alpha;
-  args.tma_store = (ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  args.splits = splits;
+  args.tma_store = (splits == 1 && ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
   if (args.tma_store) {
     if (int r = make_out_map(&tm_out, out, uint64_t(n), uint64_t(m), uint64_t(ldo),
                              uint32_t(bn), 128u))
@@ -777,15 +831,19 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
   }
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(unsigned((n + 127) / 128), unsigned(mtiles), 1);
+  cfg.gridDim = dim3(unsigned(ntiles), unsigned(mtiles), unsigned(splits));
   cfg.blockDim = dim3(kFp4Threads, 1, 1);
   cfg.dynamicSmemBytes = smem_of(stages);
   cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = unsigned(splits);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = splits > 1 ? 2 : 1;
   return cuda_status(cudaLaunchKernelEx(&cfg, gemm_fp4_kernel, tm_w, tm_a, tm_out, args),
                      "gemm_nvfp4 launch");
 }

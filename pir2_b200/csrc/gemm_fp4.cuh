@@ -13,6 +13,12 @@
 // and issues the block-scaled MMAs, warps 2-5 run the epilogue.  A 256-
 // element K block is 128 bytes per row; its 16 factors per row are four
 // 512-byte atoms (128 rows x 4 factors), contiguous in the global layout.
+//
+// Few tokens (one token tile) give few CTAs, so the K blocks are split over
+// a cluster of `splits` CTAs along z: each writes its fp32 partial tile to
+// its own (then idle) stage memory, and rank r sums channels
+// [r*128/splits, (r+1)*128/splits) of all ranks through distributed shared
+// memory in rank order before the alpha/bias epilogue.
 #pragma once
 #include "args.cuh"
 #include "ptx.cuh"
@@ -32,6 +38,7 @@ struct Fp4GemmArgs {
   int stages;
   float alpha;
   int tma_store;
+  int splits;                    // K split over a cluster along z (1..8)
 };
 
 constexpr int kFp4Threads = 192;
@@ -107,6 +114,9 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * 128;
   const int m0 = blockIdx.y * 128;        // token tiles start on atom rows
+  const int kb_begin = (int(blockIdx.z) * args.num_kb) / args.splits;
+  const int kb_end = ((int(blockIdx.z) + 1) * args.num_kb) / args.splits;
+  const int nkb = kb_end - kb_begin;
   constexpr uint32_t kTmemCols = 256;     // accumulator (<=128) + SFA + SFB
   const uint32_t sfa_col = 128, sfb_col = 144;
 
@@ -139,29 +149,30 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
     if (elect_one_sync()) {
       const uint32_t tx = uint32_t(stage_bytes);
       bool waited = false;
-      for (int i = 0; i < args.num_kb; ++i) {
+      for (int i = 0; i < nkb; ++i) {
         const int s = i % stages;
         const uint32_t phase = (i / stages) & 1;
         if (!mbar_wait(&empty[s], phase ^ 1, kStatusTimeoutProducer))
           break;
+        const int kb = kb_begin + i;
         uint8_t *st = smem + s * stage_bytes;
         mbar_arrive_expect_tx(&full[s], tx);
-        tma_load_2d(st, &tm_w, &full[s], i * kFp4BlockBytes, n0);
-        bulk_load(st + kFp4WeightTile + op_b_bytes, sfw_block + size_t(i) * kSfStageBytes,
+        tma_load_2d(st, &tm_w, &full[s], kb * kFp4BlockBytes, n0);
+        bulk_load(st + kFp4WeightTile + op_b_bytes, sfw_block + size_t(kb) * kSfStageBytes,
                   kSfStageBytes, &full[s]);
         if (!waited) {
           pdl_wait();   // activations and their factors come from the previous kernel
           waited = true;
         }
-        tma_load_2d(st + kFp4WeightTile, &tm_a, &full[s], i * kFp4BlockBytes, m0);
+        tma_load_2d(st + kFp4WeightTile, &tm_a, &full[s], kb * kFp4BlockBytes, m0);
         bulk_load(st + kFp4WeightTile + op_b_bytes + kSfStageBytes,
-                  sfa_block + size_t(i) * kSfStageBytes, kSfStageBytes, &full[s]);
+                  sfa_block + size_t(kb) * kSfStageBytes, kSfStageBytes, &full[s]);
       }
     }
   } else if (warp == 1) {
     if (elect_one_sync()) {
       const uint32_t idesc = idesc_nvf4(128, bn);
-      for (int i = 0; i < args.num_kb; ++i) {
+      for (int i = 0; i < nkb; ++i) {
         const int s = i % stages;
         const uint32_t phase = (i / stages) & 1;
         if (!mbar_wait(&full[s], phase, kStatusTimeoutMma))
@@ -199,7 +210,19 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
     const int valid_m = min(bn, args.m - m0);
     const uint32_t lane_addr = tmem_base + (uint32_t(quarter * 32) << 16);
     __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem);
-    if (have_acc) {
+    if (have_acc && args.splits > 1) {
+      // fp32 partial tile [bn][128] over the stage memory: every MMA (and
+      // so every read of the stages) completed before accum_full.
+      float *part = reinterpret_cast<float *>(smem);
+      for (int j0 = 0; j0 < bn; j0 += 16) {
+        uint32_t r[16];
+        tmem_ld_16(lane_addr + j0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          part[(j0 + i) * 128 + ch] = __uint_as_float(r[i]);
+      }
+    } else if (have_acc) {
       for (int j0 = 0; j0 < bn; j0 += 16) {
         uint32_t r[16];
         tmem_ld_16(lane_addr + j0, r);
@@ -229,6 +252,47 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
       }
     }
   }
+  if (args.splits > 1) {
+    // Every thread of every CTA in the cluster takes part in both barriers.
+    cluster_sync();
+    if (warp >= 2) {
+      // Rank r owns channels [r*slice, (r+1)*slice); a thread takes four
+      // consecutive channels and walks the tokens, one 16-byte load per
+      // peer and token, summed in rank order.
+      const int et = threadIdx.x - 64;
+      const uint32_t rank = cluster_ctarank();
+      const int splits = args.splits;
+      const int slice = 128 / splits;
+      const int tpt = slice / 4;
+      const int cl = (et % tpt) * 4;
+      const int cq = int(rank) * slice + cl;
+      const int cc = n0 + cq;
+      const int valid_m = min(bn, args.m - m0);
+      float b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        b[i] = (args.bias != nullptr && cc + i < args.n) ? __bfloat162float(args.bias[cc + i]) : 0.f;
+      const uint32_t part_addr = smem_u32(smem) + uint32_t(cq * 4);
+      for (int j = et / tpt; j < valid_m; j += 128 / tpt) {
+        const uint32_t off = uint32_t(j * 128 * 4);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int p = 0; p < splits; ++p) {
+          const int4 v = ld_cluster_v4(map_peer(part_addr, uint32_t(p)) + off);
+          acc[0] = __fadd_rn(acc[0], __int_as_float(v.x));
+          acc[1] = __fadd_rn(acc[1], __int_as_float(v.y));
+          acc[2] = __fadd_rn(acc[2], __int_as_float(v.z));
+          acc[3] = __fadd_rn(acc[3], __int_as_float(v.w));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (cc + i < args.n)
+            args.out[int64_t(m0 + j) * args.ldo + cc + i] =
+                __float2bfloat16_rn(__fadd_rn(__fmul_rn(args.alpha, acc[i]), b[i]));
+      }
+    }
+    cluster_sync();
+  }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -10,7 +10,10 @@
 //   out = bf16(bf16(h * cos) + bf16(rotate_half(h) * sin)).
 // v heads are copied.  Outputs are [B, H, T, D] contiguous.
 #pragma once
+#include <algorithm>
+
 #include "args.cuh"
+#include "gemm_i8.cuh"
 #include "ptx.cuh"
 
 namespace pir2b {
@@ -117,6 +120,48 @@ cudaError_t run_qk_norm_rope(const QkRopeArgs &a, int64_t rows,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, qk_norm_rope_kernel, a);
+}
+
+// Packed int4 codes (two per byte, low nibble first) -> sign-extended int8
+// codes, one per byte: the int8 container layout of the same values, so the
+// int8 GEMM produces the int4 GEMM's int32 sums.  16 packed bytes per
+// thread and step, grid-stride.
+__global__ void __launch_bounds__(256) unpack_int4_kernel(const uint4 *__restrict__ src,
+                                                          uint4 *__restrict__ dst, int64_t chunks) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const uint4 w = src[i];
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lo = sext_nibbles(words[j] & 0x0F0F0F0Fu);
+      const uint32_t hi = sext_nibbles((words[j] >> 4) & 0x0F0F0F0Fu);
+      out[2 * j] = __byte_perm(lo, hi, 0x5140);
+      out[2 * j + 1] = __byte_perm(lo, hi, 0x7362);
+    }
+    dst[2 * i] = make_uint4(out[0], out[1], out[2], out[3]);
+    dst[2 * i + 1] = make_uint4(out[4], out[5], out[6], out[7]);
+  }
+}
+
+cudaError_t run_unpack_int4(const void *src, void *dst, int64_t chunks, int sms,
+                            cudaStream_t st) {
+  const int64_t want = (chunks + 255) / 256;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(want, int64_t(sms) * 8));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(blocks), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, unpack_int4_kernel, static_cast<const uint4 *>(src),
+                            static_cast<uint4 *>(dst), chunks);
 }
 
 } // namespace pir2b

@@ -24,6 +24,13 @@ def load_integer_extension():
     return _lib.lib()
 
 
+# W4A4 GEMMs over more token rows than this run on the int8 kernel over
+# unpacked codes (same int32 sums, so bitwise the same output): past the
+# small-M regime the GEMM is bound by MMA issue rather than weight bytes, and
+# the int8 kernel reads its operands by TMA with no in-kernel unpack.
+WIDE_INT4_ROWS = 64
+
+
 @dataclass
 class PackedActivation:
     data: torch.Tensor
@@ -164,13 +171,16 @@ class IntegerLinear(torch.nn.Module):
             raise ValueError("Incompatible activation pack")
         if residual is None:
             residual = self.__dict__.pop("_pending_residual", None)
+        data, weight, bits = packed.data, self.packed_weight, self.bits
+        if bits == 4 and data.shape[0] > WIDE_INT4_ROWS:
+            data, weight, bits = ops.unpack_int4(data), self.wide_weight(), 8
         out = ops.gemm(
-            packed.data,
+            data,
             packed.scales,
-            self.packed_weight,
+            weight,
             self.weight_scale,
             self.bias,
-            self.bits,
+            bits,
             bias_mode=self._bias_mode(),
             out_lut=out_lut,
             residual=residual,
@@ -178,6 +188,16 @@ class IntegerLinear(torch.nn.Module):
             tactic=self.tactic,
         )
         return out.reshape(*packed.shape, self.out_features)
+
+    def wide_weight(self):
+        """The int4 weights unpacked to int8 containers, made once per
+        weight tensor (kept outside the module's state)."""
+        key = (self.packed_weight.data_ptr(), self.packed_weight.device)
+        cached = self.__dict__.get("_wide_weight")
+        if cached is None or cached[0] != key:
+            cached = (key, ops.unpack_int4(self.packed_weight))
+            self.__dict__["_wide_weight"] = cached
+        return cached[1]
 
     def pending_residual(self, residual):
         """Stages a residual for the next forward of this layer only."""

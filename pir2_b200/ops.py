@@ -279,6 +279,49 @@ def qk_norm_rope(qkv, q_weight, k_weight, cos, sin, *, tokens, hq, hk, eps, head
     return q, k, v
 
 
+def unpack_int4(packed, out=None):
+    """Low-nibble-first int4 codes uint8 [rows, k/2] -> int8 [rows, k]
+    (sign-extended, one code per byte): the int8 container of the same
+    values, for the int8 GEMM."""
+    if packed.dtype != torch.uint8 or packed.dim() != 2 or packed.stride(1) != 1 or not packed.is_contiguous():
+        raise ValueError("unpack_int4 needs contiguous uint8 [rows, k/2] codes")
+    rows, half = packed.shape
+    if out is None:
+        out = torch.empty((rows, 2 * half), device=packed.device, dtype=torch.int8)
+    if out.shape != (rows, 2 * half) or out.dtype != torch.int8 or not out.is_contiguous():
+        raise ValueError("unpack_int4 output must be contiguous int8 [rows, k]")
+    status = _lib.lib().pir2b_unpack_int4(packed.data_ptr(), rows, 2 * half, out.data_ptr(), _stream(packed.device))
+    _lib.check(status, "pir2b_unpack_int4")
+    return out
+
+
+def attention_causal(q, k, v, *, scale=None, out=None):
+    """Causal grouped-query attention, head_dim 128.
+
+    q: bf16 [B, hq, T, 128], k and v: bf16 [B, hk, T, 128] contiguous (the
+    layout `qk_norm_rope` returns).  Returns bf16 [B*T, hq*128] rows, the
+    o_proj input, equal to SDPA(q, k, v, is_causal=True, enable_gqa=True)
+    transposed to [B, T, hq*128] within bf16 tolerance.
+    """
+    b, hq, t, d = q.shape
+    hk = k.shape[1]
+    if k.shape != (b, hk, t, d) or v.shape != k.shape:
+        raise ValueError("attention_causal: k and v must be [B, hk, T, D] like q")
+    for x in (q, k, v):
+        if x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise ValueError("attention_causal: q, k, v must be contiguous bf16")
+    if out is None:
+        out = torch.empty((b * t, hq * d), device=q.device, dtype=torch.bfloat16)
+    if scale is None:
+        scale = d ** -0.5
+    status = _lib.lib().pir2b_attention_causal(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), b, t, hq, hk, d, float(scale), out.data_ptr(),
+        out.stride(0), _stream(q.device),
+    )
+    _lib.check(status, "pir2b_attention_causal")
+    return out
+
+
 def gemm_nvfp4(a_packed, a_sf, w_packed, w_sf, bias=None, *, n, alpha=1.0, out=None):
     """NVFP4 GEMM: bf16(alpha * sum (a * sfa)(w * sfw) [+ bias]) -> [m, n].
 

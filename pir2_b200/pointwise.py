@@ -6,10 +6,12 @@ piR2 fuses Qwen3's rotary embedding and RMSNorm with Triton kernels
 grouped q|k|v GEMM runs once, then one sm_100a kernel applies the per-head
 q_norm / k_norm, the rotary embedding and the [B, H, T, D] relayout of q, k
 and v (replacing three contiguous copies, two torch RMSNorms and two torch
-RoPE chains), then attention and the quantized o_proj run as before.
-The RoPE arithmetic is bitwise torch's; the per-head mean of squares is
-reduced in a different order than torch's (tolerance-level, like piR2's
-own fused norms).
+RoPE chains).  With `causal_kernel=True` causal attention runs on
+`ops.attention_causal`, which writes the o_proj input rows directly
+(replacing torch SDPA and the [B, H, T, D] -> [B, T, H*D] transpose copy);
+the default keeps torch SDPA, measured faster at the GR00T shape.  The RoPE arithmetic is bitwise torch's; the per-head mean of
+squares is reduced in a different order than torch's (tolerance-level, like
+piR2's own fused norms), and so is the attention softmax.
 """
 
 import torch.nn.functional as F
@@ -18,8 +20,9 @@ from . import ops
 
 
 class TextAttentionFusion:
-    def __init__(self, model, controller):
+    def __init__(self, model, controller, *, causal_kernel=False):
         self.controller = controller
+        self.causal_kernel = causal_kernel
         self.saved = []
         names = {id(m): n for n, m in model.named_modules()}
         self.targets = []
@@ -59,6 +62,9 @@ class TextAttentionFusion:
                     hk=attn.kv_heads,
                     eps=attn.q_norm.variance_epsilon,
                 )
+                if self.causal_kernel:
+                    y = ops.attention_causal(q, k, v)
+                    return attn.o_proj(y.view(b, t, attn.heads * attn.head_dim))
                 y = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
                 return attn.o_proj(y.transpose(1, 2).reshape(b, t, attn.heads * attn.head_dim))
 

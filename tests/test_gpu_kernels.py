@@ -362,6 +362,92 @@ def test_attention_rows_strided_query_and_argument_errors():
         ops.attention_rows(q, long_kv[:, :w], long_kv[:, w:], batch=1, heads=heads, head_dim=d)
 
 
+@pytest.mark.parametrize("rows,k", [(1, 128), (544, 2048), (37, 6144), (4096, 1536)])
+def test_unpack_int4_matches_oracle(rows, k):
+    g = np.random.default_rng(rows + k)
+    packed = g.integers(0, 256, size=(rows, k // 2), dtype=np.uint8)
+    got = ops.unpack_int4(torch.from_numpy(packed).cuda()).cpu().numpy()
+    assert np.array_equal(got, oracle.unpack_int4(packed))
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("m", [65, 300, 1088])
+@torch.inference_mode()
+def test_w4a4_many_token_layer_on_unpacked_codes_equals_int4_kernel(m):
+    """An IntegerLinear(bits=4) over more than WIDE_INT4_ROWS rows runs the
+    int8 GEMM on unpacked codes; its output is bitwise the int4 kernel's and
+    the oracle's, with and without a residual."""
+    from pir2_b200.integer import WIDE_INT4_ROWS, IntegerLinear, prepare_activation
+
+    assert m > WIDE_INT4_ROWS
+    torch.manual_seed(m)
+    with torch.device("cuda"):
+        linear = torch.nn.Linear(1536, 1000, bias=True).to(torch.bfloat16)
+    layer = IntegerLinear.from_linear(linear, bits=4)
+    x = torch.randn(m, 1536, device="cuda", dtype=torch.bfloat16)
+    residual = torch.randn(m, 1000, device="cuda", dtype=torch.bfloat16)
+    packed = prepare_activation(x, 4)
+    direct = ops.gemm(packed.data, packed.scales, layer.packed_weight, layer.weight_scale, layer.bias, 4,
+                      n_store=1000)
+    equal = lambda a, b: np.array_equal(bits_of(a), bits_of(b))   # noqa: E731
+    assert equal(layer.forward_packed(packed), direct)
+    direct_res = ops.gemm(packed.data, packed.scales, layer.packed_weight, layer.weight_scale, layer.bias,
+                          4, n_store=1000, residual=residual)
+    assert equal(layer.forward_packed(packed, residual=residual), direct_res)
+    qa = packed.data.cpu().numpy()
+    ref = oracle.gemm_epilogue(
+        oracle.int_matmul(oracle.unpack_int4(qa), oracle.unpack_int4(layer.packed_weight.cpu().numpy())),
+        packed.scales.cpu().numpy(), layer.weight_scale.cpu().numpy(), bits_of(layer.bias.cpu()), 2,
+    )[:, :1000]
+    assert np.array_equal(bits_of(direct.cpu()), ref)
+    assert_status_clean()
+
+
+@pytest.mark.parametrize(
+    "b,t,hq,hk",
+    [
+        (1, 544, 16, 8),    # GR00T text layers: 9 query tiles, 9 key blocks
+        (2, 544, 16, 8),
+        (1, 1, 2, 1),
+        (1, 63, 4, 4),      # one ragged query tile, no grouping
+        (1, 65, 4, 2),      # second tile holds one query
+        (3, 200, 8, 2),     # ragged key block, group of 4
+    ],
+)
+def test_attention_causal_matches_fp32_sdpa(b, t, hq, hk):
+    # Tolerance: bf16 output rounding (2^-8 relative) plus fp32 summation
+    # order and the bf16 probabilities fed to the P.V MMA; inputs are
+    # exactly representable bf16 and the reference runs in fp32.
+    g = torch.Generator(device="cuda").manual_seed(t + hq)
+    q = torch.randn(b, hq, t, 128, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(b, hk, t, 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(b, hk, t, 128, device="cuda", generator=g).to(torch.bfloat16)
+    out = ops.attention_causal(q, k, v)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q.float(), k.float().repeat_interleave(hq // hk, 1), v.float().repeat_interleave(hq // hk, 1),
+        is_causal=True,
+    )
+    ref = ref.transpose(1, 2).reshape(b * t, hq * 128)
+    torch.testing.assert_close(out.float(), ref, atol=4e-3, rtol=8e-3)
+    assert _lib.device_status() == 0
+
+
+def test_attention_causal_writes_strided_rows_only():
+    """Rows of a wider buffer: columns beyond hq*128 are left untouched."""
+    b, t, hq, hk = 1, 100, 4, 2
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(b, hq, t, 128, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(b, hk, t, 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(b, hk, t, 128, device="cuda", generator=g).to(torch.bfloat16)
+    wide = torch.full((b * t, hq * 128 + 64), 7.0, device="cuda", dtype=torch.bfloat16)
+    ops.attention_causal(q, k, v, out=wide[:, : hq * 128])
+    assert torch.equal(wide[:, hq * 128 :], torch.full_like(wide[:, hq * 128 :], 7.0))
+    ref = ops.attention_causal(q, k, v)
+    assert torch.equal(wide[:, : hq * 128], ref)
+    with pytest.raises(ValueError):
+        ops.attention_causal(q, k[:, :, :50].contiguous(), v)
+
+
 @pytest.mark.parametrize("m,k,half", [(544, 2048, 6144), (17, 1536, 256), (300, 256, 384)])
 def test_gemm_swiglu_bitwise(m, k, half):
     """gate|up GEMM with the SwiGLU epilogue == the gated pack's value

@@ -18,7 +18,15 @@ def bits_of(t):
     return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 256, 128), (17, 1536, 1536), (64, 2048, 4096), (300, 1536, 640), (544, 2048, 2048)])
+# Split K over a cluster: (17, 1536, 1536) over 4 ranks with ragged slices
+# of 1-2 K blocks, (64, 2048, 4096) over 4, (17, 4096, 608) over 8 with a
+# ragged last channel tile, (5, 6144, 1536) over 8 with 3 K blocks per rank;
+# the others run unsplit.
+@pytest.mark.parametrize(
+    "m,k,n",
+    [(1, 256, 128), (17, 1536, 1536), (64, 2048, 4096), (300, 1536, 640), (544, 2048, 2048),
+     (17, 4096, 608), (5, 6144, 1536)],
+)
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_nvfp4_gemm_matches_dequantized_product(m, k, n, with_bias):
     g = torch.Generator().manual_seed(m + k + n)

@@ -304,6 +304,45 @@ def test_swiglu_epilogue_fusion_is_bitwise():
         adapter.close()
 
 
+@torch.inference_mode()
+def test_text_attention_causal_kernel_matches_sdpa_path_and_restores():
+    """Quantized text attention with the causal row kernel == the same fused
+    layer on torch SDPA + transpose, to bf16 tolerance: the attention core
+    differs only in summation order, which may move a few o_proj input codes
+    by one step, so the check is on the relative error of the whole output."""
+    from pir2_b200.harness import DiTConfig, VLMConfig, build_policy
+    from pir2_b200.pointwise import TextAttentionFusion
+
+    policy = build_policy("cuda", dit=DiTConfig(layers=2), vlm=VLMConfig(layers=2, vocab=2048))
+    names = inventory(policy)[0]
+    executed = {n for n in names if n.startswith("backbone.layers")}
+    adapter = TransformerINT(policy, executed, native=True, expanded=True)
+    torch.manual_seed(11)
+    x = torch.randn(1, 544, 2048, device="cuda", dtype=torch.bfloat16)
+    cos, sin = policy.backbone.rope(544, x.device, x.dtype)
+    attns = [layer.self_attn for layer in policy.backbone.layers]
+    sdpa = TextAttentionFusion(policy, adapter, causal_kernel=False)
+    kernel = TextAttentionFusion(policy, adapter, causal_kernel=True)
+    try:
+        adapter.set("w8a8")
+        sdpa.set(8)
+        refs = [attn(x, cos, sin) for attn in attns]
+        sdpa.close()
+        kernel.set(8)
+        assert all("forward" in attn.__dict__ for attn in attns)
+        for attn, ref in zip(attns, refs):
+            out = attn(x, cos, sin).float()
+            err = (out - ref.float()).norm() / ref.float().norm()
+            assert err < 1e-2, float(err)
+        kernel.close()
+        assert all("forward" not in attn.__dict__ for attn in attns)
+    finally:
+        sdpa.close()
+        kernel.close()
+        adapter.close()
+    assert _lib.device_status() == 0
+
+
 @pytest.mark.parametrize("flags", [{"fp_grouped": True}, {"fp_rmsnorm": True}, {"fusion": True}])
 @torch.inference_mode()
 def test_fp4_session_refuses_unimplemented_floating_fusions(flags):

@@ -50,6 +50,11 @@ def test_argument_errors_are_reported_without_touching_the_device():
     assert status == _lib.EINVAL and b"head_dim" in lib.pir2b_last_error()
     status = lib.pir2b_attention_rows(None, 192, None, 192, None, 192, None, 192, 1, 1, 1 << 21, 4, 48, 1.0, None)
     assert status == _lib.EINVAL
+    # Causal attention: head_dim 64 is not instantiated; hq not a multiple of hk.
+    status = lib.pir2b_attention_causal(None, None, None, 1, 16, 16, 8, 64, 1.0, None, 2048, None)
+    assert status == _lib.EINVAL and b"head_dim 128" in lib.pir2b_last_error()
+    status = lib.pir2b_attention_causal(None, None, None, 1, 16, 12, 8, 128, 1.0, None, 2048, None)
+    assert status == _lib.EINVAL
 
 
 def _plan(lib, bits, m, npad, kpad):
