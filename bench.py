@@ -194,6 +194,9 @@ def gemm_bytes(s):
         # E2M1 operands (half a byte per value) + one UE4M3 factor per 16.
         return (s["n"] + s["m"]) * s["k"] * 9 // 16 + 2 * s["m"] * s["n"]
     wb = s["npad"] * s["k"] * s["bits"] // 8
+    if s.get("input") == "rows":
+        # Fused pack: the GEMM reads the bf16 rows themselves.
+        return wb + 2 * s["m"] * s["k_logical"] + 4 * s["npad"] + 2 * s["m"] * s["n"]
     return wb + s["m"] * s["k"] * s["bits"] // 8 + 4 * s["m"] + 4 * s["npad"] + 2 * s["m"] * s["n"]
 
 

@@ -208,6 +208,28 @@ int pir2b_dit_ffn_static(const void *qa, const float *sa, const void *up_w, cons
                          int down_bias_mode, const void *residual, int64_t ldr, int64_t m,
                          int64_t d, int64_t f, void *out, int64_t ldo, void *stream);
 
+/* pir2b_gemm with two options for chains of small-M projections.
+ *
+ * Fused activation pack (x non-null, qa and sa null): bf16 rows x[m, ldx]
+ * (m <= 64, k % 8 == 0, int8 weights) are quantized inside the GEMM by the
+ * plain symmetric-row-v1 pack (coexecution/kernels/ampere_ada/integer.py:
+ * 27-94, the pack pir2b_quant_rows runs), so the result is bitwise
+ * pir2b_quant_rows followed by pir2b_gemm, with one launch instead of two.
+ * Each CTA stages whole rows in shared memory to find the row maxima, or,
+ * when x_max is given ([m, x_parts] partial maxima of |x|, x_parts % 4 ==
+ * 0, e.g. the max_out of the GEMM that wrote x), only its own K slice.
+ * Returns PIR2B_EINVAL when the rows do not fit (then pack separately).
+ *
+ * max_out (non-null): also writes max_out[r, g] = max |out[r, 16g..16g+15]|
+ * for g < npad / 16 (the output's per-16-channel maxima, ready as the
+ * x_max of a fused pack of `out`); needs npad % 16 == 0 and 16-byte aligned
+ * output rows.  Exactly one of qa / x is non-null. */
+int pir2b_gemm_fused(const void *qa, const float *sa, const void *x, int64_t ldx, int64_t k,
+                     const float *x_max, int64_t x_parts, const void *qw, const float *sw,
+                     const void *bias, int bias_mode, const void *out_lut, const void *residual,
+                     int64_t ldr, int bits, int64_t m, int64_t npad, int64_t kpad, void *out,
+                     int64_t ldo, int64_t n_store, float *max_out, void *stream);
+
 /* W8A8 gate|up GEMM with the SwiGLU epilogue: out[m, c] =
  * bf16(f32(silu_lut[g]) * f32(u)) for c < half_n, where g and u are the
  * exact dequantized bf16 GEMM outputs of gate channel c and up channel c.

@@ -37,6 +37,10 @@ SIGNATURES = {
     "pir2b_gemm": [
         _P, _P, _P, _P, _P, _I, _P, _P, _I64, _I, _I64, _I64, _I64, _P, _I64, _I64, _I, _P,
     ],
+    "pir2b_gemm_fused": [
+        _P, _P, _P, _I64, _I64, _P, _I64, _P, _P, _P, _I, _P, _P, _I64, _I, _I64, _I64, _I64, _P, _I64,
+        _I64, _P, _P,
+    ],
     "pir2b_pack_nvfp4": [_P, _I64, _I64, _P, _P, _P],
     "pir2b_gemm_nvfp4": [_P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _P, _I64, _P],
     "pir2b_dit_ffn_workspace": [_I64, _I64],

@@ -61,6 +61,23 @@ struct GemmArgs {
   // channels and tile 1 the matching up channels; the CTA writes
   // bf16(silu_lut[gate] * up) for those 128 output channels.
   const __nv_bfloat16 *silu_lut;    // [65536] or null
+  // Fused activation pack (int8, one token tile): bf16 rows x[m, ldx]
+  // replace the packed activations.  The CTA bulk-copies the rows (its K
+  // slice when x_max gives the row maxima, else whole rows) into shared
+  // memory, derives the row scales and writes the int8 codes of its K
+  // slice in the swizzled operand layout.
+  const __nv_bfloat16 *x;           // null: packed activations through TMA
+  int64_t ldx;
+  int k;                            // logical K of x (codes past k are 0)
+  const float *x_max;               // [m, x_parts] partial |x| maxima, or null
+  int x_parts;
+  int fused_kb;                     // K blocks of codes the CTA holds
+  int x_stride;                     // bytes per staged row
+  int x_bytes;                      // staged rows region
+  // Per-16-channel |y| maxima of the bf16 output, [m, max_parts], or null:
+  // a later fused pack of this output reads them as its x_max.
+  float *max_out;
+  int max_parts;
 };
 
 cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,

@@ -350,11 +350,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(const Attn
 // q [B, HQ, T, 128], k and v [B, HK, T, 128] (the layout of
 // qk_norm_rope_kernel), output rows out[b*T + t, h*128 + d] for the o_proj
 // pack, replacing torch SDPA (is_causal, enable_gqa) and its transpose copy.
-// Grid (HQ, ceil(T / 64), B): a CTA takes 64 queries of one head, its four
-// warps 16 each; key/value blocks of 64 stream through a two-stage
-// cp.async ring (the block after the current one is in flight while the
-// current one is used); the same register-resident bf16 MMA + online
-// softmax as above, with keys after the query masked.
+// Grid (HQ, ceil(T / 64), B), eight warps per CTA: warp w takes queries
+// 16*(w & 3) .. +16 of the CTA's 64 and the key blocks of parity w >> 2, so
+// the two warp groups walk the causal key range side by side (half the
+// serial path of the last query tile).  Pairs of 64-key blocks stream
+// through a two-stage cp.async ring (the next pair in flight while the
+// current one is used); each warp keeps the register-resident bf16 MMA +
+// online softmax state of the row kernel, keys after the query masked, and
+// the groups' states (m, l, O) are merged through shared memory at the end.
 struct CausalArgs {
   const __nv_bfloat16 *q;
   const __nv_bfloat16 *k;
@@ -367,56 +370,62 @@ struct CausalArgs {
 
 constexpr int kCausalD = 128;
 constexpr int kCausalP = kCausalD + 8;           // odd number of 16-byte units
+constexpr int kCausalThreads = 256;
+constexpr int kCausalPair = 2 * kAttnKBlock;     // keys per ring stage
 
 __host__ __device__ inline size_t attention_causal_smem() {
-  return size_t(kAttnQTile) * kCausalP * 2 * 5;  // q tile + two K/V stages
+  // q tile + two stages of K and V for a pair of key blocks.
+  return size_t(kAttnQTile) * kCausalP * 2 + size_t(2) * 2 * kCausalPair * kCausalP * 2;
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attention_causal_kernel(const CausalArgs a) {
+__global__ void __launch_bounds__(kCausalThreads) attention_causal_kernel(const CausalArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   constexpr int D = kCausalD, P = kCausalP, KS = D / 16, DN = D / 8, NB = kAttnKBlock / 8;
   const int h = blockIdx.x, b = blockIdx.z;
   const int t0 = blockIdx.y * kAttnQTile;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q4 = lane & 3;
+  const int qg = warp & 3, kg = warp >> 2;
   const int kvh = h / (a.hq / a.hk);
   __nv_bfloat16 *qs = reinterpret_cast<__nv_bfloat16 *>(smem_raw);   // [64][P]
-  __nv_bfloat16 *kv = qs + kAttnQTile * P;                            // [2][K|V][64][P]
-  const __nv_bfloat16 *qg = a.q + ((int64_t(b) * a.hq + h) * a.T) * D;
-  const __nv_bfloat16 *kg = a.k + ((int64_t(b) * a.hk + kvh) * a.T) * D;
-  const __nv_bfloat16 *vg = a.v + ((int64_t(b) * a.hk + kvh) * a.T) * D;
+  __nv_bfloat16 *kv = qs + kAttnQTile * P;                            // [2][K|V][128][P]
+  const __nv_bfloat16 *qg_ptr = a.q + ((int64_t(b) * a.hq + h) * a.T) * D;
+  const __nv_bfloat16 *kg_ptr = a.k + ((int64_t(b) * a.hk + kvh) * a.T) * D;
+  const __nv_bfloat16 *vg_ptr = a.v + ((int64_t(b) * a.hk + kvh) * a.T) * D;
   constexpr int vecs = D / 8;
   const int tn = min(kAttnQTile, a.T - t0);
   const int nblocks = (min(a.T, t0 + kAttnQTile) + kAttnKBlock - 1) / kAttnKBlock;
+  const int npairs = (nblocks + 1) / 2;
 
   pdl_wait();
   pdl_launch_dependents();
-  for (int i = tid; i < kAttnQTile * vecs; i += kAttnThreads) {
+  for (int i = tid; i < kAttnQTile * vecs; i += kCausalThreads) {
     const int t = i / vecs, d0 = (i % vecs) * 8;
     if (t < tn)
-      cp_async_16(qs + t * P + d0, qg + int64_t(t0 + t) * D + d0);
+      cp_async_16(qs + t * P + d0, qg_ptr + int64_t(t0 + t) * D + d0);
     else
       *reinterpret_cast<uint4 *>(qs + t * P + d0) = make_uint4(0, 0, 0, 0);
   }
-  auto load_block = [&](int kb, int stage) {
-    __nv_bfloat16 *ks = kv + stage * 2 * kAttnKBlock * P;
-    __nv_bfloat16 *vs = ks + kAttnKBlock * P;
-    for (int i = tid; i < kAttnKBlock * vecs; i += kAttnThreads) {
+  auto load_pair = [&](int pair, int stage) {
+    __nv_bfloat16 *ks = kv + stage * 2 * kCausalPair * P;
+    __nv_bfloat16 *vs = ks + kCausalPair * P;
+    const int kend = min(a.T, nblocks * kAttnKBlock);   // keys any query here can see
+    for (int i = tid; i < kCausalPair * vecs; i += kCausalThreads) {
       const int j = i / vecs, d0 = (i % vecs) * 8;
-      const int key = kb * kAttnKBlock + j;
-      if (key < a.T) {
-        cp_async_16(ks + j * P + d0, kg + int64_t(key) * D + d0);
-        cp_async_16(vs + j * P + d0, vg + int64_t(key) * D + d0);
+      const int key = pair * kCausalPair + j;
+      if (key < kend) {
+        cp_async_16(ks + j * P + d0, kg_ptr + int64_t(key) * D + d0);
+        cp_async_16(vs + j * P + d0, vg_ptr + int64_t(key) * D + d0);
       } else {
         *reinterpret_cast<uint4 *>(ks + j * P + d0) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4 *>(vs + j * P + d0) = make_uint4(0, 0, 0, 0);
       }
     }
   };
-  load_block(0, 0);
-  cp_async_commit();                               // group: q tile + block 0
+  load_pair(0, 0);
+  cp_async_commit();                               // group: q tile + pair 0
 
-  const int r0 = warp * 16;
+  const int r0 = qg * 16;
   const bool active = r0 < tn;
   float o[DN][4];
 #pragma unroll
@@ -425,16 +434,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_causal_kernel(const Ca
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
   uint32_t qa[KS][4];
   const int t_lo = t0 + r0 + g, t_hi = t_lo + 8;    // this thread's query rows
-  for (int kb = 0; kb < nblocks; ++kb) {
-    if (kb + 1 < nblocks) {
-      load_block(kb + 1, (kb + 1) & 1);
+  for (int pr = 0; pr < npairs; ++pr) {
+    if (pr + 1 < npairs) {
+      load_pair(pr + 1, (pr + 1) & 1);
       cp_async_commit();
       cp_async_wait_group<1>();
     } else {
       cp_async_wait_group<0>();
     }
     __syncthreads();
-    if (kb == 0 && active) {
+    if (pr == 0 && active) {
 #pragma unroll
       for (int s = 0; s < KS; ++s) {
         const int row = r0 + (lane & 15);
@@ -442,10 +451,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_causal_kernel(const Ca
         ldsm_x4(smem_u32(qs) + uint32_t((row * P + col) * 2), qa[s][0], qa[s][1], qa[s][2], qa[s][3]);
       }
     }
-    // A block whose keys all come after the warp's last query adds nothing.
-    if (active && kb * kAttnKBlock <= t0 + r0 + 15) {
-      const uint32_t ks_addr = smem_u32(kv + (kb & 1) * 2 * kAttnKBlock * P);
-      const uint32_t vs_addr = ks_addr + uint32_t(kAttnKBlock * P * 2);
+    const int kb = 2 * pr + kg;
+    // A block past the tile or after the warp's last query adds nothing.
+    if (active && kb < nblocks && kb * kAttnKBlock <= t0 + r0 + 15) {
+      const uint32_t ks_addr =
+          smem_u32(kv + (pr & 1) * 2 * kCausalPair * P + kg * kAttnKBlock * P);
+      const uint32_t vs_addr = ks_addr + uint32_t(kCausalPair * P * 2);
       float s_acc[NB][4];
 #pragma unroll
       for (int n = 0; n < NB; ++n) {
@@ -480,8 +491,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_causal_kernel(const Ca
       bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 1));
       bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, 2));
       const float mn_lo = fmaxf(m_lo, bm_lo), mn_hi = fmaxf(m_hi, bm_hi);
-      // Key 0 is visible to every query, so m is finite from block 0 on;
-      // the guards only keep exp(-inf - -inf) out.
+      // A row with every key so far masked keeps m = -inf and adds nothing;
+      // the guards keep exp(-inf - -inf) out.
       const float al_lo = (m_lo == -INFINITY) ? 0.f : expf(m_lo - mn_lo);
       const float al_hi = (m_hi == -INFINITY) ? 0.f : expf(m_hi - mn_hi);
       m_lo = mn_lo;
@@ -522,31 +533,56 @@ __global__ void __launch_bounds__(kAttnThreads) attention_causal_kernel(const Ca
     }
     __syncthreads();   // this stage is refilled by the next iteration's prefetch
   }
-  if (!active)
-    return;
   l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
   l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
   l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
   l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-  const float i_lo = 1.0f / l_lo, i_hi = 1.0f / l_hi;
+  // Merge: the odd-block warps leave (m, l, O) in the (now idle) K/V ring,
+  // the even-block warps of the same queries fold them in and store.  Key 0
+  // lies in block 0, so the even group's m is finite for every query.
+  float *xo = reinterpret_cast<float *>(kv);                // [4][DN][4][32]
+  float *xs = xo + 4 * DN * 4 * 32;                         // [4][4][32]: m_lo m_hi l_lo l_hi
+  if (kg == 1 && active) {
+#pragma unroll
+    for (int n = 0; n < DN; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        xo[((qg * DN + n) * 4 + e) * 32 + lane] = o[n][e];
+    xs[(qg * 4 + 0) * 32 + lane] = m_lo;
+    xs[(qg * 4 + 1) * 32 + lane] = m_hi;
+    xs[(qg * 4 + 2) * 32 + lane] = l_lo;
+    xs[(qg * 4 + 3) * 32 + lane] = l_hi;
+  }
+  __syncthreads();
+  if (kg == 1 || !active)
+    return;
+  const float m1_lo = xs[(qg * 4 + 0) * 32 + lane], m1_hi = xs[(qg * 4 + 1) * 32 + lane];
+  const float l1_lo = xs[(qg * 4 + 2) * 32 + lane], l1_hi = xs[(qg * 4 + 3) * 32 + lane];
+  const float mm_lo = fmaxf(m_lo, m1_lo), mm_hi = fmaxf(m_hi, m1_hi);
+  const float a0_lo = expf(m_lo - mm_lo), a0_hi = expf(m_hi - mm_hi);
+  const float a1_lo = m1_lo == -INFINITY ? 0.f : expf(m1_lo - mm_lo);
+  const float a1_hi = m1_hi == -INFINITY ? 0.f : expf(m1_hi - mm_hi);
+  const float i_lo = 1.0f / (l_lo * a0_lo + l1_lo * a1_lo);
+  const float i_hi = 1.0f / (l_hi * a0_hi + l1_hi * a1_hi);
 #pragma unroll
   for (int n = 0; n < DN; ++n) {
+    const float *x = xo + ((qg * DN + n) * 4) * 32 + lane;
+    const float v0 = (o[n][0] * a0_lo + x[0] * a1_lo) * i_lo;
+    const float v1 = (o[n][1] * a0_lo + x[32] * a1_lo) * i_lo;
+    const float v2 = (o[n][2] * a0_hi + x[64] * a1_hi) * i_hi;
+    const float v3 = (o[n][3] * a0_hi + x[96] * a1_hi) * i_hi;
     const int d = h * D + n * 8 + 2 * q4;
-    if (t_lo < a.T) {
-      __nv_bfloat16 *dst = a.out + (int64_t(b) * a.T + t_lo) * a.ldo + d;
-      *reinterpret_cast<uint32_t *>(dst) = pack_bf16x2(o[n][0] * i_lo, o[n][1] * i_lo);
-    }
-    if (t_hi < a.T) {
-      __nv_bfloat16 *dst = a.out + (int64_t(b) * a.T + t_hi) * a.ldo + d;
-      *reinterpret_cast<uint32_t *>(dst) = pack_bf16x2(o[n][2] * i_hi, o[n][3] * i_hi);
-    }
+    if (t_lo < a.T)
+      *reinterpret_cast<uint32_t *>(a.out + (int64_t(b) * a.T + t_lo) * a.ldo + d) = pack_bf16x2(v0, v1);
+    if (t_hi < a.T)
+      *reinterpret_cast<uint32_t *>(a.out + (int64_t(b) * a.T + t_hi) * a.ldo + d) = pack_bf16x2(v2, v3);
   }
 }
 
 cudaError_t run_attention_causal(const CausalArgs &a, int B, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(a.hq), unsigned((a.T + kAttnQTile - 1) / kAttnQTile), unsigned(B));
-  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.blockDim = dim3(kCausalThreads, 1, 1);
   cfg.dynamicSmemBytes = attention_causal_smem();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

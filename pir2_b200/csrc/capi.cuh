@@ -235,6 +235,50 @@ static bool plan_small_m(int bits, int64_t m, int ntiles, int num_kb, int max_sm
   return true;
 }
 
+// Fused activation pack (bf16 rows in, int8 codes made by the GEMM CTA):
+// the small-M plan with weight-only stages, plus a region for the codes of
+// the CTA's K slice and one for the staged bf16 rows.
+struct FusedInput {
+  const void *x;
+  int64_t ldx;
+  int64_t k;
+  const float *x_max;
+  int64_t x_parts;
+  int fused_kb;
+  int x_stride;
+  int x_bytes;
+};
+
+static size_t gemm_smem_fused(int bn, int stages, int fused_kb, int x_bytes) {
+  return 1024 + size_t(stages) * 16384 + size_t(fused_kb) * bn * 128 + size_t(x_bytes) + 1024 +
+         (4 * stages + 1) * 8 + 16;
+}
+
+static bool plan_fused(int64_t m, int ntiles, int num_kb, int max_smem, FusedInput *fin,
+                       GemmPlan *plan) {
+  GemmPlan p;
+  if (m > 64 || !plan_small_m(8, m, ntiles, num_kb, max_smem, &p))
+    return false;
+  const int fused_kb = (num_kb + p.splits - 1) / p.splits;
+  const bool parts = fin->x_max != nullptr;
+  const int x_stride = parts ? fused_kb * 256 : int((fin->k * 2 + 15) / 16 * 16);
+  const int x_bytes = int(m) * x_stride;
+  // The split-K partial tile and the rank's staging slice reuse the stages.
+  const int min_stages = p.splits > 1 ? int((size_t(p.bn) * 640 + 16383) / 16384) : 2;
+  int stages = std::max(std::max(2, min_stages), std::min(p.stages, fused_kb));
+  while (stages > std::max(2, min_stages) &&
+         gemm_smem_fused(p.bn, stages, fused_kb, x_bytes) > size_t(max_smem))
+    --stages;
+  const size_t smem = gemm_smem_fused(p.bn, stages, fused_kb, x_bytes);
+  if (smem > size_t(max_smem) || size_t(m) * x_stride >= (size_t(1) << 20))
+    return false;
+  fin->fused_kb = fused_kb;
+  fin->x_stride = x_stride;
+  fin->x_bytes = x_bytes;
+  *plan = GemmPlan{p.bn, 1, p.splits, stages, smem};
+  return true;
+}
+
 // Picks the token tile, the number of token tiles, the split-K cluster size,
 // the stage count and the weight tiles per CTA (small M: plan_small_m;
 // larger M: the cost model below).
@@ -359,17 +403,34 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
                        const float *sw, const void *bias, int bias_mode, const void *out_lut,
                        const void *residual, int64_t ldr, const void *silu_lut, int bits,
                        int64_t m, int64_t npad, int64_t kpad, void *out, int64_t ldo,
-                       int64_t n_store, void *stream) {
+                       int64_t n_store, void *stream, const FusedInput *fin = nullptr,
+                       float *max_out = nullptr) {
   const uint64_t row_bytes = bits == 8 ? uint64_t(kpad) : uint64_t(kpad / 2);
   const uint32_t box_cols = bits == 8 ? 128u : 64u;
   CUtensorMap tm_w, tm_a;
+  memset(&tm_a, 0, sizeof(tm_a));
   if (int r = make_map(&tm_w, qw, row_bytes, uint64_t(npad), row_bytes,
                        box_cols, 128u, bits == 8))
     return r;
-  if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, box_cols,
-                       uint32_t(plan.bn), bits == 8))
-    return r;
+  if (fin == nullptr) {
+    if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, box_cols,
+                         uint32_t(plan.bn), bits == 8))
+      return r;
+  }
   GemmArgs args;
+  memset(&args, 0, sizeof(args));
+  if (fin != nullptr) {
+    args.x = static_cast<const __nv_bfloat16 *>(fin->x);
+    args.ldx = fin->ldx;
+    args.k = int(fin->k);
+    args.x_max = fin->x_max;
+    args.x_parts = int(fin->x_parts);
+    args.fused_kb = fin->fused_kb;
+    args.x_stride = fin->x_stride;
+    args.x_bytes = fin->x_bytes;
+  }
+  args.max_out = max_out;
+  args.max_parts = int(npad / 16);
   args.sa = sa;
   args.sw = sw;
   args.bias = bias_mode == PIR2B_BIAS_ADD
@@ -389,6 +450,12 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   args.splits = plan.splits;
   args.wt = plan.wt;
   args.silu_lut = static_cast<const __nv_bfloat16 *>(silu_lut);
+  // A plan outside the kernel's shapes never reaches the device.
+  if (args.bn < 16 || args.bn > 256 || args.bn % 16 != 0 || args.stages < 2 ||
+      (args.splits != 1 && args.splits != 2 && args.splits != 4 && args.splits != 8) ||
+      (args.wt != 1 && args.wt != 2) || args.num_kb < args.splits || plan.smem == 0)
+    return fail(PIR2B_EINVAL, "internal: GEMM plan out of range (bn=%d stages=%d splits=%d wt=%d)",
+                args.bn, args.stages, args.splits, args.wt);
   // The epilogue stages the tile (or, with split-K, each cluster rank's
   // channel slice) in shared memory and writes it with one TMA store when
   // the output rows are 16-byte aligned; otherwise it stores directly.
@@ -846,6 +913,81 @@ int pir2b_gemm_nvfp4(const void *qa, const void *sfa, const void *qw,
   cfg.numAttrs = splits > 1 ? 2 : 1;
   return cuda_status(cudaLaunchKernelEx(&cfg, gemm_fp4_kernel, tm_w, tm_a, tm_out, args),
                      "gemm_nvfp4 launch");
+}
+
+int pir2b_gemm_fused(const void *qa, const float *sa, const void *x, int64_t ldx, int64_t k,
+                     const float *x_max, int64_t x_parts, const void *qw, const float *sw,
+                     const void *bias, int bias_mode, const void *out_lut, const void *residual,
+                     int64_t ldr, int bits, int64_t m, int64_t npad, int64_t kpad, void *out,
+                     int64_t ldo, int64_t n_store, float *max_out, void *stream) {
+  if (bits != 4 && bits != 8)
+    return fail(PIR2B_EINVAL, "bits must be 4 or 8, got %d", bits);
+  if (bias_mode < 0 || bias_mode > 2)
+    return fail(PIR2B_EINVAL, "bias_mode must be 0, 1 or 2");
+  if (m < 1 || m > 0x7fffffffLL || npad < 8 || npad % 8 != 0 || kpad < 128 ||
+      kpad % 128 != 0 || npad > 0x7fffffffLL || kpad > (1LL << 20))
+    return fail(PIR2B_EINVAL, "GEMM requires m >= 1, npad %% 8 == 0 and kpad %% 128 == 0");
+  if (n_store < 1 || n_store > npad || ldo < n_store)
+    return fail(PIR2B_EINVAL, "n_store must be in [1, npad] and ldo >= n_store");
+  if ((qa == nullptr) == (x == nullptr))
+    return fail(PIR2B_EINVAL, "gemm_fused takes packed activations (qa, sa) or bf16 rows x, not both");
+  if (qw == nullptr || sw == nullptr || out == nullptr)
+    return fail(PIR2B_EINVAL, "GEMM operands must be non-null");
+  if (bias_mode == PIR2B_BIAS_ADD && bias == nullptr)
+    return fail(PIR2B_EINVAL, "bias_mode ADD needs a bias vector");
+  if (!aligned(qw, 16) || !aligned(out, 2) || !aligned(sw, 4) || (bias && !aligned(bias, 2)) ||
+      (out_lut && !aligned(out_lut, 2)) || (residual && !aligned(residual, 2)))
+    return fail(PIR2B_EALIGN, "weight/scale/bias/output alignment not met");
+  if (residual != nullptr && ldr < n_store)
+    return fail(PIR2B_EINVAL, "residual row stride ldr must be >= n_store");
+  FusedInput fin;
+  memset(&fin, 0, sizeof(fin));
+  if (x != nullptr) {
+    if (bits != 8 || m > 64)
+      return fail(PIR2B_EINVAL, "the fused pack takes int8 weights and at most 64 token rows");
+    if (k < 8 || k % 8 != 0 || (k + 127) / 128 * 128 != kpad || ldx < k || ldx % 8 != 0)
+      return fail(PIR2B_EINVAL, "fused pack: need k %% 8 == 0, kpad = ceil(k/128)*128, ldx >= k, ldx %% 8 == 0");
+    if (!aligned(x, 16))
+      return fail(PIR2B_EALIGN, "fused pack: x must be 16-byte aligned");
+    if (x_max != nullptr && (x_parts < 4 || x_parts % 4 != 0 || x_parts > (1 << 20) ||
+                             !aligned(x_max, 16)))
+      return fail(PIR2B_EINVAL, "fused pack: x_max needs x_parts %% 4 == 0 and 16-byte alignment");
+    fin.x = x;
+    fin.ldx = ldx;
+    fin.k = k;
+    fin.x_max = x_max;
+    fin.x_parts = x_max != nullptr ? x_parts : 0;
+  } else {
+    if (sa == nullptr)
+      return fail(PIR2B_EINVAL, "packed activations need their row scales");
+    if (!aligned(qa, 16) || !aligned(sa, 4))
+      return fail(PIR2B_EALIGN, "packed activations must be 16-byte aligned");
+  }
+  if (max_out != nullptr) {
+    if (npad % 16 != 0 || !aligned(max_out, 4))
+      return fail(PIR2B_EINVAL, "max_out needs npad %% 16 == 0 and a 4-byte aligned buffer");
+    if (ldo % 8 != 0 || !aligned(out, 16))
+      return fail(PIR2B_EINVAL, "max_out needs 16-byte aligned output rows (ldo %% 8 == 0)");
+  }
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  GemmPlan plan;
+  if (x != nullptr) {
+    if (!plan_fused(m, int((npad + 127) / 128), int(kpad / 128), dev->max_smem, &fin, &plan))
+      return fail(PIR2B_EINVAL, "fused pack: the rows do not fit one CTA's shared memory "
+                                "(m=%lld k=%lld npad=%lld)", (long long)m, (long long)k,
+                  (long long)npad);
+  } else {
+    plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem);
+    if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
+        plan.smem > size_t(dev->max_smem))
+      return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",
+                  (long long)m, (long long)npad, (long long)kpad);
+  }
+  return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, out_lut, residual, ldr, nullptr, bits,
+                     m, npad, kpad, out, ldo, n_store, stream, x != nullptr ? &fin : nullptr,
+                     max_out);
 }
 
 int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const float *sw,

@@ -46,15 +46,6 @@ constexpr int kFp4BlockBytes = 128;          // 256 fp4 elements per row
 constexpr int kFp4WeightTile = 128 * kFp4BlockBytes;
 constexpr int kSfStageBytes = 2048;          // four 512-byte atoms
 
-__device__ __forceinline__ void bulk_load(void *dst, const void *src,
-                                          uint32_t bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
-      "[%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Descriptor of one scale atom in shared memory for tcgen05.cp: 32 rows of
 // 16 contiguous bytes, no swizzle (8-row core matrices 128 bytes apart).
 __device__ __forceinline__ uint64_t sf_atom_desc(uint32_t saddr) {

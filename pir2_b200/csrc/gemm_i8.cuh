@@ -31,6 +31,7 @@
 #pragma once
 #include "args.cuh"
 #include "ptx.cuh"
+#include "quant.cuh"
 
 namespace pir2b {
 
@@ -106,6 +107,127 @@ __device__ __forceinline__ void unpack_int4_stage(const uint8_t *src,
   }
 }
 
+// Per-16-channel maxima of |y| over a staged bf16 output tile [rows][width]
+// (width a multiple of 16), written to max_out[m0 + j, group0 + g].
+__device__ __forceinline__ void store_group_max(const GemmArgs &args, const __nv_bfloat16 *stage,
+                                                int width, int rows, int m0, int group0, int et) {
+  const int groups = width / 16;
+  for (int it = et; it < rows * groups; it += 128) {
+    const int j = it / groups, g = it - j * groups;
+    const uint4 *p = reinterpret_cast<const uint4 *>(stage + j * width + g * 16);
+    float mx = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 u = p[h];
+      const __nv_bfloat162 *v = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(v[i]);
+        mx = fmaxf(mx, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+    if (group0 + g < args.max_parts)
+      args.max_out[int64_t(m0 + j) * args.max_parts + group0 + g] = mx;
+  }
+}
+
+// Fused activation pack, run by the four epilogue warps (et = 0..127) of a
+// CTA whose token tile starts at m0.  The symmetric-row-v1 quantization of
+// the plain pack (integer.py:27-94: s = max|x| * (1/127), 1 for an all-zero
+// row; q = clamp(rint(x / s), -127, 127); zero codes past K and for padding
+// rows), written straight into this CTA's operand tiles:
+//  1. one thread bulk-copies the rows (the K slice only when x_max holds
+//     the row maxima, else whole rows) into shared memory;
+//  2. row maxima from x_max (float bits compared as integers: every value
+//     is a non-negative maximum) or from the staged whole rows;
+//  3. the scales go to s_sa for the epilogue, and the codes of K blocks
+//     [kb_begin, kb_begin + nkb) to the 128-byte-swizzled K-major tiles.
+__device__ __forceinline__ void fused_pack(const GemmArgs &args, uint8_t *xs, uint8_t *codes,
+                                           float *s_sa, uint64_t *xbar, int bn, int m0,
+                                           int kb_begin, int nkb, int et) {
+  const int rows = min(bn, args.m - m0);
+  const int col0 = kb_begin * kBlockK;
+  const bool parts = args.x_max != nullptr;
+  const int xcol0 = parts ? col0 : 0;
+  const int xcols = parts ? min(nkb * kBlockK, args.k - col0) : args.k;
+  const int lane = et & 31;
+  if (et == 0) {
+    mbar_arrive_expect_tx(xbar, uint32_t(rows * xcols * 2));
+    for (int r = 0; r < rows; ++r)
+      bulk_load(xs + r * args.x_stride, args.x + int64_t(m0 + r) * args.ldx + xcol0,
+                uint32_t(xcols * 2), xbar);
+  }
+  int *s_max = reinterpret_cast<int *>(s_sa);
+  for (int j = et; j < bn; j += 128)
+    s_max[j] = 0;
+  named_barrier(1, 128);
+  if (parts) {
+    // x_parts % 4 == 0: every float4 lies within one row.
+    const float4 *src = reinterpret_cast<const float4 *>(args.x_max + int64_t(m0) * args.x_parts);
+    const int total4 = rows * args.x_parts / 4;
+#pragma unroll 4
+    for (int f = et; f < total4; f += 128) {
+      const float4 v = __ldg(src + f);
+      const float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      atomicMax(s_max + (4 * f) / args.x_parts, __float_as_int(mx));
+    }
+  }
+  mbar_wait(xbar, 0, kStatusTimeoutConvert);
+  if (!parts) {
+    for (int r = et >> 5; r < rows; r += 4) {
+      const uint4 *row = reinterpret_cast<const uint4 *>(xs + r * args.x_stride);
+      float mx = 0.f;
+      for (int c = lane; c < xcols / 8; c += 32) {
+        const uint4 u = row[c];
+        const __nv_bfloat162 *v = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(v[i]);
+          mx = fmaxf(mx, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+#pragma unroll
+      for (int d = 16; d; d >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+      if (lane == 0)
+        s_max[r] = __float_as_int(mx);
+    }
+  }
+  named_barrier(1, 128);
+  for (int j = et; j < bn; j += 128) {
+    const float mx = __int_as_float(s_max[j]);
+    s_sa[j] = j < rows ? row_scale<8>(mx) : 0.f;
+  }
+  named_barrier(1, 128);
+  const int per_block = bn * 8;   // 16-byte code chunks per K block
+  for (int it = et; it < nkb * per_block; it += 128) {
+    const int b = it / per_block, rem = it - b * per_block;
+    const int j = rem >> 3, c = rem & 7;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (j < rows) {
+      const float s = s_sa[j];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = col0 + b * kBlockK + c * 16 + h * 8;
+        if (col < args.k) {
+          const uint4 u = *reinterpret_cast<const uint4 *>(xs + j * args.x_stride + (col - xcol0) * 2);
+          const __nv_bfloat16 *v = reinterpret_cast<const __nv_bfloat16 *>(&u);
+          uint32_t q[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = __float2int_rn(__fdiv_rn(__bfloat162float(v[i]), s));
+            q[i] = uint32_t(max(-127, min(127, r)) & 255);
+          }
+          w[2 * h] = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
+          w[2 * h + 1] = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
+        }
+      }
+    }
+    *reinterpret_cast<uint4 *>(codes + b * per_block * 16 + j * 128 + ((c ^ (j & 7)) << 4)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // kBits == 8: operands arrive as int8 through TMA in the swizzled layout.
 // kBits == 4: operands arrive as packed int4 (64 bytes per row and K block,
 // no swizzle) and the four epilogue warps unpack them per stage.
@@ -132,18 +254,25 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int wt = kBits == 8 ? args.wt : 1;
   const int op_a_bytes = wt * kWeightTileBytes;   // unpacked int8 weight tile(s)
   const int op_b_bytes = bn * kBlockK;            // unpacked int8 token tile
-  const int stage_bytes = op_a_bytes + op_b_bytes;
+  // Fused pack: the token codes of all of this CTA's K blocks sit in their
+  // own region, so the ring stages hold weights only.
+  const bool fused = kBits == 8 && args.x != nullptr;
+  const int stage_bytes = op_a_bytes + (fused ? 0 : op_b_bytes);
   // W4A4 keeps the packed TMA destination next to the unpacked operands.
   const int packed_bytes = (kBits == 4) ? (kTileN + bn) * 64 : 0;
   const int packed_stride = (packed_bytes + 1023) & ~1023;
   uint8_t *packed_base = smem + stages * stage_bytes;
-  float *s_sa = reinterpret_cast<float *>(packed_base + stages * packed_stride);
+  uint8_t *codes = packed_base + stages * packed_stride;            // [fused_kb][bn][128]
+  uint8_t *xs = codes + (fused ? args.fused_kb * op_b_bytes : 0);   // staged bf16 rows
+  float *s_sa = reinterpret_cast<float *>(xs + (fused ? args.x_bytes : 0));
   uint64_t *bars = reinterpret_cast<uint64_t *>(s_sa + 256);
   uint64_t *full = bars;                  // TMA -> consumer
   uint64_t *empty = bars + stages;        // MMA done -> producer
   uint64_t *ready = bars + 2 * stages;    // (W4A4) unpacked -> MMA
   uint64_t *accum_full = bars + 3 * stages;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * stages + 1);
+  uint64_t *xbar = bars + 3 * stages + 1;   // (fused) staged rows landed
+  uint64_t *cbar = bars + 3 * stages + 2;   // (fused) codes written -> MMA
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * stages + 3);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -163,9 +292,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&ready[s], 128);
     }
     mbar_init(accum_full, 1);
+    if (fused) {
+      mbar_init(xbar, 1);
+      mbar_init(cbar, 128);
+    }
     fence_barrier_init();
     tma_prefetch_desc(&tm_w);
-    tma_prefetch_desc(&tm_a);
+    if (!fused)
+      tma_prefetch_desc(&tm_a);
     if (args.tma_store)
       tma_prefetch_desc(&tm_out);
   }
@@ -190,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t wpolicy =
           gridDim.y == 1 ? policy_evict_first() : policy_evict_last();
       const uint32_t tx = (kBits == 8) ? uint32_t(stage_bytes)
-                                       : uint32_t((kTileN + bn) * 64);
+                                       : uint32_t((kTileN + bn) * 64);   // fused: weights only
       const int kstep = kBits == 8 ? kBlockK : 64;
       // Weight tiles of the first ring pass do not depend on the previous
       // kernel: issue them before waiting on it.
@@ -205,11 +339,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           tma_load_2d_hint(dst + kWeightTileBytes, &tm_w, &full[i], (kb_begin + i) * kstep,
                            n0 + kTileN, wpolicy);
       }
-      pdl_wait();
-      for (int i = 0; i < pre; ++i) {
-        uint8_t *dst = kBits == 8 ? smem + i * stage_bytes + op_a_bytes
-                                  : packed_base + i * packed_stride + kTileN * 64;
-        tma_load_2d(dst, &tm_a, &full[i], (kb_begin + i) * kstep, m0);
+      if (!fused) {
+        pdl_wait();
+        for (int i = 0; i < pre; ++i) {
+          uint8_t *dst = kBits == 8 ? smem + i * stage_bytes + op_a_bytes
+                                    : packed_base + i * packed_stride + kTileN * 64;
+          tma_load_2d(dst, &tm_a, &full[i], (kb_begin + i) * kstep, m0);
+        }
       }
       for (int i = pre; i < nkb; ++i) {
         const int s = i % stages;
@@ -223,7 +359,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           tma_load_2d_hint(a, &tm_w, &full[s], kx, n0, wpolicy);
           if (wt == 2)
             tma_load_2d_hint(a + kWeightTileBytes, &tm_w, &full[s], kx, n0 + kTileN, wpolicy);
-          tma_load_2d(a + op_a_bytes, &tm_a, &full[s], kx, m0);
+          if (!fused)
+            tma_load_2d(a + op_a_bytes, &tm_a, &full[s], kx, m0);
         } else {
           uint8_t *p = packed_base + s * packed_stride;
           tma_load_2d_hint(p, &tm_w, &full[s], kx, n0, wpolicy);
@@ -235,7 +372,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ------------------------------------------------------------ MMA issue
     if (elect_one_sync()) {
       const uint32_t idesc = idesc_i8(kTileN, bn);
-      bool ok = true;
+      // Fused pack: every K block's codes are written before the first MMA.
+      bool ok = !fused || mbar_wait(cbar, 0, kStatusTimeoutMma);
       for (int i = 0; i < nkb && ok; ++i) {
         const int s = i % stages;
         const uint32_t phase = (i / stages) & 1;
@@ -245,7 +383,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
-        const uint32_t b_addr = a_addr + op_a_bytes;
+        const uint32_t b_addr =
+            fused ? smem_u32(codes + i * op_b_bytes) : a_addr + op_a_bytes;
 #pragma unroll
         for (int k = 0; k < kBlockK / 32; ++k) {
           mma_i8(tmem_base, smem_desc_sw128(a_addr + k * 32),
@@ -265,9 +404,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ------------------------------------------------------------ epilogue
     const int et = threadIdx.x - 64;   // 0..127
     pdl_wait();
-    // Token scales of this tile, once, while the main loop runs.
-    for (int j = et; j < bn; j += 128)
-      s_sa[j] = (m0 + j < args.m) ? __ldg(args.sa + m0 + j) : 0.f;
+    if (fused) {
+      fused_pack(args, xs, codes, s_sa, xbar, bn, m0, kb_begin, nkb, et);
+      fence_proxy_async_smem();   // the codes are read by the tensor cores
+      mbar_arrive(cbar);
+    } else {
+      // Token scales of this tile, once, while the main loop runs.
+      for (int j = et; j < bn; j += 128)
+        s_sa[j] = (m0 + j < args.m) ? __ldg(args.sa + m0 + j) : 0.f;
+    }
     named_barrier(1, 128);
     if (kBits == 4) {
       for (int i = 0; i < nkb; ++i) {
@@ -386,6 +531,8 @@ __global__ void __launch_bounds__(kThreads, 2)
               tma_store_2d(&tm_out, stage, n0 + w * kTileN, m0);
               tma_store_commit_and_wait();
             }
+            if (args.max_out != nullptr)
+              store_group_max(args, stage, kTileN, valid_m, m0, (n0 + w * kTileN) / 16, et);
           }
         }
       } else {
@@ -405,7 +552,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   if (args.splits > 1) {
-    // Every thread of every CTA in the cluster takes part in both barriers.
+    // Every thread of every CTA in the cluster takes part in both phases of
+    // the cluster barrier: phase 1 (a full sync) publishes the partial
+    // tiles; phase 2 is split, each thread arriving once its reads of the
+    // peers' tiles are done and waiting only before exit, so the epilogue
+    // math and stores overlap it while no CTA leaves before its peers have
+    // read its tile.
     cluster_sync();
     if (warp >= 2) {
       // Rank r reduces and writes channels [r*slice, (r+1)*slice) of the
@@ -439,29 +591,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Staging tile [bn][slice] bf16 after the partial sums.
       __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem + size_t(bn) * kTileN * 4);
       const bool tma = args.tma_store != 0;
+      const bool with_res = args.residual != nullptr;
       const int jend = tma ? bn : valid_m;
-      for (int j = et / tpt; j < jend; j += tstride) {
-        const uint32_t off = uint32_t(j * kTileN * 4);
-        int4 v[8];
-#pragma unroll
-        for (int p = 0; p < 8; ++p)
-          if (p < splits)
-            v[p] = ld_cluster_v4(peer_base[p] + off);
-        int acc[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int p = 0; p < 8; ++p)
-          if (p < splits) {
-            acc[0] += v[p].x;
-            acc[1] += v[p].y;
-            acc[2] += v[p].z;
-            acc[3] += v[p].w;
-          }
+      const int first = et / tpt;
+      // Writes the four outputs of token j from its summed partials.
+      auto finish = [&](int j, const int (&acc)[4], const float (&res)[4]) {
         __nv_bfloat16 o[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           o[i] = epilogue_value(acc[i], s_sa[j], sw[i], b[i], args.bias_mode, lut);
-          if (args.residual != nullptr && in_range[i] && j < valid_m)
-            o[i] = add_residual(o[i], args, m0 + j, cc + i);
+          if (with_res && in_range[i] && j < valid_m)
+            o[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o[i]), res[i]));
         }
         if (tma) {
           __nv_bfloat162 *d = reinterpret_cast<__nv_bfloat162 *>(stage + j * slice + cl);
@@ -473,7 +613,40 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (in_range[i])
               args.out[int64_t(m0 + j) * args.ldo + cc + i] = o[i];
         }
+      };
+      // Sums the peers' partials of token j (and loads its residual values
+      // alongside the distributed-shared-memory loads).
+      auto gather = [&](int j, int (&acc)[4], float (&res)[4]) {
+        const uint32_t off = uint32_t(j * kTileN * 4);
+        int4 v[8];
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          if (p < splits)
+            v[p] = ld_cluster_v4(peer_base[p] + off);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          res[i] = 0.f;
+          if (with_res && in_range[i] && j < valid_m)
+            res[i] = __bfloat162float(args.residual[int64_t(m0 + j) * args.ldr + cc + i]);
+        }
+        acc[0] = acc[1] = acc[2] = acc[3] = 0;
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          if (p < splits) {
+            acc[0] += v[p].x;
+            acc[1] += v[p].y;
+            acc[2] += v[p].z;
+            acc[3] += v[p].w;
+          }
+      };
+      for (int j = first; j < jend; j += tstride) {
+        int acc[4];
+        float res[4];
+        gather(j, acc, res);
+        finish(j, acc, res);
       }
+      // Every read of a peer's tile by this thread is done.
+      cluster_arrive();
       if (tma) {
         fence_proxy_async_smem();
         named_barrier(1, 128);
@@ -481,9 +654,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           tma_store_2d(&tm_out, stage, n0 + int(rank) * slice, m0);
           tma_store_commit_and_wait();
         }
+        if (args.max_out != nullptr)
+          store_group_max(args, stage, slice, valid_m, m0, (n0 + int(rank) * slice) / 16, et);
       }
+    } else {
+      cluster_arrive();
     }
-    cluster_sync();
+    cluster_wait();
   }
 
   tc_fence_before();

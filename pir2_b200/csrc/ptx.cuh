@@ -269,6 +269,17 @@ __device__ __forceinline__ void tma_store_commit_and_wait() {
                    : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory, completing on an
+// mbarrier (both addresses 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src,
+                                          uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 16-byte asynchronous global -> shared copies (all in flight until the
 // wait).
 __device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
@@ -306,6 +317,17 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                "barrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
+}
+
+// The two halves of cluster_sync, for work between them.  Not .aligned:
+// they are reached from role-specific code where the lanes of a warp need
+// not be converged (an elected lane may still be issuing copies).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // Maps a shared::cta address of this CTA to the same offset in CTA `rank` of

@@ -20,7 +20,11 @@ quantized projection, keeping the model's own forward code:
   epilogue (the same torch-built LUT applied to its bf16 output), so the down
   projection packs plain values: the codes are identical, and the LUT
   gathers run once per output element inside a kernel that is already
-  running.
+  running;
+* with the fused pack enabled (`integer.FUSED_PACK_ROWS`, off by default)
+  and few W8A8 rows, the up GEMM also writes the per-16-channel maxima of
+  its output and the down GEMM packs that output inside itself from them
+  (`IntegerLinear.forward_rows`): one launch fewer, the same codes.
 
 Results are bitwise those of the unfused quantized model: the epilogue adds
 the residual to the bf16 GEMM output in fp32 and rounds once, exactly as
@@ -29,7 +33,7 @@ torch's bf16 addition does.
 
 import torch
 
-from . import ops
+from . import integer, ops
 from .connections import packed_input
 from .fused import prepare_gelu, prepare_silu
 from .linear import prepare
@@ -145,6 +149,22 @@ class ResidualFusion:
                     residual = down_q.__dict__.pop("_pending_residual")
                     out = ops.dit_ffn(packed.data, packed.scales, up_q, down_q, lut, residual)
                     return out.reshape(x.shape)
+                if (
+                    bits == 8
+                    and integer.FUSED_PACK_ROWS > 0
+                    and self.controller.candidates is None
+                    and up_q.packed_weight.shape[0] % 16 == 0
+                ):
+                    maxes = torch.empty(
+                        (packed.data.shape[0], up_q.packed_weight.shape[0] // 16),
+                        device=packed.data.device, dtype=torch.float32,
+                    )
+                    hidden = up_q.forward_packed(packed, out_lut=lut, max_out=maxes)
+                    if down_q.fused_pack_ok(hidden, with_max=True):
+                        # The down projection packs gelu(up(x)) inside its
+                        # GEMM from the up GEMM's per-16-channel maxima.
+                        return down_q.forward_rows(hidden, x_max=maxes)
+                    return self.controller.dispatch(down_q, hidden)
                 hidden = up_q.forward_packed(packed, out_lut=lut)      # gelu(up(x)), bf16
                 return self.controller.dispatch(down_q, hidden)
 

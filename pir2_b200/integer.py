@@ -30,6 +30,16 @@ def load_integer_extension():
 # the int8 kernel reads its operands by TMA with no in-kernel unpack.
 WIDE_INT4_ROWS = 64
 
+# W8A8 layers given plain bf16 rows can pack them inside the GEMM (one
+# launch instead of pack + GEMM, bitwise the same output) up to
+# FUSED_PACK_ROWS rows and, when each GEMM CTA stages whole rows,
+# FUSED_PACK_BYTES of them.  Off by default (0 rows): inside the control
+# step the in-CTA pack (row copy, row maxima and divisions run by four warps
+# of every CTA) costs more than the separate pack launch it removes (action
+# head 4.05 vs 3.15 ms on one box).
+FUSED_PACK_ROWS = 0
+FUSED_PACK_BYTES = 96 * 1024
+
 
 @dataclass
 class PackedActivation:
@@ -157,7 +167,7 @@ class IntegerLinear(torch.nn.Module):
             return _lib.BIAS_ADD
         return _lib.BIAS_NONE if self.biasless_epilogue else _lib.BIAS_ZERO
 
-    def forward_packed(self, packed, out_lut=None, residual=None):
+    def forward_packed(self, packed, out_lut=None, residual=None, max_out=None):
         """GEMM of a pack with this layer's weights.  `residual` (bf16, same
         leading shape, `out_features` wide) is added in the epilogue: the
         bf16 result plus the residual in fp32, rounded to bf16 again.  A
@@ -186,8 +196,47 @@ class IntegerLinear(torch.nn.Module):
             residual=residual,
             n_store=self.out_features,
             tactic=self.tactic,
+            max_out=max_out,
         )
         return out.reshape(*packed.shape, self.out_features)
+
+    def fused_pack_ok(self, x, *, with_max=False):
+        """Whether `forward_rows` takes these bf16 rows (with_max: the row
+        maxima come from x_max, so only K slices are staged)."""
+        if (
+            self.bits != 8
+            or not isinstance(x, torch.Tensor)
+            or x.dtype != torch.bfloat16
+            or not x.is_cuda
+            or x.dim() < 2
+            or x.stride(-1) != 1
+            or x.shape[-1] != self.in_features
+            or self.in_features % 8
+        ):
+            return False
+        rows = x.numel() // x.shape[-1]
+        return 1 <= rows <= FUSED_PACK_ROWS and (with_max or rows * x.shape[-1] * 2 <= FUSED_PACK_BYTES)
+
+    def forward_rows(self, x, x_max=None, out_lut=None, max_out=None):
+        """GEMM of bf16 rows with the plain activation pack fused into the
+        GEMM kernel: bitwise `forward_packed(prepare_activation(x, 8))`.
+        `x_max` (fp32 [rows, parts]) may carry the rows' |x| maxima, e.g. the
+        `max_out` of the layer that produced x."""
+        rows = x.reshape(-1, x.shape[-1])
+        residual = self.__dict__.pop("_pending_residual", None)
+        out = ops.gemm_rows(
+            rows,
+            self.packed_weight,
+            self.weight_scale,
+            self.bias,
+            x_max=x_max,
+            bias_mode=self._bias_mode(),
+            out_lut=out_lut,
+            residual=residual,
+            n_store=self.out_features,
+            max_out=max_out,
+        )
+        return out.reshape(*x.shape[:-1], self.out_features)
 
     def wide_weight(self):
         """The int4 weights unpacked to int8 containers, made once per

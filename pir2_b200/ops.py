@@ -143,14 +143,24 @@ def norm_quant_rows(
     return data, scales, residual
 
 
-def gemm(a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, residual=None, n_store=None, out=None, tactic=-1):
+def gemm(
+    a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, residual=None, n_store=None, out=None, tactic=-1,
+    max_out=None,
+):
     """Quantized GEMM + dequant epilogue -> bf16 [m, n_store] (or into `out`).
 
     bias_mode defaults to piR2's `gemm` semantics: add the bias, or +0 when
     the bias is None.  Pass _lib.BIAS_NONE for `gemm_biasless` without bias.
     `residual` (bf16 [m, >= n_store], unit column stride) is added to the
     bf16 result in fp32 and rounded again (the residual epilogue).
+    `max_out` (fp32 [m, npad/16]) also receives the output's per-16-channel
+    maxima of |y| (see `gemm_rows`).
     """
+    if max_out is not None:
+        return _gemm_fused(
+            w, sw, bias, bits, qa=a, sa=sa, bias_mode=bias_mode, out_lut=out_lut, residual=residual,
+            n_store=n_store, out=out, max_out=max_out,
+        )
     m = a.shape[0]
     n_pad = w.shape[0]
     k_pad = a.shape[1] * (2 if bits == 4 else 1)
@@ -180,6 +190,79 @@ def gemm(a, sa, w, sw, bias, bits, *, bias_mode=None, out_lut=None, residual=Non
     _lib.check(status, "pir2b_gemm")
     if recorder is not None:
         recorder.after(a.device, bits=bits, m=m, n=n_store, k=k_pad, npad=n_pad)
+    return out
+
+
+def gemm_rows(x, w, sw, bias, *, x_max=None, bias_mode=None, out_lut=None, residual=None, n_store=None,
+              out=None, max_out=None):
+    """W8A8 GEMM of bf16 rows with the activation pack fused into the GEMM.
+
+    x: bf16 [m <= 64, k] rows (unit column stride, k % 8 == 0); the result
+    is bitwise `gemm(*quant_rows(x, 8), w, ...)` in one launch.  `x_max`
+    (fp32 [m, parts], parts % 4 == 0) holds partial maxima of |x| covering
+    each row, e.g. the `max_out` of the GEMM that wrote x; without it each
+    CTA stages whole rows to find the maxima.  Raises ValueError when the
+    rows do not fit the kernel (the caller packs separately then).
+    """
+    return _gemm_fused(
+        w, sw, bias, 8, x=x, x_max=x_max, bias_mode=bias_mode, out_lut=out_lut, residual=residual,
+        n_store=n_store, out=out, max_out=max_out,
+    )
+
+
+def _gemm_fused(w, sw, bias, bits, *, qa=None, sa=None, x=None, x_max=None, bias_mode=None, out_lut=None,
+                residual=None, n_store=None, out=None, max_out=None):
+    src = qa if qa is not None else x
+    m = src.shape[0]
+    n_pad = w.shape[0]
+    if x is not None:
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+            raise ValueError("gemm_rows needs bf16 [m, k] rows with unit column stride")
+        k = x.shape[1]
+        k_pad = kpad(k)
+        ldx = x.stride(0) if m > 1 else k
+    else:
+        k = 0
+        k_pad = qa.shape[1] * (2 if bits == 4 else 1)
+        ldx = 0
+    if w.shape[1] * (2 if bits == 4 else 1) != k_pad:
+        raise ValueError("weights do not match the activation width")
+    if n_store is None:
+        n_store = n_pad
+    if bias_mode is None:
+        bias_mode = _lib.BIAS_ADD if bias is not None else _lib.BIAS_ZERO
+    if out is None:
+        out = torch.empty((m, n_store), device=w.device, dtype=torch.bfloat16)
+    ldo = out.stride(0) if out.ndim == 2 else n_store
+    if out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError("GEMM output must be BF16 with unit column stride")
+    ldr = 0
+    if residual is not None:
+        residual = residual.reshape(m, -1) if residual.dim() != 2 else residual
+        if residual.dtype != torch.bfloat16 or residual.stride(-1) != 1 or residual.shape[1] < n_store:
+            raise ValueError("Residual must be BF16 [M, >= N] with unit column stride")
+        ldr = residual.stride(0) if m > 1 else residual.shape[1]
+    parts = 0
+    if x_max is not None:
+        if x_max.dtype != torch.float32 or x_max.dim() != 2 or x_max.shape[0] != m or not x_max.is_contiguous():
+            raise ValueError("x_max must be contiguous fp32 [m, parts]")
+        parts = x_max.shape[1]
+    if max_out is not None and (
+        max_out.dtype != torch.float32 or max_out.shape != (m, n_pad // 16) or not max_out.is_contiguous()
+    ):
+        raise ValueError("max_out must be contiguous fp32 [m, npad / 16]")
+    recorder = launch_recorder
+    if recorder is not None:
+        recorder.before(w.device)
+    status = _lib.lib().pir2b_gemm_fused(
+        _ptr(qa), _ptr(sa), _ptr(x), ldx, k, _ptr(x_max), parts, w.data_ptr(), sw.data_ptr(), _ptr(bias),
+        bias_mode, _ptr(out_lut), _ptr(residual), ldr, bits, m, n_pad, k_pad, out.data_ptr(), ldo, n_store,
+        _ptr(max_out), _stream(w.device),
+    )
+    _lib.check(status, "pir2b_gemm_fused")
+    if recorder is not None:
+        recorder.after(w.device, bits=bits, m=m, n=n_store, k=k_pad, npad=n_pad,
+                       input="rows" if x is not None else "packed", k_logical=k)
     return out
 
 

@@ -73,6 +73,9 @@ class TransformerINT:
                 return result
         if getattr(x, "_robotics_packed_input", False):
             return q.forward_packed(x.for_bits(q.bits))
+        if lut is None and up is None and q.fused_pack_ok(x):
+            # Few W8A8 rows: the plain pack runs inside the GEMM.
+            return q.forward_rows(x)
         return q.forward_packed(prepare(x, q.bits, lut, up))
 
     def _pack_dispatch_input(self, q, x, lut=None, up=None):

@@ -362,6 +362,91 @@ def test_attention_rows_strided_query_and_argument_errors():
         ops.attention_rows(q, long_kv[:, :w], long_kv[:, w:], batch=1, heads=heads, head_dim=d)
 
 
+def _int8_layer(g, n, k, bias=True):
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    qw, sw = oracle.quantize_weight(oracle.bf16_bits_to_f32(bits_of(w)), 8)
+    b = None
+    if bias:
+        b = np.zeros(qw.shape[0], dtype=np.uint16)
+        b[:n] = bits_of((torch.randn(n, generator=g) * 0.01).to(torch.bfloat16))
+        b = to_dev(b)
+    return torch.from_numpy(qw).cuda(), torch.from_numpy(sw).cuda(), b
+
+
+@pytest.mark.parametrize(
+    "m,k,n",
+    [
+        (17, 1536, 1536),   # DiT o-proj: 8-rank split-K, 1-2 K blocks per rank
+        (1, 1536, 1536),
+        (32, 1536, 4608),
+        (17, 2048, 3072),
+        (5, 328, 200),      # ragged K (kpad 384) and channels
+        (64, 1024, 1024),
+    ],
+)
+@pytest.mark.parametrize("residual", [False, True])
+def test_gemm_rows_fused_pack_equals_pack_then_gemm(m, k, n, residual):
+    """The in-GEMM activation pack gives bitwise the pack kernel + GEMM."""
+    g = torch.Generator().manual_seed(m * 3 + k + n)
+    x = randn_bf16(g, m, k, outliers=True).cuda()
+    qw, sw, b = _int8_layer(g, n, k)
+    res = randn_bf16(g, m, n).cuda() if residual else None
+    qa, sa = ops.quant_rows(x, 8)
+    want = ops.gemm(qa, sa, qw, sw, b, 8, n_store=n, residual=res)
+    got = ops.gemm_rows(x, qw, sw, b, n_store=n, residual=res)
+    assert np.array_equal(bits_of(got), bits_of(want))
+    # A strided view of wider rows reads only the first k columns.
+    wide = torch.cat([x, randn_bf16(g, m, 64).cuda()], 1)
+    got2 = ops.gemm_rows(wide[:, :k], qw, sw, b, n_store=n, residual=res)
+    assert np.array_equal(bits_of(got2), bits_of(want))
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("m,d,f", [(17, 1536, 6144), (3, 256, 1024), (32, 512, 2048)])
+def test_gemm_max_out_feeds_the_next_fused_pack(m, d, f):
+    """up GEMM (GELU table epilogue) writes per-16-channel |y| maxima; the
+    down GEMM packs the up output inside itself from those maxima and its own
+    K slice: bitwise the pack kernel + GEMM chain."""
+    from pir2_b200.fused import prepare_gelu
+
+    g = torch.Generator().manual_seed(m + d + f)
+    x = randn_bf16(g, m, d, outliers=True).cuda()
+    up_w, up_s, up_b = _int8_layer(g, f, d)
+    dn_w, dn_s, dn_b = _int8_layer(g, d, f)
+    lut = prepare_gelu(torch.device("cuda"), torch.bfloat16, "tanh")
+    res = randn_bf16(g, m, d).cuda()
+    qa, sa = ops.quant_rows(x, 8)
+    h_ref = ops.gemm(qa, sa, up_w, up_s, up_b, 8, n_store=f, out_lut=lut)
+    maxes = torch.full((m, up_w.shape[0] // 16), -1.0, device="cuda")
+    h = ops.gemm(qa, sa, up_w, up_s, up_b, 8, n_store=f, out_lut=lut, max_out=maxes)
+    assert np.array_equal(bits_of(h), bits_of(h_ref))
+    want_max = h_ref.float().abs().reshape(m, -1, 16).amax(-1)
+    assert torch.equal(maxes, want_max)
+    qh, sh = ops.quant_rows(h_ref, 8)
+    want = ops.gemm(qh, sh, dn_w, dn_s, dn_b, 8, n_store=d, residual=res)
+    got = ops.gemm_rows(h, dn_w, dn_s, dn_b, x_max=maxes, n_store=d, residual=res)
+    assert np.array_equal(bits_of(got), bits_of(want))
+    # The fused pack can itself emit maxima for a following one.
+    m2 = torch.full((m, dn_w.shape[0] // 16), -1.0, device="cuda")
+    got3 = ops.gemm_rows(h, dn_w, dn_s, dn_b, x_max=maxes, n_store=d, residual=res, max_out=m2)
+    assert np.array_equal(bits_of(got3), bits_of(want))
+    assert torch.equal(m2, want.float().abs().reshape(m, -1, 16).amax(-1))
+    assert_status_clean()
+
+
+def test_gemm_rows_rejects_what_it_cannot_fuse():
+    g = torch.Generator().manual_seed(1)
+    qw, sw, b = _int8_layer(g, 256, 8192)
+    with pytest.raises(ValueError):
+        ops.gemm_rows(randn_bf16(g, 65, 8192).cuda(), qw, sw, b)    # more than one token tile
+    with pytest.raises(ValueError):
+        ops.gemm_rows(randn_bf16(g, 64, 8192).cuda(), qw, sw, b)    # whole rows exceed shared memory
+    qw2, sw2, b2 = _int8_layer(g, 256, 100)
+    with pytest.raises(ValueError):
+        ops.gemm_rows(randn_bf16(g, 4, 100).cuda(), qw2, sw2, b2)   # k % 8 != 0
+    assert_status_clean()
+
+
 @pytest.mark.parametrize("rows,k", [(1, 128), (544, 2048), (37, 6144), (4096, 1536)])
 def test_unpack_int4_matches_oracle(rows, k):
     g = np.random.default_rng(rows + k)

@@ -13,7 +13,7 @@ import pytest
 import torch
 
 import oracle
-from pir2_b200 import _lib
+from pir2_b200 import _lib, ops
 from pir2_b200.connections import AdditionalConnections
 from pir2_b200.fused import prepare_gelu
 from pir2_b200.integer import prepare_activation
@@ -240,11 +240,14 @@ def test_dit_attention_fusion_matches_sdpa_forward_and_restores(cross):
     torch.testing.assert_close(fused.float(), reference.float(), atol=2e-2, rtol=2e-2)
 
 
-@pytest.mark.parametrize("bits,ffn_kernel", [(8, False), (8, True), (4, False)])
+@pytest.mark.parametrize("bits,ffn_kernel,fused_pack", [(8, False, False), (8, True, False), (4, False, False), (8, False, True)])
 @torch.inference_mode()
-def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits, ffn_kernel):
+def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits, ffn_kernel, fused_pack, monkeypatch):
     """Residual adds in the o-proj / down-proj epilogues and the FFN GELU in
-    the up-projection epilogue give bitwise the unfused quantized blocks."""
+    the up-projection epilogue give bitwise the unfused quantized blocks;
+    so does the opt-in in-GEMM activation pack (o-proj from whole rows,
+    down-proj from the up GEMM's per-16-channel maxima)."""
+    from pir2_b200 import integer
     from pir2_b200.fusion import ResidualFusion
     from pir2_b200.harness import DiTConfig, VLMConfig, build_policy
 
@@ -267,9 +270,17 @@ def test_residual_and_gelu_epilogue_fusion_is_bitwise(bits, ffn_kernel):
             ctx = context if block.attn1.is_cross_attention else None
             outs.append(block(x, encoder_hidden_states=ctx, temb=temb))
         fusion.set(bits, norm_pack=False)
+        if fused_pack:
+            monkeypatch.setattr(integer, "FUSED_PACK_ROWS", 64)
+            monkeypatch.setattr(integer, "FUSED_PACK_BYTES", 128 * 1024)   # 34 rows of 1536
+            calls = []
+            original = ops.gemm_rows
+            monkeypatch.setattr(ops, "gemm_rows", lambda *a, **k: calls.append(k.get("x_max") is not None) or original(*a, **k))
         for block, ref in zip(model.transformer_blocks, outs):
             ctx = context if block.attn1.is_cross_attention else None
             equal(block(x, encoder_hidden_states=ctx, temb=temb), ref)
+        if fused_pack:
+            assert True in calls and False in calls   # down-proj from maxima, o-proj from whole rows
     finally:
         fusion.close()
         adapter.close()
