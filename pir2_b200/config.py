@@ -57,6 +57,9 @@ class OptimizationConfig:
     compiled_host_guards: bool = False
     fusion_mode: str = "all"
     operator_profile: Path | None = None
+    # Packed-weight cache file (weight_cache): loaded when present and valid
+    # for these weights, written after quantizing when absent.
+    packed_weights: Path | None = None
 
     def __post_init__(self):
         floating = ("fp8", "fp4")
@@ -132,6 +135,10 @@ class OptimizationConfig:
                 "Norm quantization fusion requires fusion and low-bit precision",
             ),
             (self.residual_norm_quant and not self.norm_modulation_quant, "Residual fusion requires norm_modulation_quant"),
+            (
+                self.packed_weights is not None and self.precision not in ("w8a8", "w4a4"),
+                "A packed-weight cache requires precision=w8a8 or w4a4",
+            ),
         ]
         for failed, message in checks:
             if failed:

@@ -155,9 +155,27 @@ class GrootOptimizations:
         from .producers import QuantizationProducers
         from .transformer import TransformerINT
 
+        packed = None
+        cache = self.config.packed_weights
+        if cache is not None and Path(cache).exists():
+            from . import weight_cache
+
+            modules = dict(model.named_modules())
+            packed = weight_cache.load(cache, {n: modules[n] for n in executed}, next(model.parameters()).device)
+            self.coverage["packed_weights"] = {"path": str(cache), "loaded": True}
         self.controller = TransformerINT(
-            model, set(executed), native=True, expanded=expanded, condition_group=self.config.group_conditioning
+            model,
+            set(executed),
+            native=True,
+            expanded=expanded,
+            condition_group=self.config.group_conditioning,
+            packed=packed,
         )
+        if cache is not None and packed is None:
+            from . import weight_cache
+
+            weight_cache.save(self.controller, cache)
+            self.coverage["packed_weights"] = {"path": str(cache), "loaded": False, "written": True}
         self.stack.callback(self.controller.close)
         self.extra = AdditionalConnections(SimpleNamespace(model=model), self.controller, categories)
         self.stack.callback(self.extra.close)
@@ -213,6 +231,8 @@ class GrootOptimizations:
             if key in self._configuration_file_hashes and actual != self._configuration_file_hashes[key]:
                 raise RuntimeError(f"Installed optimization configuration file changed: {key}")
             config[key] = None if path is None else {"sha256": actual}
+        if config.get("packed_weights") is not None:
+            config["packed_weights"] = str(config["packed_weights"])
         return {
             "config": config,
             "coverage": self.coverage,

@@ -16,7 +16,7 @@ from .projections import inventory
 
 
 class TransformerINT:
-    def __init__(self, model, executed, native=False, expanded=False, condition_group=False):
+    def __init__(self, model, executed, native=False, expanded=False, condition_group=False, packed=None):
         sites, groups, activations, text = inventory(model, expanded)
         if condition_group:
             dit = model.action_head.model
@@ -30,9 +30,15 @@ class TransformerINT:
         self.groups = [g for g in groups if all(n in self.sites for n in g)]
         self.activations = [a for a in activations if a[2] in self.sites]
         self.text = [(m, n) for m, n in text if n in self.sites]
+        # `packed` ({site: {bits: (packed_weight, weight_scale, bias)}}, from
+        # weight_cache.load) skips install-time quantization.
         self.quant = {
             bits: {
-                n: PreparedLinear.from_linear(m, bits=bits, pack_reuse=True, biasless_epilogue=True)
+                n: (
+                    PreparedLinear(*packed[n][bits], m.in_features, m.out_features, bits, 0, True, True)
+                    if packed is not None
+                    else PreparedLinear.from_linear(m, bits=bits, pack_reuse=True, biasless_epilogue=True)
+                )
                 for n, (m, _, _) in self.sites.items()
             }
             for bits in (8, 4)
