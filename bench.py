@@ -42,6 +42,7 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # probe (8188 MAC/clk/SM x 148 SMs at the sampled clock): 4.5 POPS.
 INT8_PEAK_TOPS = 4520.0
 FP4_NOMINAL_TOPS = 9000.0
+FP8_NOMINAL_TOPS = 4500.0
 
 
 def parse():
@@ -50,7 +51,7 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--precision", choices=["w8a8", "w4a4", "fp4"], default="w8a8")
+    p.add_argument("--precision", choices=["w8a8", "w4a4", "fp4", "fp8"], default="w8a8")
     p.add_argument("--batch", type=int, default=1, help="robots per GPU")
     p.add_argument(
         "--robots",
@@ -193,6 +194,8 @@ def gemm_bytes(s):
     if s["bits"] == "fp4":
         # E2M1 operands (half a byte per value) + one UE4M3 factor per 16.
         return (s["n"] + s["m"]) * s["k"] * 9 // 16 + 2 * s["m"] * s["n"]
+    if s["bits"] == "fp8":
+        s = dict(s, bits=8)   # one byte per E4M3 value, like int8
     wb = s["npad"] * s["k"] * s["bits"] // 8
     if s.get("input") == "rows":
         # Fused pack: the GEMM reads the bf16 rows themselves.
@@ -251,11 +254,14 @@ def roofline(engine, hbm_peak, peak_kind, precision):
             large["ops"] += 2.0 * s["m"] * s["n"] * s["k"]
             large["n"] += 1
     total = small["t"] + large["t"]
+    peak_tops = {"fp4": FP4_NOMINAL_TOPS, "fp8": FP8_NOMINAL_TOPS}.get(precision, INT8_PEAK_TOPS)
     achieved = small["bytes"] / (small["t"] * 1e-3) / 1e9 if small["t"] else 0.0
     tops = large["ops"] / (large["t"] * 1e-3) / 1e12 if large["t"] else 0.0
     return {
         "_gemm_ms_small": small["t"],
-        "kernel": ("gemm_fp4_kernel" if precision == "fp4" else f"gemm_i8_kernel<{precision[1]}>")
+        "kernel": {"fp4": "gemm_fp4_kernel", "fp8": "gemm_i8_kernel<9> (kind::f8f6f4)"}.get(
+            precision, f"gemm_i8_kernel<{precision[1:2]}>"
+        )
         + " small-M (M<=64) launches",
         "bound": "hbm",
         "achieved": round(achieved, 1),
@@ -273,11 +279,12 @@ def roofline(engine, hbm_peak, peak_kind, precision):
             "bound": "tensor",
             "launches": large["n"],
             "achieved_tops": round(tops, 1),
-            "peak_tops": INT8_PEAK_TOPS if precision != "fp4" else FP4_NOMINAL_TOPS,
-            "frac": round(tops / (INT8_PEAK_TOPS if precision != "fp4" else FP4_NOMINAL_TOPS), 4),
-            "peak_source": "measured int8 kind::i8 issue-rate probe"
-            if precision != "fp4"
-            else "nominal dense FP4 (no measured FP4 peak)",
+            "peak_tops": peak_tops,
+            "frac": round(tops / peak_tops, 4),
+            "peak_source": {
+                "fp4": "nominal dense FP4 (no measured FP4 peak)",
+                "fp8": "nominal dense FP8 (no measured FP8 peak)",
+            }.get(precision, "measured int8 kind::i8 issue-rate probe"),
         },
     }
 
@@ -338,7 +345,7 @@ def run_reference(args, world, rank):
         "higher_is_better": False,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1"}[args.precision],
+        "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1", "fp8": "e4m3"}[args.precision],
         "data": "synthetic",
         "config": {
             "workload": f"GR00T-shaped control step, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
@@ -360,8 +367,8 @@ def build_engine(args, local):
 
     device = torch.device("cuda", local)
     policy = harness.build_policy(device)
-    if args.precision == "fp4":
-        config = OptimizationConfig(precision="fp4", scope="all")
+    if args.precision in ("fp4", "fp8"):
+        config = OptimizationConfig(precision=args.precision, scope="all")
     else:
         config = OptimizationConfig(
             precision=args.precision,
@@ -448,7 +455,7 @@ def run_ours(args, world, rank, local):
             "higher_is_better": False,
             "scaling": "weak" if args.robots is None else "strong",
             "vs_baseline": None,
-            "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1"}[args.precision],
+            "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1", "fp8": "e4m3"}[args.precision],
             "data": "synthetic",
             "config": {
                 "workload": f"GR00T-shaped control step per GPU, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
@@ -555,6 +562,8 @@ def run_kernel(args):
     from pir2_b200 import ops
 
     m, k, n = (int(v) for v in args.kernel.split(","))
+    if args.precision not in ("w8a8", "w4a4"):
+        raise SystemExit("--kernel times the integer GEMM (--precision w8a8 or w4a4)")
     bits = 8 if args.precision == "w8a8" else 4
     kp, npd = ops.kpad(k), ops.npad(n)
     wbytes = npd * kp * bits // 8

@@ -123,6 +123,10 @@ int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
  * (pir2_integer_epilogue::gemm with a residual, epilogue.py:360-398);
  * out: bf16, row stride ldo, columns [0, n_store) written.
  * kpad % 128 == 0, npad % 8 == 0, n_store <= npad, m >= 1.
+ * The weight tiles are requested before the kernel's programmatic-dependent
+ * wait (they overlap the previous kernel): qw, like every GEMM weight in
+ * this header, must not be written by the kernel launched just before on
+ * the same stream (weights are packed at install time).
  * tactic: -1 selects the tile shape by heuristic; piR2's Ada tactic ids
  * 0..7 are accepted and ignored (tiles are chosen for B200). */
 int pir2b_gemm(const void *qa, const float *sa, const void *qw,
@@ -229,6 +233,36 @@ int pir2b_gemm_fused(const void *qa, const float *sa, const void *x, int64_t ldx
                      const void *bias, int bias_mode, const void *out_lut, const void *residual,
                      int64_t ldr, int bits, int64_t m, int64_t npad, int64_t kpad, void *out,
                      int64_t ldo, int64_t n_store, float *max_out, void *stream);
+
+/* Per-tensor E4M3 quantization of bf16 rows x[rows, ldx] (k % 8 == 0) into
+ * q[rows, k] and one fp32 scale, the FP8 path's activation and weight pack:
+ *   fast == 0: coexecution/kernels/blackwell/csrc/fp8_cutlass_linear.cu:
+ *     61-120 (quantize_bf16 / pack_linear_weight): scale = max(amax/448,
+ *     1e-12), q = e4m3_rn_satfinite(clamp(x * (1/scale), +-448));
+ *   fast != 0: coexecution/optimization/backends/thor/packing.py:451-519
+ *     (prepare_fp8): scale = max(amax * (1/448), 1e-12), q = e4m3(clamp(
+ *     x / scale, +-448)) with round-to-nearest division;
+ * amax is the maximum of the finite |x|.  The scale is also written to
+ * scale_rep[0..n_rep) (null when n_rep == 0), the replicated vector the
+ * FP8 GEMM reads as per-row or per-channel scales.  One launch.  weights
+ * != 0 when q are GEMM weights: every GEMM entry of this library reads its
+ * weights before its programmatic-dependent wait (they are normally packed
+ * at install time), so a weight pack launched right before a GEMM must not
+ * let it start early; with weights != 0 it does not. */
+int pir2b_quant_fp8(const void *x, int64_t ldx, int64_t rows, int64_t k, int fast, int weights,
+                    void *q, float *scale, float *scale_rep, int64_t n_rep, void *stream);
+
+/* E4M3 GEMM on tcgen05 kind::f8f6f4 with fp32 accumulation:
+ *   out[m, n] = bf16(f32(f32(acc * sa[m]) * sw[n]) [+ bias[n]]) [+ residual]
+ * with the per-tensor scales given as replicated vectors (sa: m floats,
+ * sw: npad floats, from pir2b_quant_fp8).  Replaces the CUTLASS FP8 GEMM
+ * (fp8_cutlass_linear.cu:470-665, linear_forward_packed_tactic :1026-1145,
+ * whose epilogue applies scale_a * scale_b and the per-column bias).
+ * qa [m, kpad], qw [npad, kpad] E4M3 bytes, kpad % 128 == 0. */
+int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float *sw,
+                   const void *bias, int bias_mode, const void *residual, int64_t ldr, int64_t m,
+                   int64_t npad, int64_t kpad, void *out, int64_t ldo, int64_t n_store,
+                   void *stream);
 
 /* W8A8 gate|up GEMM with the SwiGLU epilogue: out[m, c] =
  * bf16(f32(silu_lut[g]) * f32(u)) for c < half_n, where g and u are the

@@ -6,10 +6,12 @@ forward: for W8A8 / W4A4 the symmetric-row-v1 activation pack (quant.py
 the per-channel weight quantization (`quantize_weight`, integer.py:211-256),
 the exact int32 product and the epilogue of integer_gemm.cu:37-59; for fp4
 the NVFP4 pack of both operands (thor/packing.py:24-54) and the fp64
-dequantized product.  Everything between the Linears (norms, attention,
+dequantized product; for fp8 the per-tensor E4M3 quantization of both
+operands (fp8_cutlass_linear.cu:61-120, `quant_fp8`) and the fp64 product
+times scale_a * scale_b plus bias.  Everything between the Linears (norms, attention,
 activations) stays plain torch on whatever device the policy lives on; the
 Linears compute on the host and return to that device.  Linears the fp4 path cannot
-take (K % 256 or N % 32) stay bf16, as on the GPU.
+take (K % 256 or N % 32) stay bf16, as on the GPU; for fp8 that is K % 128 or N % 16.
 """
 
 import numpy as np
@@ -64,6 +66,20 @@ def _nvfp4_forward(module):
     return forward
 
 
+def _fp8_forward(module, fast=False):
+    qw, sw = oq.quant_fp8(_bits_of(module.weight))
+    bias = None if module.bias is None else _bits_of(module.bias)
+    n, k = module.out_features, module.in_features
+
+    def forward(x):
+        lead = x.shape[:-1]
+        qa, sa = oq.quant_fp8(_bits_of(x.reshape(-1, k)), fast=fast)
+        y = oq.fp8_gemm(qa, sa, qw, sw, bias)
+        return _from_bits(oq.f32_to_bf16_bits(y.astype(np.float32)), lead, n, x.device)
+
+    return forward
+
+
 def install_oracle_linears(policy, precision):
     """Replace every bf16 Linear's forward (instance attribute) in place."""
     for module in policy.modules():
@@ -73,6 +89,10 @@ def install_oracle_linears(policy, precision):
             if module.in_features % 256 or module.out_features % 32:
                 continue
             module.forward = _nvfp4_forward(module)
+        elif precision == "fp8":
+            if module.in_features % 128 or module.out_features % 16:
+                continue
+            module.forward = _fp8_forward(module)
         else:
             module.forward = _integer_forward(module, {"w8a8": 8, "w4a4": 4}[precision])
     return policy

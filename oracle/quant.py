@@ -36,6 +36,9 @@ __all__ = [
     "pack_nvfp4",
     "unpack_nvfp4",
     "nvfp4_gemm",
+    "quant_fp8",
+    "e4m3_decode",
+    "fp8_gemm",
 ]
 
 F32 = np.float32
@@ -413,3 +416,51 @@ def nvfp4_gemm(pa, sfa, pw, sfw, m, n, k, bias_bits=None, alpha=1.0):
     if bias_bits is not None:
         y = y + bf16_bits_to_f32(bias_bits).astype(np.float64)[None, :]
     return f32_to_bf16_bits(y.astype(F32))
+
+
+# ----------------------------------------------------------------- FP8
+def quant_fp8(x_bits, *, fast=False):
+    """Per-tensor E4M3 quantization of bf16 values.
+
+    Default: fp8_cutlass_linear.cu:61-120 (quantize_bf16, also the weight
+    pack pack_linear_weight :1011-1024): amax of the finite |x| (fp32),
+    scale = max(amax / 448, 1e-12), q = e4m3_rn_satfinite(clamp(x * (1 /
+    scale), -448, 448)).  fast=True: thor/packing.py:451-519 (prepare_fp8):
+    scale = max(amax * (1/448), 1e-12), q = e4m3(clamp(x / scale)); the
+    division is IEEE round-to-nearest here.  A NaN input clamps to -448 as
+    fminf(448, fmaxf(-448, NaN)) does.  Returns (codes uint8, scale fp32).
+    """
+    x = bf16_bits_to_f32(np.asarray(x_bits, dtype=np.uint16)).astype(F32)
+    a = np.abs(x)
+    a = np.where(np.isfinite(a), a, F32(0))
+    amax = F32(a.max()) if a.size else F32(0)
+    if fast:
+        scale = max(F32(amax * F32(1.0 / 448.0)), F32(1e-12))
+        y = (x / F32(scale)).astype(F32)
+    else:
+        scale = max(F32(amax / F32(448.0)), F32(1e-12))
+        inv = F32(F32(1.0) / F32(scale))
+        y = (x * inv).astype(F32)
+    y = np.where(np.isnan(y), F32(-448.0), y)
+    y = np.clip(y, F32(-448.0), F32(448.0)).astype(F32)
+    code, _ = e4m3_round(np.abs(y))
+    code = np.where(np.signbit(y), code | np.uint8(0x80), code).astype(np.uint8)
+    return code, F32(scale)
+
+
+def e4m3_decode(codes):
+    """E4M3fn codes -> float64 values."""
+    c = np.asarray(codes, dtype=np.uint8)
+    mag = _E4M3[c & 0x7F]
+    return np.where(c & 0x80, -mag, mag)
+
+
+def fp8_gemm(qa, sa, qw, sw, bias_bits=None):
+    """fp64 reference of the E4M3 GEMM: (sum_k a[m,k] w[n,k]) * sa * sw
+    [+ bias], for per-tensor scales sa, sw (the CUTLASS epilogue's
+    scale_a * scale_b, fp8_cutlass_linear.cu:630-643)."""
+    acc = e4m3_decode(qa) @ e4m3_decode(qw).T
+    y = acc * float(sa) * float(sw)
+    if bias_bits is not None:
+        y = y + bf16_bits_to_f32(np.asarray(bias_bits, dtype=np.uint16)).astype(np.float64)
+    return y

@@ -86,6 +86,10 @@ static int device_info(DeviceInfo **out) {
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                d.max_smem);
     if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_i8_kernel<9>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               d.max_smem);
+    if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemm_fp4_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                d.max_smem);
@@ -407,16 +411,18 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
                        int64_t m, int64_t npad, int64_t kpad, void *out, int64_t ldo,
                        int64_t n_store, void *stream, const FusedInput *fin = nullptr,
                        float *max_out = nullptr) {
-  const uint64_t row_bytes = bits == 8 ? uint64_t(kpad) : uint64_t(kpad / 2);
-  const uint32_t box_cols = bits == 8 ? 128u : 64u;
+  // bits: 8 (int8), 4 (packed int4) or 9 (E4M3 bytes).
+  const bool byte_operands = bits != 4;
+  const uint64_t row_bytes = byte_operands ? uint64_t(kpad) : uint64_t(kpad / 2);
+  const uint32_t box_cols = byte_operands ? 128u : 64u;
   CUtensorMap tm_w, tm_a;
   memset(&tm_a, 0, sizeof(tm_a));
   if (int r = make_map(&tm_w, qw, row_bytes, uint64_t(npad), row_bytes,
-                       box_cols, 128u, bits == 8))
+                       box_cols, 128u, byte_operands))
     return r;
   if (fin == nullptr) {
     if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, box_cols,
-                         uint32_t(plan.bn), bits == 8))
+                         uint32_t(plan.bn), byte_operands))
       return r;
   }
   GemmArgs args;
@@ -488,8 +494,9 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e =
-      bits == 8 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, tm_out, args)
-                : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, tm_out, args);
+      bits == 8   ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, tm_out, args)
+      : bits == 9 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<9>, tm_w, tm_a, tm_out, args)
+                  : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, tm_out, args);
   return cuda_status(e, "gemm launch");
 }
 
@@ -990,6 +997,70 @@ int pir2b_gemm_fused(const void *qa, const float *sa, const void *x, int64_t ldx
   return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, out_lut, residual, ldr, nullptr, bits,
                      m, npad, kpad, out, ldo, n_store, stream, x != nullptr ? &fin : nullptr,
                      max_out);
+}
+
+int pir2b_quant_fp8(const void *x, int64_t ldx, int64_t rows, int64_t k, int fast, int weights,
+                    void *q, float *scale, float *scale_rep, int64_t n_rep, void *stream) {
+  if (rows < 1 || k < 8 || k % 8 != 0 || k > (1 << 20) || ldx < k || ldx % 8 != 0 ||
+      rows > (int64_t(1) << 33) / k)
+    return fail(PIR2B_EINVAL, "quant_fp8 needs rows >= 1, k %% 8 == 0 and ldx >= k, ldx %% 8 == 0");
+  if (x == nullptr || q == nullptr || scale == nullptr || (n_rep > 0 && scale_rep == nullptr) ||
+      n_rep < 0)
+    return fail(PIR2B_EINVAL, "quant_fp8 operands must be non-null");
+  if (!aligned(x, 16) || !aligned(q, 8) || !aligned(scale, 4) || (scale_rep && !aligned(scale_rep, 4)))
+    return fail(PIR2B_EALIGN, "quant_fp8: x 16-byte, q 8-byte, scales 4-byte aligned");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  Fp8QuantArgs a;
+  a.x = static_cast<const __nv_bfloat16 *>(x);
+  a.ldx = ldx;
+  a.rows = rows;
+  a.k = int(k);
+  a.q = static_cast<uint8_t *>(q);
+  a.scale = scale;
+  a.scale_rep = n_rep > 0 ? scale_rep : nullptr;
+  a.n_rep = n_rep;
+  a.fast = fast ? 1 : 0;
+  a.weights = weights ? 1 : 0;
+  // About 32 K elements (4 chunks per thread) per CTA, at most a portable
+  // cluster of 8 (and no more CTAs than rows).
+  const int64_t want = (rows * k + 32767) / 32768;
+  const int ranks = int(std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(want, 8), rows)));
+  return cuda_status(run_fp8_quant(a, ranks, static_cast<cudaStream_t>(stream)), "quant_fp8 launch");
+}
+
+int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float *sw,
+                   const void *bias, int bias_mode, const void *residual, int64_t ldr, int64_t m,
+                   int64_t npad, int64_t kpad, void *out, int64_t ldo, int64_t n_store,
+                   void *stream) {
+  if (bias_mode < 0 || bias_mode > 2)
+    return fail(PIR2B_EINVAL, "bias_mode must be 0, 1 or 2");
+  if (m < 1 || m > 0x7fffffffLL || npad < 8 || npad % 8 != 0 || kpad < 128 ||
+      kpad % 128 != 0 || npad > 0x7fffffffLL || kpad > (1LL << 20))
+    return fail(PIR2B_EINVAL, "FP8 GEMM requires m >= 1, npad %% 8 == 0 and kpad %% 128 == 0");
+  if (n_store < 1 || n_store > npad || ldo < n_store)
+    return fail(PIR2B_EINVAL, "n_store must be in [1, npad] and ldo >= n_store");
+  if (qa == nullptr || sa == nullptr || qw == nullptr || sw == nullptr || out == nullptr)
+    return fail(PIR2B_EINVAL, "FP8 GEMM operands must be non-null");
+  if (bias_mode == PIR2B_BIAS_ADD && bias == nullptr)
+    return fail(PIR2B_EINVAL, "bias_mode ADD needs a bias vector");
+  if (!aligned(qa, 16) || !aligned(qw, 16) || !aligned(out, 2) || !aligned(sa, 4) ||
+      !aligned(sw, 4) || (bias && !aligned(bias, 2)) || (residual && !aligned(residual, 2)))
+    return fail(PIR2B_EALIGN, "FP8 GEMM alignment not met");
+  if (residual != nullptr && ldr < n_store)
+    return fail(PIR2B_EINVAL, "residual row stride ldr must be >= n_store");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  // E4M3 operands have the int8 byte layout: the same tile plans.
+  const GemmPlan plan = plan_gemm(8, m, npad, kpad, dev->sms, dev->max_smem);
+  if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
+      plan.smem > size_t(dev->max_smem))
+    return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",
+                (long long)m, (long long)npad, (long long)kpad);
+  return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, nullptr, residual, ldr, nullptr, 9, m,
+                     npad, kpad, out, ldo, n_store, stream);
 }
 
 int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const float *sw,

@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __nv_bfloat16 o[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            o[i] = have_acc ? epilogue_value(int(r[i]), s_sa[cj * 16 + i], sw, b, a.bias_mode_up, lut)
+            o[i] = have_acc ? epilogue_value(acc_value<false>(r[i]), s_sa[cj * 16 + i], sw, b, a.bias_mode_up, lut)
                             : __float2bfloat16_rn(0.f);
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const __nv_bfloat16 o = epilogue_value(acc[i], s_sa[j], sw[i], b[i], a.bias_mode_down, nullptr);
+          const __nv_bfloat16 o = epilogue_value(acc_value<false>(uint32_t(acc[i])), s_sa[j], sw[i], b[i], a.bias_mode_down, nullptr);
           const float r = __bfloat162float(a.residual[int64_t(j) * a.ldr + cc + i]);
           a.out[int64_t(j) * a.ldo + cc + i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o), r));
         }

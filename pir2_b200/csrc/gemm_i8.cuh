@@ -41,11 +41,18 @@ constexpr int kTileN = 128;          // channels per CTA (UMMA_M)
 constexpr int kBlockK = 128;         // K elements per stage
 constexpr int kWeightTileBytes = kTileN * kBlockK;  // 16 KB int8
 
-__device__ __forceinline__ __nv_bfloat16 epilogue_value(int acc, float sa,
+// The accumulator word as fp32: an exact int32 sum (integer kinds) or an
+// fp32 sum (E4M3, kind::f8f6f4).
+template <bool kF8>
+__device__ __forceinline__ float acc_value(uint32_t bits) {
+  return kF8 ? __uint_as_float(bits) : __int2float_rn(int(bits));
+}
+
+__device__ __forceinline__ __nv_bfloat16 epilogue_value(float acc, float sa,
                                                         float sw, float bias,
                                                         int bias_mode,
                                                         const uint16_t *lut) {
-  float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
+  float y = __fmul_rn(__fmul_rn(acc, sa), sw);
   if (bias_mode != 0)
     y = __fadd_rn(y, bias);
   __nv_bfloat16 o = __float2bfloat16_rn(y);
@@ -229,6 +236,9 @@ __device__ __forceinline__ void fused_pack(const GemmArgs &args, uint8_t *xs, ui
 }
 
 // kBits == 8: operands arrive as int8 through TMA in the swizzled layout.
+// kBits == 9: the same for E4M3 bytes, multiplied by kind::f8f6f4 into fp32
+// accumulators (per-tensor scales arrive replicated as the per-row and
+// per-channel scale vectors; split-K partials are fp32, summed in rank order).
 // kBits == 4: operands arrive as packed int4 (64 bytes per row and K block,
 // no swizzle) and the four epilogue warps unpack them per stage.
 //
@@ -251,7 +261,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int stages = args.stages;
   // wt = 2 (int8, no split-K): two 128-channel weight tiles share each token
   // tile, two TMEM accumulators, twice the MMA work per staged byte.
-  const int wt = kBits == 8 ? args.wt : 1;
+  constexpr bool kF8 = kBits == 9;
+  constexpr bool kByte = kBits != 4;   // one byte per operand element, TMA-swizzled
+  const int wt = kByte ? args.wt : 1;
   const int op_a_bytes = wt * kWeightTileBytes;   // unpacked int8 weight tile(s)
   const int op_b_bytes = bn * kBlockK;            // unpacked int8 token tile
   // Fused pack: the token codes of all of this CTA's K blocks sit in their
@@ -323,16 +335,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       // several token tiles other CTAs re-read them from L2.
       const uint64_t wpolicy =
           gridDim.y == 1 ? policy_evict_first() : policy_evict_last();
-      const uint32_t tx = (kBits == 8) ? uint32_t(stage_bytes)
+      const uint32_t tx = kByte ? uint32_t(stage_bytes)
                                        : uint32_t((kTileN + bn) * 64);   // fused: weights only
-      const int kstep = kBits == 8 ? kBlockK : 64;
+      const int kstep = kByte ? kBlockK : 64;
       // Weight tiles of the first ring pass do not depend on the previous
       // kernel: issue them before waiting on it.
       const int pre = min(nkb, stages);
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], tx);
-        uint8_t *dst = kBits == 8 ? smem + i * stage_bytes
-                                  : packed_base + i * packed_stride;
+        uint8_t *dst = kByte ? smem + i * stage_bytes
+                             : packed_base + i * packed_stride;
         tma_load_2d_hint(dst, &tm_w, &full[i], (kb_begin + i) * kstep, n0,
                          wpolicy);
         if (wt == 2)
@@ -342,8 +354,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!fused) {
         pdl_wait();
         for (int i = 0; i < pre; ++i) {
-          uint8_t *dst = kBits == 8 ? smem + i * stage_bytes + op_a_bytes
-                                    : packed_base + i * packed_stride + kTileN * 64;
+          uint8_t *dst = kByte ? smem + i * stage_bytes + op_a_bytes
+                               : packed_base + i * packed_stride + kTileN * 64;
           tma_load_2d(dst, &tm_a, &full[i], (kb_begin + i) * kstep, m0);
         }
       }
@@ -354,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         mbar_arrive_expect_tx(&full[s], tx);
         const int kx = (kb_begin + i) * kstep;
-        if (kBits == 8) {
+        if (kByte) {
           uint8_t *a = smem + s * stage_bytes;
           tma_load_2d_hint(a, &tm_w, &full[s], kx, n0, wpolicy);
           if (wt == 2)
@@ -371,13 +383,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
     if (elect_one_sync()) {
-      const uint32_t idesc = idesc_i8(kTileN, bn);
+      const uint32_t idesc = kF8 ? idesc_f8(kTileN, bn) : idesc_i8(kTileN, bn);
       // Fused pack: every K block's codes are written before the first MMA.
       bool ok = !fused || mbar_wait(cbar, 0, kStatusTimeoutMma);
       for (int i = 0; i < nkb && ok; ++i) {
         const int s = i % stages;
         const uint32_t phase = (i / stages) & 1;
-        ok = (kBits == 8) ? mbar_wait(&full[s], phase, kStatusTimeoutMma)
+        ok = kByte ? mbar_wait(&full[s], phase, kStatusTimeoutMma)
                           : mbar_wait(&ready[s], phase, kStatusTimeoutMma);
         if (!ok)
           break;
@@ -387,12 +399,21 @@ __global__ void __launch_bounds__(kThreads, 2)
             fused ? smem_u32(codes + i * op_b_bytes) : a_addr + op_a_bytes;
 #pragma unroll
         for (int k = 0; k < kBlockK / 32; ++k) {
-          mma_i8(tmem_base, smem_desc_sw128(a_addr + k * 32),
-                 smem_desc_sw128(b_addr + k * 32), idesc,
-                 (i > 0 || k > 0) ? 1u : 0u);
+          if (kF8)
+            mma_f8(tmem_base, smem_desc_sw128(a_addr + k * 32),
+                   smem_desc_sw128(b_addr + k * 32), idesc,
+                   (i > 0 || k > 0) ? 1u : 0u);
+          else
+            mma_i8(tmem_base, smem_desc_sw128(a_addr + k * 32),
+                   smem_desc_sw128(b_addr + k * 32), idesc,
+                   (i > 0 || k > 0) ? 1u : 0u);
           if (wt == 2)
-            mma_i8(tmem_base + acc_cols, smem_desc_sw128(a_addr + kWeightTileBytes + k * 32),
-                   smem_desc_sw128(b_addr + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
+            if (kF8)
+              mma_f8(tmem_base + acc_cols, smem_desc_sw128(a_addr + kWeightTileBytes + k * 32),
+                     smem_desc_sw128(b_addr + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
+            else
+              mma_i8(tmem_base + acc_cols, smem_desc_sw128(a_addr + kWeightTileBytes + k * 32),
+                     smem_desc_sw128(b_addr + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
         }
         mma_commit(&empty[s]);
       }
@@ -458,8 +479,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const __nv_bfloat16 g = epilogue_value(int(rg[i]), s_sa[j0 + i], sw_g, b_g, bias_mode, nullptr);
-            const __nv_bfloat16 u = epilogue_value(int(ru[i]), s_sa[j0 + i], sw_u, b_u, bias_mode, nullptr);
+            const __nv_bfloat16 g = epilogue_value(acc_value<kF8>(rg[i]), s_sa[j0 + i], sw_g, b_g, bias_mode, nullptr);
+            const __nv_bfloat16 u = epilogue_value(acc_value<kF8>(ru[i]), s_sa[j0 + i], sw_u, b_u, bias_mode, nullptr);
             const float sg = __bfloat162float(__ushort_as_bfloat16(__ldg(silu + __bfloat16_as_ushort(g))));
             const __nv_bfloat16 h = __float2bfloat16_rn(__fmul_rn(sg, __bfloat162float(u)));
             if (tma)
@@ -506,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             __nv_bfloat16 o[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              o[i] = epilogue_value(int(r[i]), s_sa[j0 + i], sw, b, bias_mode, lut);
+              o[i] = epilogue_value(acc_value<kF8>(r[i]), s_sa[j0 + i], sw, b, bias_mode, lut);
             if (with_res) {
 #pragma unroll
               for (int i = 0; i < 16; ++i)
@@ -599,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         __nv_bfloat16 o[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          o[i] = epilogue_value(acc[i], s_sa[j], sw[i], b[i], args.bias_mode, lut);
+          o[i] = epilogue_value(acc_value<kF8>(uint32_t(acc[i])), s_sa[j], sw[i], b[i], args.bias_mode, lut);
           if (with_res && in_range[i] && j < valid_m)
             o[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o[i]), res[i]));
         }
@@ -630,14 +651,30 @@ __global__ void __launch_bounds__(kThreads, 2)
             res[i] = __bfloat162float(args.residual[int64_t(m0 + j) * args.ldr + cc + i]);
         }
         acc[0] = acc[1] = acc[2] = acc[3] = 0;
+        if (kF8) {
+          // fp32 partial sums, added in rank order.
+          float f[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int p = 0; p < 8; ++p)
-          if (p < splits) {
-            acc[0] += v[p].x;
-            acc[1] += v[p].y;
-            acc[2] += v[p].z;
-            acc[3] += v[p].w;
-          }
+          for (int p = 0; p < 8; ++p)
+            if (p < splits) {
+              f[0] = __fadd_rn(f[0], __int_as_float(v[p].x));
+              f[1] = __fadd_rn(f[1], __int_as_float(v[p].y));
+              f[2] = __fadd_rn(f[2], __int_as_float(v[p].z));
+              f[3] = __fadd_rn(f[3], __int_as_float(v[p].w));
+            }
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            acc[i] = __float_as_int(f[i]);
+        } else {
+#pragma unroll
+          for (int p = 0; p < 8; ++p)
+            if (p < splits) {
+              acc[0] += v[p].x;
+              acc[1] += v[p].y;
+              acc[2] += v[p].z;
+              acc[3] += v[p].w;
+            }
+        }
       };
       for (int j = first; j < jend; j += tstride) {
         int acc[4];

@@ -190,6 +190,20 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc,
       : "memory");
 }
 
+// E4M3 x E4M3 -> fp32 MMA (kind::f8f6f4, K = 32 per instruction, the same
+// shared-memory operand layout as kind::i8).
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc,
+                                       uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on `bar` when all previously issued tcgen05 ops of this
 // thread have completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -250,6 +264,12 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) |
          ((m >> 4) << 24);
+}
+
+// Instruction descriptor of kind::f8f6f4: fp32 accumulator (D format 1),
+// E4M3 A and B (format 0), both K-major.
+__host__ __device__ constexpr uint32_t idesc_f8(uint32_t m, uint32_t n) {
+  return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
 // 2-D tiled bulk tensor store from this CTA's shared memory (rows and

@@ -648,4 +648,162 @@ cudaError_t run_norm_quant(const NormArgs &a, int out_format, int64_t rows,
   return launch_norm2<16>(a, rows, norm, mod, res, st);
 }
 
+// ------------------------------------------------------------------ FP8
+// Per-tensor E4M3 quantization of bf16 rows, both reference variants:
+//  * default (fp8_cutlass_linear.cu:61-120, quantize_bf16): amax of the
+//    finite |x|; scale = max(amax / 448, 1e-12); q = e4m3_rn_satfinite(
+//    clamp(x * (1 / scale), -448, 448));
+//  * fast (thor/packing.py:451-519, prepare_fp8): scale = max(amax *
+//    (1/448), 1e-12); q = e4m3(clamp(x / scale, -448, 448)), with IEEE
+//    round-to-nearest division here.
+// One launch: a cluster of C CTAs splits the rows, each reduces its |x|
+// maximum, every rank combines the C partial maxima through distributed
+// shared memory, then casts its rows.  The scale is written to `scale` and
+// replicated into `scale_rep` (the per-row / per-channel scale vector the
+// E4M3 GEMM epilogue reads).
+struct Fp8QuantArgs {
+  const __nv_bfloat16 *x;
+  int64_t ldx;
+  int64_t rows;
+  int k;                 // k % 8 == 0
+  uint8_t *q;            // [rows, k]
+  float *scale;          // [1]
+  float *scale_rep;      // [n_rep] or null
+  int64_t n_rep;
+  int fast;
+  // 1: the codes are GEMM weights.  The GEMM reads its weights before its
+  // programmatic-dependent wait, so the kernel then lets dependent launches
+  // start only at its end (no early trigger).
+  int weights;
+};
+
+constexpr float kFp8Max = 448.0f;
+constexpr float kFp8MinScale = 1.0e-12f;
+
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+constexpr int kFp8Threads = 1024;
+constexpr int kFp8Cached = 4;   // 16-byte chunks per thread kept in registers between the passes
+
+__global__ void __launch_bounds__(kFp8Threads) fp8_quant_kernel(const Fp8QuantArgs a) {
+  __shared__ float red[32];
+  __shared__ float s_part;
+  __shared__ float s_scale[2];
+  pdl_wait();
+  if (!a.weights)
+    pdl_launch_dependents();
+  uint32_t nranks;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(nranks));
+  const uint32_t rank = cluster_ctarank();
+  const int64_t r0 = a.rows * rank / nranks, r1 = a.rows * (rank + 1) / nranks;
+  const int nch = a.k / 8;
+  const int items = int((r1 - r0) * nch);   // 16-byte chunks of this CTA (< 2^31)
+  const bool flat = a.ldx == a.k;           // rows back to back: chunk i at r0*k + 8i
+  auto chunk_ptr = [&](int i) -> int64_t {  // element offset of chunk i in x
+    if (flat)
+      return r0 * a.k + int64_t(i) * 8;
+    const int row = i / nch;
+    return (r0 + row) * a.ldx + int64_t(i - row * nch) * 8;
+  };
+  auto out_ptr = [&](int i) -> int64_t {
+    if (flat)
+      return r0 * a.k + int64_t(i) * 8;
+    const int row = i / nch;
+    return (r0 + row) * int64_t(a.k) + int64_t(i - row * nch) * 8;
+  };
+  uint4 cache[kFp8Cached];
+  float m = 0.f;
+  auto absmax8 = [&](const uint4 &raw) {
+    const __nv_bfloat16 *v = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = fabsf(__bfloat162float(v[e]));
+      if (isfinite(f))
+        m = fmaxf(m, f);
+    }
+  };
+  // Pass 1: maximum of the finite |x|.  The first kFp8Cached chunks of each
+  // thread are loaded together and kept in registers for pass 2.
+#pragma unroll
+  for (int j = 0; j < kFp8Cached; ++j) {
+    const int i = int(threadIdx.x) + j * kFp8Threads;
+    cache[j] = i < items ? __ldg(reinterpret_cast<const uint4 *>(a.x + chunk_ptr(i)))
+                         : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < kFp8Cached; ++j)
+    absmax8(cache[j]);
+#pragma unroll 4
+  for (int i = int(threadIdx.x) + kFp8Cached * kFp8Threads; i < items; i += kFp8Threads)
+    absmax8(__ldg(reinterpret_cast<const uint4 *>(a.x + chunk_ptr(i))));
+  m = block_max(m, red);
+  if (threadIdx.x == 0)
+    s_part = m;
+  cluster_sync();
+  if (threadIdx.x == 0) {
+    float amax = 0.f;
+    for (uint32_t p = 0; p < nranks; ++p)
+      amax = fmaxf(amax, __int_as_float(ld_cluster_s32(map_peer(smem_u32(&s_part), p))));
+    const float scale = a.fast ? fmaxf(__fmul_rn(amax, 1.0f / kFp8Max), kFp8MinScale)
+                               : fmaxf(__fdiv_rn(amax, kFp8Max), kFp8MinScale);
+    s_scale[0] = scale;
+    s_scale[1] = __fdiv_rn(1.0f, scale);
+  }
+  // Every rank has read every partial maximum (no CTA leaves while a peer
+  // still reads it), and s_scale is visible to the whole CTA.
+  cluster_sync();
+  const float scale = s_scale[0], inv = s_scale[1];
+  // Pass 2: cast (chunks beyond the register cache are read again).
+  auto cast8 = [&](int i, const uint4 &raw) {
+    const __nv_bfloat16 *v = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float x = __bfloat162float(v[e]);
+      const float y = a.fast ? __fdiv_rn(x, scale) : __fmul_rn(x, inv);
+      f[e] = fminf(kFp8Max, fmaxf(-kFp8Max, y));
+    }
+    uint2 out;
+    out.x = cvt_e4m3x2(f[0], f[1]) | (cvt_e4m3x2(f[2], f[3]) << 16);
+    out.y = cvt_e4m3x2(f[4], f[5]) | (cvt_e4m3x2(f[6], f[7]) << 16);
+    *reinterpret_cast<uint2 *>(a.q + out_ptr(i)) = out;
+  };
+#pragma unroll
+  for (int j = 0; j < kFp8Cached; ++j) {
+    const int i = int(threadIdx.x) + j * kFp8Threads;
+    if (i < items)
+      cast8(i, cache[j]);
+  }
+#pragma unroll 4
+  for (int i = int(threadIdx.x) + kFp8Cached * kFp8Threads; i < items; i += kFp8Threads)
+    cast8(i, __ldg(reinterpret_cast<const uint4 *>(a.x + chunk_ptr(i))));
+  if (rank == 0 && threadIdx.x == 0)
+    *a.scale = scale;
+  if (a.scale_rep != nullptr)
+    for (int64_t i = int64_t(rank) * kFp8Threads + threadIdx.x; i < a.n_rep;
+         i += int64_t(nranks) * kFp8Threads)
+      a.scale_rep[i] = scale;
+}
+
+cudaError_t run_fp8_quant(const Fp8QuantArgs &a, int ranks, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(ranks), 1, 1);
+  cfg.blockDim = dim3(kFp8Threads, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = unsigned(ranks);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, fp8_quant_kernel, a);
+}
+
 } // namespace pir2b

@@ -1,6 +1,6 @@
-"""NVFP4 Linear layers and producers on the B200 kernels.
+"""NVFP4 and FP8 (E4M3) Linear layers and NVFP4 producers on the B200 kernels.
 
-Mirrors the FP4 half of coexecution/optimization/backends/thor/linear.py
+Mirrors coexecution/optimization/backends/thor/linear.py
 (`FloatingLinear`, :30-190) and packing.py (`FloatingPacked`, the fused
 norm/smoothing producers, :15-448): weights are packed once as E2M1 with
 UE4M3 factors per 16 elements (the CUTLASS 128x4 swizzled factor layout,
@@ -8,9 +8,13 @@ UE4M3 factors per 16 elements (the CUTLASS 128x4 swizzled factor layout,
 LayerNorm / RMSNorm / AdaLN / residual / SmoothQuant division), and the GEMM
 runs on tcgen05 kind::mxf4nvf4 with fp32 accumulation and bf16 output.
 
-This build supports precision "fp4"; FP8 is not part of it.  A K block of
-the B200 kernel is 256 values, so in_features must be a multiple of 256
-(piR2 requires 32); out_features must be a multiple of 32 as in piR2.
+FP8 layers (precision "fp8") quantize weights and activations per tensor
+to E4M3 (`ops.quant_fp8`: the quantize_bf16 arithmetic, or prepare_fp8's
+with `fast_fp8`) and run the tcgen05 kind::f8f6f4 GEMM with fp32
+accumulation; FP8 in_features must be a multiple of 128 (piR2: 16).  An
+NVFP4 K block of the B200 kernel is 256 values, so fp4 in_features must be
+a multiple of 256 (piR2 requires 32); out_features must be a multiple of 32
+(fp4) or 16 (fp8) as in piR2.  The fused producers are fp4 only.
 """
 
 import math
@@ -109,23 +113,35 @@ def prepare_norm(x, precision, *, eps, scale=None, shift=None, residual=None, sm
     return packed, (None if summed is None else summed.reshape(x.shape))
 
 
+def aligned_for(precision, in_features, out_features):
+    """Whether a Linear meets the B200 kernels' alignment for `precision`."""
+    if precision == "fp8":
+        return in_features % 128 == 0 and out_features % 16 == 0
+    return in_features % 256 == 0 and out_features % 32 == 0
+
+
 class FloatingLinear(torch.nn.Module):
-    """Block-scaled E2M1 GEMM with packed weights (thor/linear.py:30-190)."""
+    """E4M3 or block-scaled E2M1 GEMM with packed weights (thor/linear.py:30-190)."""
 
     def __init__(self, linear, name, precision="fp4", *, fast_fp8=False, fp4_swap_ab=False, smoothing_scale=None):
         super().__init__()
-        _require_fp4(precision)
-        if fast_fp8:
+        if precision not in ("fp8", "fp4"):
+            raise ValueError("Floating precision must be fp8 or fp4")
+        if fast_fp8 and precision != "fp8":
             raise ValueError("Fast FP8 quantization requires precision=fp8")
+        if fp4_swap_ab and precision != "fp4":
+            raise ValueError("FP4 Swap-AB requires precision=fp4")
         if (
             not linear.weight.is_cuda
             or linear.weight.dtype != torch.bfloat16
-            or linear.in_features % 256
-            or linear.out_features % 32
+            or not aligned_for(precision, linear.in_features, linear.out_features)
         ):
-            raise ValueError("fp4 requires CUDA BF16 weights, in_features % 256 == 0 and out_features % 32 == 0")
+            raise ValueError(f"{precision} requires aligned CUDA BF16 Linear weights")
         if torch.cuda.get_device_capability(linear.weight.device) != (10, 0):
-            raise ValueError("The B200 FP4 adapter runs on sm_100 devices")
+            raise ValueError("The B200 floating adapter runs on sm_100 devices")
+        if precision == "fp8" and smoothing_scale is not None:
+            raise ValueError("SmoothQuant with fp8 is not implemented in this build")
+        self.fast_fp8 = fast_fp8
         self.name = name
         self.precision = precision
         self.fp4_swap_ab = fp4_swap_ab   # the tcgen05 kernel has no separate swap-AB variant
@@ -140,7 +156,15 @@ class FloatingLinear(torch.nn.Module):
             if not torch.isfinite(weight_input).all():
                 raise ValueError("SmoothQuant overflowed BF16 weights")
         self.register_buffer("smoothing_scale", smoothing_scale)
-        packed, scale = ops.pack_nvfp4(weight_input)
+        if precision == "fp8":
+            # Per-tensor E4M3 weights (pack_linear_weight, fp8_cutlass_linear.cu:
+            # 1011-1024); the scale is kept as piR2's scalar and replicated
+            # per output channel for the GEMM epilogue.
+            packed, scale, columns = ops.quant_fp8(weight_input, replicate=self.out_features, weights=True)
+            scale = scale.reshape(())
+            self.register_buffer("weight_scale_columns", columns)
+        else:
+            packed, scale = ops.pack_nvfp4(weight_input)
         self.register_buffer("packed_weight", packed)
         self.register_buffer("weight_scale", scale)
         self.register_buffer(
@@ -168,13 +192,24 @@ class FloatingLinear(torch.nn.Module):
         ):
             raise ValueError("Floating quantization requires nonempty CUDA BF16 inference activations")
         matrix = value.reshape(-1, self.in_features).contiguous()
+        if self.precision == "fp8":
+            # Activation scale replicated per row for the GEMM epilogue.
+            q, _, rows = ops.quant_fp8(matrix, fast=self.fast_fp8)
+            return q, rows
         if self.smoothing_scale is not None:
             packed = prepare_smoothed(matrix, self.precision, self.smoothing_scale)
             return packed.data, packed.scale
         return ops.pack_nvfp4(matrix)
 
     def forward_packed(self, packed, scale, leading_shape):
-        result = ops.gemm_nvfp4(packed, scale, self.packed_weight, self.weight_scale, self.bias, n=self.out_features)
+        if self.precision == "fp8":
+            result = ops.gemm_fp8(
+                packed, scale, self.packed_weight, self.weight_scale_columns, self.bias, n=self.out_features
+            )
+        else:
+            result = ops.gemm_nvfp4(
+                packed, scale, self.packed_weight, self.weight_scale, self.bias, n=self.out_features
+            )
         return result.reshape(*leading_shape, self.out_features)
 
     def forward(self, value):
@@ -188,17 +223,20 @@ class FloatingProjections:
     meet the FP4 alignment (others stay bf16, as piR2's alignment checks
     exclude them)."""
 
-    def __init__(self, model, executed, *, smoothing=None):
+    def __init__(self, model, executed, *, smoothing=None, precision="fp4", fast_fp8=False):
         self.sites = {}
         self.skipped = []
         modules = dict(model.named_modules())
         for name in executed:
             module = modules[name]
-            if module.in_features % 256 or module.out_features % 32:
+            if not aligned_for(precision, module.in_features, module.out_features):
                 self.skipped.append(name)
                 continue
             scale = None if smoothing is None else smoothing.get(name)
-            self.sites[name] = (module, FloatingLinear(module, name, "fp4", smoothing_scale=scale))
+            self.sites[name] = (
+                module,
+                FloatingLinear(module, name, precision, fast_fp8=fast_fp8, smoothing_scale=scale),
+            )
         self.saved = []
 
     def set(self):

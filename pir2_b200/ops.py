@@ -405,6 +405,61 @@ def attention_causal(q, k, v, *, scale=None, out=None):
     return out
 
 
+def quant_fp8(x, *, fast=False, replicate=None, weights=False):
+    """Per-tensor E4M3 quantization of bf16 rows x [rows, k] (k % 8 == 0).
+
+    Returns (codes uint8 [rows, k], scale fp32 [1], replicated fp32
+    [replicate]) -- the replicated vector (default: one per row) is the
+    per-row or per-channel scale the FP8 GEMM reads.  fast=True selects
+    piR2's prepare_fp8 arithmetic instead of quantize_bf16's.  weights=True
+    when the codes are GEMM weights (the GEMMs read weights before their
+    programmatic-dependent wait; this launch then does not let the next
+    kernel start early).
+    """
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("quant_fp8 needs CUDA bf16 [rows, k] rows with unit column stride")
+    rows, k = x.shape
+    n_rep = rows if replicate is None else int(replicate)
+    q = torch.empty((rows, k), device=x.device, dtype=torch.uint8)
+    scale = torch.empty(1, device=x.device, dtype=torch.float32)
+    rep = torch.empty(max(n_rep, 1), device=x.device, dtype=torch.float32)
+    ldx = x.stride(0) if rows > 1 else k
+    status = _lib.lib().pir2b_quant_fp8(
+        x.data_ptr(), ldx, rows, k, 1 if fast else 0, 1 if weights else 0, q.data_ptr(), scale.data_ptr(),
+        rep.data_ptr() if n_rep > 0 else None, n_rep, _stream(x.device),
+    )
+    _lib.check(status, "pir2b_quant_fp8")
+    return q, scale, rep[:n_rep]
+
+
+def gemm_fp8(qa, sa_rows, qw, sw_cols, bias=None, *, n, residual=None, out=None):
+    """E4M3 GEMM (tcgen05 kind::f8f6f4, fp32 accumulate) -> bf16 [m, n]:
+    bf16(f32(acc * sa[m]) * sw[c] + bias[c]) with the replicated per-tensor
+    scale vectors of `quant_fp8`."""
+    m, kpad = qa.shape
+    npad = qw.shape[0]
+    if qw.shape[1] != kpad or qa.dtype != torch.uint8 or qw.dtype != torch.uint8:
+        raise ValueError("FP8 operands must be uint8 E4M3 codes with matching K")
+    if out is None:
+        out = torch.empty((m, n), device=qa.device, dtype=torch.bfloat16)
+    ldr = 0
+    if residual is not None:
+        residual = residual.reshape(m, -1)
+        ldr = residual.stride(0) if m > 1 else residual.shape[1]
+    bias_mode = _lib.BIAS_ADD if bias is not None else _lib.BIAS_NONE
+    recorder = launch_recorder
+    if recorder is not None:
+        recorder.before(qa.device)
+    status = _lib.lib().pir2b_gemm_fp8(
+        qa.data_ptr(), sa_rows.data_ptr(), qw.data_ptr(), sw_cols.data_ptr(), _ptr(bias), bias_mode,
+        _ptr(residual), ldr, m, npad, kpad, out.data_ptr(), out.stride(0), n, _stream(qa.device),
+    )
+    _lib.check(status, "pir2b_gemm_fp8")
+    if recorder is not None:
+        recorder.after(qa.device, bits="fp8", m=m, n=n, k=kpad, npad=npad)
+    return out
+
+
 def gemm_nvfp4(a_packed, a_sf, w_packed, w_sf, bias=None, *, n, alpha=1.0, out=None):
     """NVFP4 GEMM: bf16(alpha * sum (a * sfa)(w * sfw) [+ bias]) -> [m, n].
 

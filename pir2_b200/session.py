@@ -86,8 +86,6 @@ class GrootOptimizations:
         enabled = [flag for flag in OUT_OF_SCOPE_FLAGS if getattr(self.config, flag)]
         if enabled:
             raise ValueError(f"Not part of the B200 quantized-Linear build: {', '.join(enabled)}")
-        if self.config.precision == "fp8":
-            raise ValueError("FP8 is not part of the B200 quantized-Linear build")
         self._configuration_file_hashes = {
             key: hashlib.sha256(Path(path).read_bytes()).hexdigest()
             for key in CONFIG_FILES
@@ -117,12 +115,13 @@ class GrootOptimizations:
             "available": len(sites),
             "categories": sorted(categories),
         }
-        if self.config.precision == "fp4":
+        if self.config.precision in ("fp4", "fp8"):
             from .floating import FloatingProjections
 
+            precision = self.config.precision
             # piR2's floating fusions (grouped / shared-input projections,
             # SwiGLU, GELU and RMSNorm packing, AdaLN connections) are not in
-            # this build's fp4 path: refuse them instead of ignoring them.
+            # this build's floating paths: refuse them instead of ignoring them.
             unsupported = [
                 flag
                 for flag in ("fp_shared_inputs", "fp_grouped", "fp_swiglu", "fp_gelu", "fp_rmsnorm")
@@ -130,8 +129,10 @@ class GrootOptimizations:
             ]
             if self.config.fusion or self.config.norm_modulation_quant:
                 unsupported.append("fusion")
+            if precision == "fp8" and self.config.fp_smoothquant is not None:
+                unsupported.append("fp_smoothquant")
             if unsupported:
-                raise ValueError(f"Not implemented for fp4 in this build: {', '.join(unsupported)}")
+                raise ValueError(f"Not implemented for {precision} in this build: {', '.join(unsupported)}")
 
             smoothing = None
             if self.config.fp_smoothquant is not None:
@@ -147,7 +148,9 @@ class GrootOptimizations:
                 smoothing, self.coverage["smoothquant"] = load_profile(
                     self.config.fp_smoothquant, selected, groups, self.config.precision
                 )
-            self.floating = FloatingProjections(model, executed, smoothing=smoothing)
+            self.floating = FloatingProjections(
+                model, executed, smoothing=smoothing, precision=precision, fast_fp8=self.config.fp8_fast_quant
+            )
             self.stack.callback(self.floating.close)
             self.floating.set()
             return

@@ -39,7 +39,7 @@ VLM = harness.VLMConfig(layers=2, vocab=2048)
 DIT = harness.DiTConfig(layers=2)
 
 # Relative-L2 bounds on the actions: (fused vs oracle policy, vs bf16).
-TOLERANCE = {"w8a8": (0.05, 0.10), "w4a4": (0.50, 0.80), "fp4": (0.10, 0.60)}
+TOLERANCE = {"w8a8": (0.05, 0.10), "w4a4": (0.50, 0.80), "fp4": (0.10, 0.60), "fp8": (0.05, 0.30)}
 
 
 def _rel_l2(a, b):
@@ -48,8 +48,8 @@ def _rel_l2(a, b):
 
 
 def _fused(precision):
-    if precision == "fp4":
-        return OptimizationConfig(precision="fp4", scope="all")
+    if precision in ("fp4", "fp8"):
+        return OptimizationConfig(precision=precision, scope="all")
     return OptimizationConfig(
         precision=precision, fusion=True, scope="all", group_conditioning=True,
         norm_modulation_quant=True, residual_norm_quant=True,
@@ -76,7 +76,7 @@ def test_unfused_actions_equal_oracle_policy_bitwise(policies, precision):
     assert torch.equal(actions, oracle_policy(*inputs))
 
 
-@pytest.mark.parametrize("precision", ["w8a8", "w4a4", "fp4"])
+@pytest.mark.parametrize("precision", ["w8a8", "w4a4", "fp4", "fp8"])
 @torch.inference_mode()
 def test_fused_actions_match_oracle_policy(policies, precision):
     policy, inputs, bf16_actions = policies

@@ -1,0 +1,77 @@
+"""FP8 (E4M3, per-tensor) path on the B200 kernels: the quantizer's codes
+and scale are bitwise the oracle's (both reference variants), the tcgen05
+kind::f8f6f4 GEMM matches the oracle's fp64 sum of dequantized products to
+one bf16 rounding step (rtol 2^-7) plus atol 1e-3 for fp32 accumulation
+order, and FloatingLinear(precision="fp8") equals quantizer + GEMM."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from pir2_b200 import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def bits_of(t):
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("rows,k", [(1, 128), (17, 1536), (544, 2048), (3000, 256), (7, 1032)])
+@pytest.mark.parametrize("fast", [False, True])
+def test_quant_fp8_codes_and_scale_equal_oracle(rows, k, fast):
+    g = torch.Generator().manual_seed(rows + k)
+    x = torch.randn(rows, k, generator=g) * 2.0
+    x[0, :6] = torch.tensor([0.0, -0.0, float("inf"), -float("inf"), float("nan"), 1e-30])
+    xb = x.to(torch.bfloat16)
+    q, scale, rep = ops.quant_fp8(xb.cuda(), fast=fast)
+    want_q, want_s = oracle.quant_fp8(bits_of(xb), fast=fast)
+    assert np.float32(scale.item()) == want_s
+    assert torch.equal(rep, torch.full_like(rep, float(want_s)))
+    assert np.array_equal(q.cpu().numpy(), want_q)
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize(
+    "m,k,n",
+    [(1, 2048, 4096), (17, 1536, 1536), (64, 1024, 2048), (300, 1536, 640), (544, 2048, 4096)],
+)
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_gemm_fp8_matches_dequantized_product(m, k, n, with_bias):
+    g = torch.Generator().manual_seed(m * 3 + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16) if with_bias else None
+    qa, sa, sa_rows = ops.quant_fp8(x.cuda())
+    qw, sw, sw_cols = ops.quant_fp8(w.cuda(), replicate=n, weights=True)
+    out = ops.gemm_fp8(qa, sa_rows, qw, sw_cols, None if bias is None else bias.cuda(), n=n)
+    torch.cuda.synchronize()
+    want = oracle.fp8_gemm(qa.cpu().numpy(), sa.item(), qw.cpu().numpy(), sw.item(),
+                           None if bias is None else bits_of(bias))
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=2 ** -7, atol=1e-3)
+    assert _lib.device_status() == 0
+
+
+def test_gemm_fp8_residual_and_floating_linear():
+    from pir2_b200.floating import FloatingLinear
+
+    g = torch.Generator().manual_seed(3)
+    with torch.device("cuda"):
+        linear = torch.nn.Linear(1536, 4608, bias=True).to(torch.bfloat16)
+    x = torch.randn(2, 17, 1536, generator=g).to(torch.bfloat16).cuda()
+    layer = FloatingLinear(linear, "probe", "fp8")
+    qa, _, rows = ops.quant_fp8(x.reshape(-1, 1536))
+    direct = ops.gemm_fp8(qa, rows, layer.packed_weight, layer.weight_scale_columns, layer.bias, n=4608)
+    assert torch.equal(layer(x).reshape(-1, 4608), direct)
+    res = torch.randn(34, 4608, generator=g).to(torch.bfloat16).cuda()
+    with_res = ops.gemm_fp8(qa, rows, layer.packed_weight, layer.weight_scale_columns, layer.bias, n=4608,
+                            residual=res)
+    want = (direct.float() + res.float()).to(torch.bfloat16)
+    assert torch.equal(with_res, want)
+    fast = FloatingLinear(linear, "probe", "fp8", fast_fp8=True)
+    q2, _, rows2 = ops.quant_fp8(x.reshape(-1, 1536), fast=True)
+    assert torch.equal(fast(x).reshape(-1, 4608),
+                       ops.gemm_fp8(q2, rows2, fast.packed_weight, fast.weight_scale_columns, fast.bias, n=4608))
+    assert _lib.device_status() == 0
