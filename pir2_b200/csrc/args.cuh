@@ -85,7 +85,7 @@ cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
 cudaError_t run_norm_quant(const NormArgs &a, int out_format, int64_t rows,
                            int norm, bool mod, bool res, cudaStream_t st);
 
-template <int kBits>
+template <int kBits, bool kWide = false>
 __global__ void gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w,
                                const __grid_constant__ CUtensorMap tm_a,
                                const __grid_constant__ CUtensorMap tm_out,

@@ -78,17 +78,17 @@ static int device_info(DeviceInfo **out) {
                            cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   }
   if (!d.attrs_set) {
-    e = cudaFuncSetAttribute(gemm_i8_kernel<8>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             d.max_smem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_i8_kernel<4>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               d.max_smem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_i8_kernel<9>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               d.max_smem);
+    const void *gemms[] = {
+        reinterpret_cast<const void *>(gemm_i8_kernel<8, false>),
+        reinterpret_cast<const void *>(gemm_i8_kernel<8, true>),
+        reinterpret_cast<const void *>(gemm_i8_kernel<4, false>),
+        reinterpret_cast<const void *>(gemm_i8_kernel<4, true>),
+        reinterpret_cast<const void *>(gemm_i8_kernel<9, false>),
+        reinterpret_cast<const void *>(gemm_i8_kernel<9, true>)};
+    e = cudaSuccess;
+    for (const void *f : gemms)
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemm_fp4_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -493,10 +493,15 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  // Token tiles above 64 rows take the wide instantiation.
+  const bool wide = plan.bn > 64;
   cudaError_t e =
-      bits == 8   ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8>, tm_w, tm_a, tm_out, args)
-      : bits == 9 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<9>, tm_w, tm_a, tm_out, args)
-                  : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4>, tm_w, tm_a, tm_out, args);
+      !wide ? (bits == 8   ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8, false>, tm_w, tm_a, tm_out, args)
+               : bits == 9 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<9, false>, tm_w, tm_a, tm_out, args)
+                           : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4, false>, tm_w, tm_a, tm_out, args))
+            : (bits == 8   ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<8, true>, tm_w, tm_a, tm_out, args)
+               : bits == 9 ? cudaLaunchKernelEx(&cfg, gemm_i8_kernel<9, true>, tm_w, tm_a, tm_out, args)
+                           : cudaLaunchKernelEx(&cfg, gemm_i8_kernel<4, true>, tm_w, tm_a, tm_out, args));
   return cuda_status(e, "gemm launch");
 }
 

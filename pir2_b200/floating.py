@@ -218,14 +218,54 @@ class FloatingLinear(torch.nn.Module):
         return self.forward_packed(packed, scale, shape)
 
 
+class FloatingInputGroup:
+    """One activation pack per owner call for sibling projections of the
+    same input (q|k|v, k|v, gate|up): thor/linear.py:193-229.  GEMMs, weight
+    scales and layers stay independent; the cache lives only inside one
+    owner invocation and is keyed on the identical input tensor; a direct
+    projection call outside an owner call never reuses it.  Serial
+    inference only, like the reference."""
+
+    def __init__(self, linears):
+        if any(q.smoothing_scale is not linears[0].smoothing_scale for q in linears):
+            raise ValueError("Shared packing requires identical SmoothQuant scales")
+        self.linears = linears
+        self.active = False
+        self.cache = None
+
+    def run(self, forward, *args, **kwargs):
+        previous = self.active, self.cache
+        self.active, self.cache = True, None
+        try:
+            return forward(*args, **kwargs)
+        finally:
+            self.active, self.cache = previous
+
+    def project(self, value, index):
+        linear = self.linears[index]
+        if not self.active:
+            return linear(value)
+        if self.cache is None or self.cache[0] is not value or index in self.cache[3]:
+            packed, scale = linear.pack_input(value)
+            self.cache = (value, packed, scale, set())
+        _, packed, scale, used = self.cache
+        result = linear.forward_packed(packed, scale, value.shape[:-1])
+        used.add(index)
+        if len(used) == len(self.linears):
+            self.cache = None
+        return result
+
+
 class FloatingProjections:
     """Reversible installation of FloatingLinear on the executed sites that
     meet the FP4 alignment (others stay bf16, as piR2's alignment checks
     exclude them)."""
 
-    def __init__(self, model, executed, *, smoothing=None, precision="fp4", fast_fp8=False):
+    def __init__(self, model, executed, *, smoothing=None, precision="fp4", fast_fp8=False, shared_inputs=False,
+                 groups=()):
         self.sites = {}
         self.skipped = []
+        self.groups = []
         modules = dict(model.named_modules())
         for name in executed:
             module = modules[name]
@@ -237,6 +277,16 @@ class FloatingProjections:
                 module,
                 FloatingLinear(module, name, precision, fast_fp8=fast_fp8, smoothing_scale=scale),
             )
+        if shared_inputs:
+            # Sibling projections of one owner module (the same input tensor).
+            for names in groups:
+                if not all(n in self.sites for n in names):
+                    continue
+                owner = names[0].rpartition(".")[0]
+                if any(n.rpartition(".")[0] != owner for n in names):
+                    continue
+                group = FloatingInputGroup([self.sites[n][1] for n in names])
+                self.groups.append((modules[owner], [self.sites[n][0] for n in names], group))
         self.saved = []
 
     def set(self):
@@ -244,6 +294,12 @@ class FloatingProjections:
         for module, linear in self.sites.values():
             self.saved.append((module, "forward" in module.__dict__, module.__dict__.get("forward")))
             module.forward = linear.forward
+        for owner, members, group in self.groups:
+            self.saved.append((owner, "forward" in owner.__dict__, owner.__dict__.get("forward")))
+            original = owner.forward
+            owner.forward = lambda *args, g=group, f=original, **kw: g.run(f, *args, **kw)
+            for index, member in enumerate(members):
+                member.forward = lambda x, g=group, i=index: g.project(x, i)
 
     def close(self):
         for module, had, forward in self.saved:

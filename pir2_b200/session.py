@@ -124,7 +124,7 @@ class GrootOptimizations:
             # this build's floating paths: refuse them instead of ignoring them.
             unsupported = [
                 flag
-                for flag in ("fp_shared_inputs", "fp_grouped", "fp_swiglu", "fp_gelu", "fp_rmsnorm")
+                for flag in ("fp_grouped", "fp_swiglu", "fp_gelu", "fp_rmsnorm")
                 if getattr(self.config, flag)
             ]
             if self.config.fusion or self.config.norm_modulation_quant:
@@ -149,8 +149,15 @@ class GrootOptimizations:
                     self.config.fp_smoothquant, selected, groups, self.config.precision
                 )
             self.floating = FloatingProjections(
-                model, executed, smoothing=smoothing, precision=precision, fast_fp8=self.config.fp8_fast_quant
+                model,
+                executed,
+                smoothing=smoothing,
+                precision=precision,
+                fast_fp8=self.config.fp8_fast_quant,
+                shared_inputs=self.config.fp_shared_inputs,
+                groups=inventory(model, expanded=expanded)[1],
             )
+            self.coverage["shared_input_groups"] = len(self.floating.groups)
             self.stack.callback(self.floating.close)
             self.floating.set()
             return

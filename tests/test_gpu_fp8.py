@@ -75,3 +75,33 @@ def test_gemm_fp8_residual_and_floating_linear():
     assert torch.equal(fast(x).reshape(-1, 4608),
                        ops.gemm_fp8(q2, rows2, fast.packed_weight, fast.weight_scale_columns, fast.bias, n=4608))
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("precision", ["fp8", "fp4"])
+@torch.inference_mode()
+def test_shared_input_packing_is_bitwise_and_packs_once(precision, monkeypatch):
+    """fp_shared_inputs: sibling projections of one input (q|k|v, k|v,
+    gate|up) pack it once per owner call; actions are bitwise unchanged."""
+    from types import SimpleNamespace
+
+    from pir2_b200 import harness
+    from pir2_b200.config import OptimizationConfig
+    from pir2_b200.session import GrootOptimizations
+
+    vlm, dit = harness.VLMConfig(layers=1, vocab=2048), harness.DiTConfig(layers=2)
+    policy = harness.build_policy("cuda", vlm=vlm, dit=dit)
+    inputs = harness.synthetic_inputs(1, "cuda", vlm=vlm, dit=dit)
+    pack = "quant_fp8" if precision == "fp8" else "pack_nvfp4"
+    original = getattr(ops, pack)
+    calls = []
+    monkeypatch.setattr(ops, pack, lambda *a, **k: calls.append(1) or original(*a, **k))
+    results = []
+    for shared in (False, True):
+        config = OptimizationConfig(precision=precision, scope="all", fp_shared_inputs=shared)
+        with GrootOptimizations(SimpleNamespace(model=policy), config) as session:
+            calls.clear()   # weight packs happen at install
+            actions = policy(*inputs)
+            results.append((actions, len(calls), session.coverage["shared_input_groups"]))
+    assert torch.equal(results[0][0], results[1][0])
+    assert results[1][2] > 0 and results[1][1] < results[0][1]
+    assert _lib.device_status() == 0
