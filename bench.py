@@ -368,7 +368,7 @@ def build_engine(args, local):
     device = torch.device("cuda", local)
     policy = harness.build_policy(device)
     if args.precision in ("fp4", "fp8"):
-        config = OptimizationConfig(precision=args.precision, scope="all")
+        config = OptimizationConfig(precision=args.precision, scope="all", fp_shared_inputs=True)
     else:
         config = OptimizationConfig(
             precision=args.precision,
