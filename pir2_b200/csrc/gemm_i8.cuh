@@ -696,17 +696,24 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (jj < jend)
               v[q] = ld_cluster_v4(peer_base[q % S] + uint32_t(jj * kTileN * 4));
           }
+          // Every residual value of the round is requested before the
+          // first one is used.
+          float res_all[per][4];
+#pragma unroll
+          for (int u = 0; u < per; ++u) {
+            const int jj = j + u * tstride;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              res_all[u][i] = 0.f;
+              if (with_res && in_range[i] && jj < valid_m)
+                res_all[u][i] = __bfloat162float(args.residual[int64_t(m0 + jj) * args.ldr + cc + i]);
+            }
+          }
 #pragma unroll
           for (int u = 0; u < per; ++u) {
             const int jj = j + u * tstride;
             if (jj < jend) {
-              float res[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                res[i] = 0.f;
-                if (with_res && in_range[i] && jj < valid_m)
-                  res[i] = __bfloat162float(args.residual[int64_t(m0 + jj) * args.ldr + cc + i]);
-              }
+              const float (&res)[4] = res_all[u];
               int acc[4] = {0, 0, 0, 0};
               if (kF8) {
                 float f[4] = {0.f, 0.f, 0.f, 0.f};
