@@ -295,11 +295,21 @@ def cpu_oracle_step(args, budget_s):
     bounded sample: one VLM decoder layer (544 tokens) and a two-block DiT
     (one cross-, one self-attention block) through the 4 Euler steps, scaled
     to 16 layers / 16 blocks.  Returns (ms_per_step, cores, sample text)."""
+    from threadpoolctl import threadpool_limits
+
     from oracle.model import install_oracle_linears
     from pir2_b200 import harness
 
-    cores = os.cpu_count() or 1
+    # Every host thread this process may run on, for torch and for numpy's
+    # BLAS (torchrun starts ranks with OMP_NUM_THREADS=1, which would leave
+    # the oracle's products on one thread).
+    cores = len(os.sched_getaffinity(0)) or 1
     torch.set_num_threads(cores)
+    with threadpool_limits(limits=cores, user_api="blas"):
+        return _cpu_oracle_sample(args, budget_s, cores, install_oracle_linears, harness)
+
+
+def _cpu_oracle_sample(args, budget_s, cores, install_oracle_linears, harness):
     vlm = harness.VLMConfig(layers=1, vocab=2048)
     dit = harness.DiTConfig(layers=2)
     policy = harness.build_policy("cpu", vlm=vlm, dit=dit)

@@ -220,14 +220,16 @@ def test_bench_rank_reduction_over_gloo():
 
 
 def test_bench_reference_arm_prints_the_contract_line():
+    # OMP_NUM_THREADS=1 as torchrun sets it: the arm still uses every core.
     out = subprocess.run(
         [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--cpu-sample-seconds", "1"],
-        capture_output=True, text=True, timeout=600, cwd=ROOT,
+        capture_output=True, text=True, timeout=600, cwd=ROOT, env={**os.environ, "OMP_NUM_THREADS": "1"},
     )
     assert out.returncode == 0, out.stderr[-2000:]
     line = json.loads(out.stdout.strip().splitlines()[-1])
     for key in ("metric", "value", "unit", "impl", "cpu_baseline", "e2e", "higher_is_better", "config"):
         assert key in line
     assert line["impl"] == "reference" and line["higher_is_better"] is False
-    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["kind"] == "port"
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
     assert line["e2e"]["h2d_bytes_per_step"] == 0
