@@ -630,16 +630,22 @@ def main():
         torch.cuda.set_device(0)
         run_kernel(args)
         return
+    if args.impl == "reference":
+        # Rank 0 alone times the host path; no process group is needed.
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if args.robots is not None:
+            if args.robots % world:
+                raise SystemExit(f"--robots {args.robots} does not split over {world} GPUs")
+            args.batch = args.robots // world
+        run_reference(args, world, int(os.environ.get("RANK", "0")))
+        return
     world, rank, local = dist_setup(args)
     if args.robots is not None:
         if args.robots % world:
             raise SystemExit(f"--robots {args.robots} does not split over {world} GPUs")
         args.batch = args.robots // world
     try:
-        if args.impl == "reference":
-            run_reference(args, world, rank)
-        else:
-            run_ours(args, world, rank, local)
+        run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

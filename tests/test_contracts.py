@@ -233,3 +233,23 @@ def test_bench_reference_arm_prints_the_contract_line():
     assert line["cpu_baseline"]["kind"] == "port"
     assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_bench_reference_arm_under_torchrun_prints_one_line():
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = subprocess.run(
+        [
+            sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+            "--master-addr", "127.0.0.1", "--master-port", str(port), str(ROOT / "bench.py"),
+            "--impl", "reference", "--gpus", "2", "--steps", "1", "--cpu-sample-seconds", "1",
+        ],
+        capture_output=True, text=True, timeout=600, cwd=ROOT,
+    )
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [json.loads(s) for s in out.stdout.splitlines() if s.startswith("{")]
+    assert len(lines) == 1 and lines[0]["impl"] == "reference" and lines[0]["n_gpus"] == 2
+    assert lines[0]["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
