@@ -67,6 +67,7 @@ def parse():
         help="time one quantized GEMM shape alone (for kernel profiling), not the step",
     )
     p.add_argument("--kernel-weights-mb", type=float, default=600.0, help="rotating weight copies for --kernel")
+    p.add_argument("--kernel-residual", action="store_true", help="--kernel with the bf16 residual epilogue")
     return p.parse_args()
 
 
@@ -587,11 +588,12 @@ def run_kernel(args):
     sa = torch.rand(m, device="cuda", generator=g)
     sw = torch.rand(npd, device="cuda", generator=g)
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    res = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16) if args.kernel_residual else None
     iters = max(args.steps, copies)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 1)):
-            ops.gemm(qa, sa, weights[i % copies], sw, None, bits, n_store=n, out=out)
+            ops.gemm(qa, sa, weights[i % copies], sw, None, bits, n_store=n, out=out, residual=res)
     torch.cuda.synchronize()
     # One CUDA graph of `iters` launches back to back (each a different weight
     # copy), replayed: the launches chain with programmatic dependent launch
@@ -599,7 +601,7 @@ def run_kernel(args):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(iters):
-            ops.gemm(qa, sa, weights[i % copies], sw, None, bits, n_store=n, out=out)
+            ops.gemm(qa, sa, weights[i % copies], sw, None, bits, n_store=n, out=out, residual=res)
     for _ in range(max(args.warmup, 1)):
         graph.replay()
     torch.cuda.synchronize()
@@ -613,10 +615,11 @@ def run_kernel(args):
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1) * 1e3 / iters)
     us = sorted(times)[2]
-    algo = wbytes + m * cols + 4 * m + 4 * npd + 2 * m * n
+    algo = wbytes + m * cols + 4 * m + 4 * npd + 2 * m * n * (2 if res is not None else 1)
     hbm, _ = peaks()
     print(json.dumps({
-        "kernel": f"gemm_i8_kernel<{bits}>", "m": m, "k": k, "n": n, "us_per_launch": round(us, 3),
+        "kernel": f"gemm_i8_kernel<{bits}>", "m": m, "k": k, "n": n, "residual": res is not None,
+        "us_per_launch": round(us, 3),
         "algorithmic_bytes": algo, "GBs": round(algo / us / 1e3, 1), "hbm_frac": round(algo / us / 1e3 / hbm, 4),
         "TOPS": round(2 * m * n * k / us / 1e6, 1), "int8_frac": round(2 * m * n * k / us / 1e6 / INT8_PEAK_TOPS, 4),
         "weight_copies": copies, "launches": iters,
