@@ -299,7 +299,11 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
   // number of token tiles and the split-K cluster size:
   //  * a 128 x BN x 128 K block costs max(347, 2 BN) MMA cycles (measured
   //    kind::i8 issue rate: N <= 128 has a fixed ~87-cycle MMA, full rate is
-  //    8192 MAC/clk/SM);
+  //    8192 MAC/clk/SM), and at least the TMA round trip (~2700 cycles) over
+  //    the stages in flight: per-CTA traces show K blocks of ~540 cycles
+  //    with 5 stages whatever the token tile.  With that term M=544 runs
+  //    4 token tiles of 144 on 128 CTAs (6 stages) instead of 3 of 192 on
+  //    96 (5 stages): VLM prefill 2.15 -> 2.03 ms in the control step;
   //  * its operands (16 KB of weights + 128 BN bytes) arrive at the CTA's
   //    share of HBM (~3400 B/clk for weights streamed once, single token
   //    tile) or of L2 (~9000 B/clk when several token tiles re-read the
@@ -307,10 +311,10 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
   //  * each CTA pays ~3000 cycles of launch, prologue and epilogue, +1500 for
   //    the cluster reduction of split-K;
   //  * CTAs under ~113 KB of shared memory run two per SM.
-  // Measured against a K-block latency model (which wins on isolated
-  // launches) this one gives the faster VLM prefill inside the full CUDA
-  // graph of the control step, where each GEMM shares its SMs with the
-  // programmatically launched kernels around it.
+  // A model of the K-block latency alone (which wins on isolated launches)
+  // gave a slower VLM prefill inside the full CUDA graph of the control
+  // step, where each GEMM shares its SMs with the programmatically launched
+  // kernels around it, than this combined one.
   double best_cost = 1e30;
   const int mt0 = int((m + 255) / 256);
   const int mt1 = m <= 256 ? mt0 : mt0 + 3;
@@ -345,7 +349,8 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
       const double w_bw = std::min(128.0, (mt == 1 ? 3400.0 : 9000.0) / active);
       const double a_bw = std::min(128.0, 9000.0 / active);
       const double kb = double(num_kb) / s;
-      const double per_kb = std::max(std::max(347.0, 2.0 * bn), w_bytes / w_bw + a_bytes / a_bw);
+      const double per_kb = std::max(std::max(std::max(347.0, 2.0 * bn), 2700.0 / stages),
+                                     w_bytes / w_bw + a_bytes / a_bw);
       const double per_cta = kb * per_kb + 3000.0 + (s > 1 ? 1500.0 : 0.0);
       const double cost = waves * per_cta;
       if (cost < best_cost * 0.999) {
