@@ -82,3 +82,17 @@ def test_gemm_planner_always_returns_a_launchable_plan():
                     assert wt in (1, 2) and (wt == 1 or (bits == 8 and splits == 1 and stages >= 3))
                     if splits > 1:
                         assert stages * (16384 + bn * 128) >= bn * (512 + 128)
+
+
+def test_vlm_prefill_plans_fill_the_machine_in_one_wave():
+    """M = 544 projections of the VLM prefill: the cost model charges every K
+    block the TMA round trip over its stages, which gives 4 token tiles of
+    144 with 6 stages on 128 CTAs (measured faster in the control step than
+    3 tiles of 192 with 5 stages on 96 CTAs)."""
+    lib = _lib.lib()
+    lib.pir2b_gemm_plan.restype = ctypes.c_int
+    for k, n, splits_want in ((2048, 4096, 1), (2048, 2048, 2), (6144, 2048, 2)):
+        status, (bn, mt, splits, stages, smem, wt) = _plan(lib, 8, 544, n, k)
+        assert status == 0
+        assert (bn, mt, splits, stages, wt) == (144, 4, splits_want, 6, 1), (k, n)
+        assert (n // 128) * mt * splits == 128
