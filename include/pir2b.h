@@ -64,6 +64,16 @@ const char *pir2b_last_error(void);
  * No counterpart in the reference (which has no bounded device waits). */
 int pir2b_device_status(int *status_out, void *stream);
 
+/* Status word value left by pir2b_wait_probe. */
+#define PIR2B_STATUS_TIMEOUT_PROBE 0x105
+
+/* Self-test of the bounded device waits: launches one thread that waits on
+ * an mbarrier nothing arrives at.  The wait gives up after its budget
+ * (about 1 s), sets the device status word to PIR2B_STATUS_TIMEOUT_PROBE
+ * and writes 0 to the device int `result`.  Asynchronous on `stream`.
+ * No counterpart in the reference. */
+int pir2b_wait_probe(int *result, void *stream);
+
 /* Per-row symmetric quantization and packing of BF16 activations.
  * Replaces the Triton `_prepare` kernel and its native twin
  * `prepare_integer<Bits>`:

@@ -19,6 +19,7 @@ MODE_PLAIN, MODE_GATED, MODE_LUT = 0, 1, 2
 BIAS_NONE, BIAS_ZERO, BIAS_ADD = 0, 1, 2
 NORM_NONE, NORM_RMS, NORM_LN = 0, 1, 2
 OUT_INT8, OUT_INT4, OUT_NVFP4 = 8, 4, 16
+STATUS_TIMEOUT_PROBE = 0x105   # device status word left by pir2b_wait_probe
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -30,6 +31,7 @@ SIGNATURES = {
     "pir2b_version": [],
     "pir2b_last_error": [],
     "pir2b_device_status": [ctypes.POINTER(_I), _P],
+    "pir2b_wait_probe": [_P, _P],
     "pir2b_quant_rows": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _P, _P, _P],
     "pir2b_norm_quant_rows": [
         _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I, _F, _I, _I64, _I64, _P, _P, _P,
@@ -86,6 +88,19 @@ def check(status, what):
         if error is ValueError:
             raise ValueError(f"{what}: {message}")
         raise Pir2bError(status, f"{what}: {message}")
+
+
+def wait_probe(result, stream=None):
+    """Launches the bounded-wait self-test kernel: one thread waits on an
+    mbarrier nothing arrives at, gives up after its ~1 s budget, sets the
+    device status word to STATUS_TIMEOUT_PROBE and writes 0 to `result`
+    (a CUDA int32 tensor of one element)."""
+    import torch
+
+    if not result.is_cuda or result.dtype != torch.int32 or result.numel() != 1:
+        raise ValueError("wait_probe needs a one-element CUDA int32 tensor")
+    handle = (stream or torch.cuda.current_stream()).cuda_stream
+    check(lib().pir2b_wait_probe(result.data_ptr(), handle), "wait_probe")
 
 
 def device_status(stream=None):

@@ -512,6 +512,17 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   return cuda_status(e, "gemm launch");
 }
 
+// Self-test of the bounded wait: one thread waits on an mbarrier that
+// nothing arrives at.  After the wait budget (about 1 s of SM clock)
+// `mbar_wait` gives up and records kStatusTimeoutProbe in the status word;
+// the kernel then writes 0 to *result (1 would mean the wait completed).
+__global__ void wait_probe_kernel(int *result) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  *result = mbar_wait(&bar, 0, kStatusTimeoutProbe) ? 1 : 0;
+}
+
 } // namespace pir2b
 
 using namespace pir2b;
@@ -521,6 +532,16 @@ extern "C" {
 int pir2b_version(void) { return 100; }
 
 const char *pir2b_last_error(void) { return g_last_error; }
+
+int pir2b_wait_probe(int *result, void *stream) {
+  if (result == nullptr || !aligned(result, 4))
+    return fail(PIR2B_EINVAL, "wait_probe needs a 4-byte aligned device int");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  wait_probe_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(result);
+  return cuda_status(cudaGetLastError(), "wait probe launch");
+}
 
 int pir2b_device_status(int *status_out, void *stream) {
   if (status_out == nullptr)

@@ -22,6 +22,7 @@ enum DeviceStatus : int {
   kStatusTimeoutMma = 0x102,
   kStatusTimeoutEpilogue = 0x103,
   kStatusTimeoutConvert = 0x104,
+  kStatusTimeoutProbe = 0x105,   // pir2b_wait_probe (self-test)
 };
 
 // Budget of a bounded wait, in SM clock cycles (~1 s at 1.965 GHz): far
