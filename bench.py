@@ -192,16 +192,23 @@ class GemmTimer:
 
 
 def gemm_bytes(s):
+    """Algorithmic HBM bytes of one recorded GEMM launch: each operand,
+    scale vector, bias, residual and output once.  `n` is the weight rows the
+    GEMM multiplies (gate and up for SwiGLU), `out_n` the bf16 columns it
+    writes (half of them for SwiGLU)."""
+    out = 2 * s["m"] * s.get("out_n", s["n"])
+    res = 2 * s["m"] * s["n"] if s.get("residual") else 0
+    res += 2 * s["npad"] if s.get("bias") else 0
     if s["bits"] == "fp4":
         # E2M1 operands (half a byte per value) + one UE4M3 factor per 16.
-        return (s["n"] + s["m"]) * s["k"] * 9 // 16 + 2 * s["m"] * s["n"]
+        return (s["n"] + s["m"]) * s["k"] * 9 // 16 + out + res
     if s["bits"] == "fp8":
         s = dict(s, bits=8)   # one byte per E4M3 value, like int8
     wb = s["npad"] * s["k"] * s["bits"] // 8
     if s.get("input") == "rows":
         # Fused pack: the GEMM reads the bf16 rows themselves.
-        return wb + 2 * s["m"] * s["k_logical"] + 4 * s["npad"] + 2 * s["m"] * s["n"]
-    return wb + s["m"] * s["k"] * s["bits"] // 8 + 4 * s["m"] + 4 * s["npad"] + 2 * s["m"] * s["n"]
+        return wb + 2 * s["m"] * s["k_logical"] + 4 * s["npad"] + out + res
+    return wb + s["m"] * s["k"] * s["bits"] // 8 + 4 * s["m"] + 4 * s["npad"] + out + res
 
 
 TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemm_i8_step_w8a8_traffic.md")

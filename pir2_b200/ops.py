@@ -189,7 +189,8 @@ def gemm(
     )
     _lib.check(status, "pir2b_gemm")
     if recorder is not None:
-        recorder.after(a.device, bits=bits, m=m, n=n_store, k=k_pad, npad=n_pad)
+        recorder.after(a.device, bits=bits, m=m, n=n_store, k=k_pad, npad=n_pad, residual=residual is not None,
+                       bias=bias is not None)
     return out
 
 
@@ -262,7 +263,8 @@ def _gemm_fused(w, sw, bias, bits, *, qa=None, sa=None, x=None, x_max=None, bias
     _lib.check(status, "pir2b_gemm_fused")
     if recorder is not None:
         recorder.after(w.device, bits=bits, m=m, n=n_store, k=k_pad, npad=n_pad,
-                       input="rows" if x is not None else "packed", k_logical=k)
+                       input="rows" if x is not None else "packed", k_logical=k, residual=residual is not None,
+                       bias=bias is not None)
     return out
 
 
@@ -296,7 +298,8 @@ def gemm_swiglu(a, sa, w, sw, bias, silu_lut, *, half_n, bias_mode=None, out=Non
     )
     _lib.check(status, "pir2b_gemm_swiglu")
     if recorder is not None:
-        recorder.after(a.device, bits=8, m=m, n=2 * half_n, k=k_pad, npad=2 * half_n)
+        recorder.after(a.device, bits=8, m=m, n=2 * half_n, k=k_pad, npad=2 * half_n, out_n=half_n,
+                       bias=bias is not None)
     return out
 
 
@@ -456,7 +459,8 @@ def gemm_fp8(qa, sa_rows, qw, sw_cols, bias=None, *, n, residual=None, out=None)
     )
     _lib.check(status, "pir2b_gemm_fp8")
     if recorder is not None:
-        recorder.after(qa.device, bits="fp8", m=m, n=n, k=kpad, npad=npad)
+        recorder.after(qa.device, bits="fp8", m=m, n=n, k=kpad, npad=npad, residual=residual is not None,
+                       bias=bias is not None)
     return out
 
 

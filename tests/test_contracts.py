@@ -253,3 +253,21 @@ def test_bench_reference_arm_under_torchrun_prints_one_line():
     lines = [json.loads(s) for s in out.stdout.splitlines() if s.startswith("{")]
     assert len(lines) == 1 and lines[0]["impl"] == "reference" and lines[0]["n_gpus"] == 2
     assert lines[0]["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
+
+
+def test_bench_algorithmic_bytes_per_gemm():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    # M=17 K=1536 N=6144 W8A8: weights, codes, row and channel scales, output.
+    s = dict(bits=8, m=17, n=6144, k=1536, npad=6144)
+    assert bench.gemm_bytes(s) == 9437184 + 26112 + 68 + 24576 + 208896
+    # The residual epilogue also reads a bf16 [m, n] tile.
+    assert bench.gemm_bytes(dict(s, residual=True)) == bench.gemm_bytes(s) + 2 * 17 * 6144
+    # W4A4: half a byte per operand value.
+    assert bench.gemm_bytes(dict(s, bits=4)) == 9437184 // 2 + 26112 // 2 + 68 + 24576 + 208896
+    # A bias vector is read once.
+    assert bench.gemm_bytes(dict(s, bias=True)) == bench.gemm_bytes(s) + 2 * 6144
+    # SwiGLU multiplies gate and up rows but writes half the columns.
+    g = dict(bits=8, m=544, n=12288, k=2048, npad=12288, out_n=6144)
+    assert bench.gemm_bytes(g) == 12288 * 2048 + 544 * 2048 + 4 * 544 + 4 * 12288 + 2 * 544 * 6144
