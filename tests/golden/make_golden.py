@@ -16,13 +16,25 @@ What it runs, unmodified, from the reference:
   * `channel_scales` (coexecution/optimization/backends/thor/smoothquant.py:
     27-45), which is plain CPU torch;
   * the explicit torch formula of the bitwise Linear test
-    (tests/gpu/test_quantization_gpu.py:37-44).
+    (tests/gpu/test_quantization_gpu.py:37-44);
+  * the NVFP4 producer `_smooth_pack` with `_store_fp4_row`
+    (coexecution/optimization/backends/thor/packing.py:24-54, :314-349)
+    and the FP8 pair `_fp8_partial_amax` / `_fp8_scale_and_cast` of
+    `prepare_fp8` (packing.py:451-519).
 
 The Triton kernels run under Triton's CPU interpreter (TRITON_INTERPRET=1).
 Two interpreter emulation gaps are closed first, so that the CPU run has the
 GPU's arithmetic: fp32 -> bf16 casts are made round-to-nearest-even (the
 interpreter truncates), and `libdevice.nearbyint` / `libdevice.rsqrt` are
-mapped to numpy (`rint`, and 1/sqrt).  Nothing in the reference is edited.
+mapped to numpy (`rint`, and 1/sqrt).  fp32 <-> E4M3 casts go through
+torch's float8_e4m3fn conversion (round-to-nearest-even; the reference
+clamps to +-448 first, so the GPU's satfinite never differs), and the one
+inline-PTX instruction of `_store_fp4_row`, `cvt.rn.satfinite.e2m1x2.f32`,
+is evaluated from its PTX definition (round-to-nearest-even onto the E2M1
+grid, saturating at 6, the first source operand in the high nibble); any
+other inline assembly still raises.  Plain `/` runs as IEEE division here
+(the oracle's FP8 `fast` variant states the same).  Nothing in the
+reference is edited.
 """
 
 import os
@@ -49,10 +61,53 @@ def _convert_float(data, src, dst, rounding_mode):
     if src == tl.bfloat16 and dst == tl.float32:
         bits = np.ascontiguousarray(data).view(np.uint16).astype(np.uint32) << 16
         return bits.view(np.float32)
+    if src == tl.float32 and dst == tl.float8e4nv:
+        t = torch.from_numpy(np.ascontiguousarray(data).view(np.float32).copy())
+        return t.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    if src == tl.float8e4nv and dst == tl.float32:
+        t = torch.from_numpy(np.ascontiguousarray(data).view(np.uint8).copy())
+        return t.view(torch.float8_e4m3fn).float().numpy()
     return _original_convert(data, src, dst, rounding_mode)
 
 
 _interp._convert_float = _convert_float
+
+E2M1_CVT = "cvt.rn.satfinite.e2m1x2.f32"
+
+
+def e2m1_rn_satfinite(v):
+    """E2M1 codes of fp32 values as `cvt.rn.satfinite` defines them: the
+    nearest of 0, 0.5, 1, 1.5, 2, 3, 4, 6 (grid steps 0.5 below 2, 1 below
+    4, 2 up to 6), ties to the even code, magnitudes above 6 saturating to
+    6, the sign bit kept (also for a result of zero)."""
+    v = np.asarray(v, dtype=np.float64)
+    if np.isnan(v).any():
+        raise ValueError("NaN input: not part of these golden cases")
+    a = np.abs(v)
+    code = np.where(a < 2.0, np.rint(a / 0.5), np.where(a < 4.0, np.rint(a) + 2.0, np.rint(a / 2.0) + 4.0))
+    code = np.minimum(code, 7.0).astype(np.uint32)
+    return code | (np.signbit(v).astype(np.uint32) << 3)
+
+
+class _AsmCall:
+    def __init__(self, handle):
+        self.handle = handle
+
+    def get_result(self, index):
+        return self.handle
+
+
+def _create_inline_asm(self, asm, constraints, values, types, is_pure, pack):
+    # `cvt.rn.satfinite.e2m1x2.f32 d, a, b` puts cvt(a) in the high nibble;
+    # _store_fp4_row passes a = $2 (its second argument), b = $1.
+    if E2M1_CVT not in asm or constraints != "=r,f,f" or len(values) != 2 or pack != 1:
+        raise NotImplementedError(f"inline asm not emulated: {asm!r}")
+    first, second = (np.asarray(h.data, dtype=np.float32) for h in values)
+    pair = (e2m1_rn_satfinite(second) << 4) | e2m1_rn_satfinite(first)
+    return _AsmCall(_interp.TensorHandle(pair.astype(np.uint32), tl.uint32))
+
+
+_interp.InterpreterBuilder.create_inline_asm = _create_inline_asm
 
 
 def _unary(fn):
@@ -78,6 +133,7 @@ from coexecution.kernels.ampere_ada import producers as ref_producers  # noqa: E
 from coexecution.optimization.backends.thor.smoothquant import (  # noqa: E402
     channel_scales,
 )
+from coexecution.optimization.backends.thor import packing as ref_packing  # noqa: E402
 
 for module in (ref_integer, ref_modulation, ref_producers):
     module.libdevice = _Libdevice
@@ -123,6 +179,47 @@ def outliers(g, rows, k, fraction=0.01, factor=20.0):
     cols = torch.randperm(k, generator=g)[: max(1, int(k * fraction))]
     x[:, cols] *= factor
     return x.to(torch.bfloat16)
+
+
+def floating_cases(out):
+    """NVFP4 (`_smooth_pack`, FP4) and FP8 (`prepare_fp8`) vectors, seeded
+    apart from the integer cases so those stay unchanged."""
+    g = torch.Generator().manual_seed(1)
+    # NVFP4: 130 rows cross a 128-row factor block; K = 96 leaves a partly
+    # used 4-factor column group; row 1 is all zero; row 2 is tiny enough
+    # that its block scales underflow E4M3 (the packer then divides by the
+    # fp32 scale itself); outliers stretch the blocks.
+    for name, (rows, k) in {"r130_k96": (130, 96), "r9_k256": (9, 256)}.items():
+        x = outliers(g, rows, k)
+        x[1] = 0.0
+        x[2] = (torch.randn(k, generator=g) * 1e-6).to(torch.bfloat16)
+        smooth = (0.5 + 1.5 * torch.rand(k, generator=g)).to(torch.float32)
+        packed = torch.zeros((rows, k // 2), dtype=torch.uint8)
+        sf = torch.zeros((triton.cdiv(rows, 128) * 128, triton.cdiv(k // 16, 4) * 4), dtype=torch.uint8)
+        ref_packing._smooth_pack[(rows,)](x, smooth, packed, sf, k, triton.next_power_of_2(k), True)
+        out[f"fp4_x_{name}"], out[f"fp4_smooth_{name}"] = bits(x), smooth.numpy().copy()
+        out[f"fp4_packed_{name}"], out[f"fp4_sf_{name}"] = packed.numpy().copy(), sf.numpy().copy()
+    # FP8: one partial block, several partial blocks, and +-inf values (left
+    # out of the amax, clamped to +-448 in the codes).
+    specials = torch.randn(33, 130, generator=g)
+    specials[0, 0], specials[5, 7] = float("inf"), float("-inf")
+    for name, x in {
+        "r17_k96": torch.randn(17, 96, generator=g).to(torch.bfloat16),
+        "r100_k128": outliers(g, 100, 128),
+        "inf_r33_k130": specials.to(torch.bfloat16),
+    }.items():
+        count = x.numel()
+        parts = triton.cdiv(count, 4096)
+        partial = torch.zeros(parts, dtype=torch.float32)
+        packed = torch.zeros(x.shape, dtype=torch.float8_e4m3fn)
+        scale = torch.zeros((), dtype=torch.float32)
+        ref_packing._fp8_partial_amax[(parts,)](x, partial, count, 4096)
+        ref_packing._fp8_scale_and_cast[(parts,)](
+            x, partial, packed, scale, count, parts, triton.next_power_of_2(parts), 4096
+        )
+        out[f"fp8_x_{name}"] = bits(x)
+        out[f"fp8_q_{name}"] = packed.view(torch.uint8).numpy().copy()
+        out[f"fp8_s_{name}"] = scale.numpy().copy()
 
 
 def main():
@@ -232,6 +329,7 @@ def main():
         out[f"lin_qw_b{b}"] = qw.to(torch.int8).numpy().copy()
         out[f"lin_ws_b{b}"] = ws_.detach().numpy().copy()
 
+    floating_cases(out)
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT}: {len(out)} arrays, {os.path.getsize(OUT)} bytes")
 

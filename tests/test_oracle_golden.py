@@ -131,3 +131,27 @@ def test_linear_matches_reference_bitwise_formula(bits):
     assert same.sum() >= 10
     assert np.array_equal(y[same], ref[same])
     assert not np.any((y != ref)[same])
+
+
+@pytest.mark.parametrize("name", ["r130_k96", "r9_k256"])
+def test_nvfp4_pack_matches_reference(name):
+    """`_smooth_pack` with FP4 (thor/packing.py:24-54, :314-349): bf16(x / s)
+    then E2M1 codes and swizzled UE4M3 block factors, byte for byte (zero
+    row, factors that underflow E4M3, a partly used factor group, two
+    128-row factor blocks)."""
+    x = oracle.bf16_bits_to_f32(GOLDEN[f"fp4_x_{name}"])
+    smooth = GOLDEN[f"fp4_smooth_{name}"]
+    values = oracle.bf16_round((x / smooth[None, :]).astype(np.float32))
+    packed, sf = oracle.pack_nvfp4(values)
+    assert np.array_equal(packed, GOLDEN[f"fp4_packed_{name}"])
+    assert np.array_equal(sf, GOLDEN[f"fp4_sf_{name}"])
+
+
+@pytest.mark.parametrize("name", ["r17_k96", "r100_k128", "inf_r33_k130"])
+def test_fp8_prepare_matches_reference(name):
+    """`prepare_fp8` (thor/packing.py:451-519): per-tensor scale from the
+    finite amax and E4M3 codes of the clamped quotients (+-inf left out of
+    the amax and clamped to +-448)."""
+    q, scale = oracle.quant_fp8(GOLDEN[f"fp8_x_{name}"], fast=True)
+    assert np.float32(scale).view(np.uint32) == GOLDEN[f"fp8_s_{name}"].view(np.uint32)
+    assert np.array_equal(q, GOLDEN[f"fp8_q_{name}"].reshape(q.shape))
