@@ -8,9 +8,10 @@ path (pir2_b200) never imports it.
 
 Pinning: tests/golden/ holds vectors produced by running the reference's own
 Triton kernels (integer.py `_prepare`, modulation.py producers, producers.py
-`_rms_tail_pack`) under Triton's CPU interpreter, the reference's CPU-runnable
-`channel_scales`, and the explicit torch formula of the reference's bitwise
-Linear test; tests/test_oracle_golden.py checks this oracle against them.
+`_rms_tail_pack`, thor/packing.py NVFP4 producers and `prepare_fp8`) under
+Triton's CPU interpreter, the reference's CPU-runnable `channel_scales`, and
+the explicit torch formula of the reference's bitwise Linear test;
+tests/test_oracle_golden.py checks this oracle against them.
 """
 
 from .quant import *  # noqa: F401,F403

@@ -17,10 +17,11 @@ What it runs, unmodified, from the reference:
     27-45), which is plain CPU torch;
   * the explicit torch formula of the bitwise Linear test
     (tests/gpu/test_quantization_gpu.py:37-44);
-  * the NVFP4 producer `_smooth_pack` with `_store_fp4_row`
-    (coexecution/optimization/backends/thor/packing.py:24-54, :314-349)
-    and the FP8 pair `_fp8_partial_amax` / `_fp8_scale_and_cast` of
-    `prepare_fp8` (packing.py:451-519).
+  * the NVFP4 producers `_smooth_pack`, `_rmsnorm_pack` and
+    `_norm_modulation_pack` with `_store_fp4_row`
+    (coexecution/optimization/backends/thor/packing.py:24-54, :109-150,
+    :314-349, :395-415) and the FP8 pair `_fp8_partial_amax` /
+    `_fp8_scale_and_cast` of `prepare_fp8` (packing.py:451-519).
 
 The Triton kernels run under Triton's CPU interpreter (TRITON_INTERPRET=1).
 Two interpreter emulation gaps are closed first, so that the CPU run has the
@@ -220,6 +221,29 @@ def floating_cases(out):
         out[f"fp8_x_{name}"] = bits(x)
         out[f"fp8_q_{name}"] = packed.view(torch.uint8).numpy().copy()
         out[f"fp8_s_{name}"] = scale.numpy().copy()
+    # Fused NVFP4 producers: RMSNorm (VLM shape) and LayerNorm + residual add
+    # + per-batch AdaLN (DiT shape, [B, T, D] = [2, 17, 1536]).
+    xr = outliers(g, 6, 2048)
+    gamma = (1.0 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    packed = torch.zeros((6, 1024), dtype=torch.uint8)
+    sf = torch.zeros((128, 128), dtype=torch.uint8)
+    ref_packing._rmsnorm_pack[(6,)](xr, gamma, packed, sf, None, 2048, 1e-6, 2048, True, False)
+    out.update(fp4rms_x=bits(xr), fp4rms_gamma=bits(gamma), fp4rms_packed=packed.numpy().copy(), fp4rms_sf=sf.numpy().copy())
+    b, t, d = 2, 17, 1536
+    xl = torch.randn(b, t, d, generator=g).to(torch.bfloat16)
+    yl = torch.randn(b, t, d, generator=g).to(torch.bfloat16)
+    scale = (torch.randn(b, d, generator=g) * 0.5).to(torch.bfloat16)
+    shift = (torch.randn(b, d, generator=g) * 0.5).to(torch.bfloat16)
+    summed = torch.zeros_like(xl)
+    packed = torch.zeros((b * t, d // 2), dtype=torch.uint8)
+    sf = torch.zeros((128, triton.cdiv(d // 16, 4) * 4), dtype=torch.uint8)
+    ref_packing._norm_modulation_pack[(b * t,)](
+        xl, scale, shift, yl, summed, packed, sf, None, d, t, d, d, 1e-6, 2048, True, True, True, False
+    )
+    out.update(
+        fp4ln_x=bits(xl), fp4ln_y=bits(yl), fp4ln_scale=bits(scale), fp4ln_shift=bits(shift),
+        fp4ln_summed=bits(summed), fp4ln_packed=packed.numpy().copy(), fp4ln_sf=sf.numpy().copy(),
+    )
 
 
 def main():

@@ -1,6 +1,7 @@
 """Pins the CPU oracle against vectors produced by the piR2 reference itself
 (tests/golden/make_golden.py runs the reference's own Triton kernels under
-the CPU interpreter, its channel_scales and its bitwise-test torch formula).
+the CPU interpreter, integer, NVFP4 and FP8 producers alike, its
+channel_scales and its bitwise-test torch formula).
 """
 
 import os
@@ -155,3 +156,26 @@ def test_fp8_prepare_matches_reference(name):
     q, scale = oracle.quant_fp8(GOLDEN[f"fp8_x_{name}"], fast=True)
     assert np.float32(scale).view(np.uint32) == GOLDEN[f"fp8_s_{name}"].view(np.uint32)
     assert np.array_equal(q, GOLDEN[f"fp8_q_{name}"].reshape(q.shape))
+
+
+def test_fused_nvfp4_producers_match_reference():
+    """`_rmsnorm_pack` and `_norm_modulation_pack` (LayerNorm + residual add
+    + per-batch AdaLN) to NVFP4 (thor/packing.py:109-150, :395-415): codes,
+    swizzled factors and the bf16 residual sum equal the oracle's
+    composition byte for byte on these vectors.  The variance sums differ in
+    order (fp32 in the interpreter, fp64 in the oracle), so other inputs may
+    land one bf16 step apart, as the reference notes for its own norms."""
+    from oracle import quant as oq
+
+    v = oq.rms_norm_values(GOLDEN["fp4rms_x"], GOLDEN["fp4rms_gamma"], 1e-6)
+    packed, sf = oq.pack_nvfp4(v)
+    assert np.array_equal(packed, GOLDEN["fp4rms_packed"]) and np.array_equal(sf, GOLDEN["fp4rms_sf"])
+
+    tokens, d = 17, 1536
+    x = oq.bf16_bits_to_f32(GOLDEN["fp4ln_x"].reshape(-1, d))
+    y = oq.bf16_bits_to_f32(GOLDEN["fp4ln_y"].reshape(-1, d))
+    r = oq.bf16_round((x + y).astype(np.float32))
+    assert np.array_equal(oq.f32_to_bf16_bits(r), GOLDEN["fp4ln_summed"].reshape(-1, d))
+    v = oq.modulate_values(oq.layer_norm_values(r, 1e-6), GOLDEN["fp4ln_scale"], GOLDEN["fp4ln_shift"], tokens)
+    packed, sf = oq.pack_nvfp4(v)
+    assert np.array_equal(packed, GOLDEN["fp4ln_packed"]) and np.array_equal(sf, GOLDEN["fp4ln_sf"])
