@@ -209,13 +209,23 @@ int pir2b_dit_ffn(const void *qa, const float *sa, const void *up_w, const float
                   void *stream);
 
 /* pir2b_dit_ffn with its scratch in a static device array of this library
- * (about 530 KB per device) instead of a caller workspace: it allocates no
- * memory.  No counterpart in the reference.  1 <= m <= 64, f <= 8192, the
- * other limits as pir2b_dit_ffn.  Each call clears the array's counters on
- * `stream` first.  All calls on one device share the array: calls on
- * different streams of the same device must not overlap (order them on one
- * stream or synchronise between them); calls on different devices are
- * independent. */
+ * (about 530 KB on every device that loads it, held until the process
+ * exits) instead of a caller workspace.  No counterpart in the reference.
+ * It is for callers that cannot call cudaMalloc once they are running, such
+ * as a robot control loop that must not allocate device memory after
+ * start-up, or a host runtime that owns every device buffer and exposes no
+ * allocator to its plugins: they pass inputs and outputs and nothing else.
+ * It calls no cudaMalloc, cudaFree or allocating library routine.
+ * 1 <= m <= 64 and f <= 8192 (the array's size; larger problems return
+ * PIR2B_EINVAL), the other limits as pir2b_dit_ffn.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.
+ * Each call clears the array's counters on `stream` first; the rest of the
+ * array keeps the last call's contents and is written before it is read.
+ * All calls on one device share the array: calls that overlap on the GPU
+ * (different streams, not ordered) race and corrupt each other's results,
+ * so order them on one stream or synchronise between them; calls on
+ * different devices are independent. */
 int pir2b_dit_ffn_static(const void *qa, const float *sa, const void *up_w, const float *up_sw,
                          const void *up_bias, int up_bias_mode, const void *gelu_lut,
                          const void *down_w, const float *down_sw, const void *down_bias,

@@ -50,6 +50,7 @@ struct DeviceInfo {
   int sms = 0;
   int max_smem = 0;
   bool attrs_set = false;
+  void *ffn_scratch = nullptr;   // device address of g_ffn_scratch (set on first use)
 };
 
 static std::mutex g_mutex;
@@ -1243,6 +1244,20 @@ int pir2b_dit_ffn(const void *qa, const float *sa, const void *up_w, const float
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  // Up CTAs wait for every other up CTA (the row maxima), so all up clusters
+  // must be resident together, and one down cluster beside them lets the
+  // grid make progress while the rest queue.  Clusters of 8 are placed per
+  // GPC, so the SM count alone does not show how many fit.
+  int clusters = 0;
+  cudaError_t oe = cudaOccupancyMaxActiveClusters(&clusters, dit_ffn_kernel, &cfg);
+  if (oe != cudaSuccess)
+    return cuda_status(oe, "dit_ffn cluster occupancy");
+  const int up_clusters = up_ctas / kFfnSplits;
+  if (clusters < up_clusters + 1)
+    return fail(PIR2B_EINVAL,
+                "dit_ffn: %d clusters of %d CTAs fit the device at once; this problem needs %d "
+                "resident (all %d up clusters and one down cluster)",
+                clusters, kFfnSplits, up_clusters + 1, up_clusters);
   return cuda_status(cudaLaunchKernelEx(&cfg, dit_ffn_kernel, tm_up, tm_act, tm_down, tm_codes, a),
                      "dit_ffn launch");
 }
@@ -1269,15 +1284,28 @@ int pir2b_dit_ffn_static(const void *qa, const float *sa, const void *up_w, cons
   const int64_t need = ffn_workspace_layout(m, f, &max_off, &scale_off, &code_off);
   if (need > kFfnStaticBytes)
     return fail(PIR2B_EINVAL, "dit_ffn_static: problem exceeds the static scratch");
-  // The array's address in the current device's context.
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  // Set-up, once per device on its first call (with that device current):
+  // the array's address in this device's context.  In host code the symbol
+  // itself is only a host-side stand-in, never a device address.
   void *scratch = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(&scratch, g_ffn_scratch);
-  if (e != cudaSuccess || scratch == nullptr)
-    return cuda_status(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
-                       "dit_ffn_static scratch address");
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (dev->ffn_scratch == nullptr) {
+      void *p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_ffn_scratch);
+      if (e != cudaSuccess || p == nullptr)
+        return cuda_status(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
+                           "dit_ffn_static scratch address");
+      dev->ffn_scratch = p;
+    }
+    scratch = dev->ffn_scratch;
+  }
   // The three counters must start at zero (a call that timed out may have
   // left them set); the rest of the scratch is written before it is read.
-  e = cudaMemsetAsync(scratch, 0, 16, static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaMemsetAsync(scratch, 0, 16, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess)
     return cuda_status(e, "dit_ffn_static counter reset");
   return pir2b_dit_ffn(qa, sa, up_w, up_sw, up_bias, up_bias_mode, gelu_lut, down_w, down_sw,

@@ -185,7 +185,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                            (kb0 + i) * kBlockK, n0, wpolicy);
         }
         // Then the codes of h, once every up CTA has written them (generic
-        // stores, read here through the async proxy).
+        // stores, read here through the async proxy).  The counters are
+        // shared with the previous launch on this workspace, which resets
+        // them as it finishes: wait for that grid before reading them, or a
+        // stale count would release the loads of the previous call's codes.
+        pdl_wait();
         wait_counter(counter_codes, unsigned(a.up_ctas));
         fence_proxy_async_global();
         uint8_t *codes = smem + num_kb * kWeightTileBytes;

@@ -583,3 +583,32 @@ def test_dit_ffn_equals_the_four_launch_chain(m, d, f):
     ws = ops.ffn_workspace(torch.device("cuda"), m, f)
     assert int(ws[:12].view(torch.int32).abs().sum()) == 0     # counters reset
     assert_status_clean()
+
+
+@pytest.mark.parametrize("m,d,f", [(17, 1536, 6144), (40, 256, 2048)])
+def test_dit_ffn_back_to_back_calls_on_one_workspace(m, d, f):
+    """Two calls with different inputs, launched back to back on one stream
+    and sharing the workspace: each output equals its own four-launch chain
+    (the second call must not read the first call's codes or counters)."""
+    from types import SimpleNamespace
+
+    g = torch.Generator().manual_seed(3 * m + d + f)
+    _, _, b_up, qa1, sa1, qw_up, sw_up = quantized_problem(g, m, d, f, 8)
+    _, _, b_dn, _, _, qw_dn, sw_dn = quantized_problem(g, m, f, d, 8)
+    _, _, _, qa2, sa2, _, _ = quantized_problem(g, m, d, f, 8)
+    lut = device_lut("tanh")
+    dev = lambda a: torch.from_numpy(a).cuda()   # noqa: E731
+    up = SimpleNamespace(packed_weight=dev(qw_up), weight_scale=dev(sw_up), bias=b_up.cuda(),
+                         out_features=f, in_features=d, _bias_mode=lambda: _lib.BIAS_ADD)
+    down = SimpleNamespace(packed_weight=dev(qw_dn), weight_scale=dev(sw_dn), bias=b_dn.cuda(),
+                           out_features=d, in_features=f, _bias_mode=lambda: _lib.BIAS_ADD)
+    inputs = [(dev(qa1), dev(sa1), randn_bf16(g, m, d).cuda()), (dev(qa2), dev(sa2), randn_bf16(g, m, d).cuda())]
+    got = [ops.dit_ffn(qa, sa, up, down, lut, res) for qa, sa, res in inputs]
+    for (qa, sa, res), out in zip(inputs, got):
+        h = ops.gemm(qa, sa, up.packed_weight, up.weight_scale, up.bias, 8, out_lut=lut, n_store=f)
+        qh, sh = ops.quant_rows(h, 8)
+        ref = ops.gemm(qh, sh, down.packed_weight, down.weight_scale, down.bias, 8, residual=res, n_store=d)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    assert not torch.equal(got[0], got[1])
+    assert_status_clean()
