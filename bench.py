@@ -10,15 +10,21 @@ from one CUDA graph.  Synthetic seeded inputs and random-init weights (no
 checkpoints or datasets exist here).  With N GPUs each rank runs its own
 robot(s) (independent instances, no collective: weak scaling); timing is
 CUDA events on the step's stream, max over ranks.  Each step streams about
-1.4 GB of packed weights, far larger than the 126 MB L2, so no L2 flush is
-needed between steps.
+3.1 GB of packed weights and activations from DRAM (the DiT's weights once
+per Euler step), far larger than the 126 MB L2, so no L2 flush is needed
+between steps.
 
 `--impl reference` times the reference's quantized-Linear arithmetic on the
 host cores instead: piR2 has no CPU implementation of this path (its kernels
 reject CPU tensors), so this is the CPU restatement in oracle/ (numpy
 quantize + exact int GEMM + dequant epilogue, torch CPU for norms and
-attention), run on a bounded sample (one VLM layer and a two-block DiT over
-the 4 Euler steps) and scaled to the full step by layer counts.
+attention), over full, unscaled control steps: the whole policy is built on
+the host, one untimed step runs, then steps are timed back to back until
+--steps are done or --cpu-budget-seconds have passed (at least one); the
+line reports the number of steps it actually timed.  The `cpu_baseline` of
+our own arm's line is a bounded sample instead (one VLM layer and a
+two-block DiT over the 4 Euler steps, scaled by layer counts), so the
+default run stays within minutes; its `sample` field says so.
 """
 
 import argparse
@@ -60,7 +66,10 @@ def parse():
         help="total robots sharded over the GPUs (batched config: B=64 -> 64/N per GPU, strong scaling)",
     )
     p.add_argument("--no-graph", action="store_true")
-    p.add_argument("--cpu-sample-seconds", type=float, default=20.0)
+    p.add_argument("--cpu-sample-seconds", type=float, default=20.0,
+                   help="host time of the CPU baseline sample in our arm's line")
+    p.add_argument("--cpu-budget-seconds", type=float, default=60.0,
+                   help="--impl reference: timed full CPU steps stop after this long (at least one)")
     p.add_argument(
         "--kernel",
         metavar="M,K,N",
@@ -211,20 +220,11 @@ def gemm_bytes(s):
     return wb + s["m"] * s["k"] * s["bits"] // 8 + 4 * s["m"] + 4 * s["npad"] + out + res
 
 
-TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemm_i8_step_w8a8_traffic.md")
-
-
-def measured_traffic(key):
-    """DRAM bytes per launch recorded by the committed ncu capture of this
-    step (profiles/gemm_i8_step_w8a8_traffic.md), or None."""
-    try:
-        with open(TRAFFIC_PROFILE) as f:
-            for line in f:
-                if line.startswith(key + ":"):
-                    return int(line.split(":", 1)[1])
-    except (OSError, ValueError):
-        pass
-    return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# small-M W8A8 GEMM, from one ncu capture of gemm_i8_kernel<8, 0> on the
+# DiT's M=17 shapes (the command and the per-shape figures are in the ncu
+# summary of that kernel under profiles/); None for the other precisions.
+SMALL_M_TRAFFIC_BYTES = {"w8a8": 7296690}
 
 
 def roofline(engine, hbm_peak, peak_kind, precision):
@@ -277,8 +277,8 @@ def roofline(engine, hbm_peak, peak_kind, precision):
         "unit": "GB/s",
         "frac": round(achieved / hbm_peak, 4),
         "peak_source": f"{peak_kind} hbm_gbs",
-        "traffic": measured_traffic("traffic_bytes_per_launch_small_m") if precision == "w8a8" else None,
-        "traffic_unit": "DRAM bytes per launch (ncu capture of this step, profiles/gemm_i8_step_w8a8_traffic.md)",
+        "traffic": SMALL_M_TRAFFIC_BYTES.get(precision),
+        "traffic_unit": "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, one-kernel capture)",
         "algorithmic_bytes_per_launch": round(small["bytes"] / max(small["n"], 1)),
         "launches": small["n"],
         "avg_launch_us": round(small["t"] * 1e3 / max(small["n"], 1), 2),
@@ -294,6 +294,19 @@ def roofline(engine, hbm_peak, peak_kind, precision):
                 "fp8": "nominal dense FP8 (no measured FP8 peak)",
             }.get(precision, "measured int8 kind::i8 issue-rate probe"),
         },
+    }
+
+
+def workload_config(args, world):
+    """The workload both arms report, identical between them: the per-GPU
+    share of the robots (one control step each) and how they are spread."""
+    return {
+        "workload": f"GR00T-shaped control step per GPU, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
+        "precision": args.precision,
+        "batch_per_gpu": args.batch,
+        "robots_total": args.batch * world,
+        "parallelism": f"independent robots, dp{world}, no collective",
+        "l2": "inputs larger than L2: each step streams ~3.1 GB of packed weights and activations (> 126 MB L2); no flush",
     }
 
 
@@ -347,29 +360,62 @@ def _cpu_oracle_sample(args, budget_s, cores, install_oracle_linears, harness):
     return full_ms, cores, sample
 
 
+def cpu_full_steps(args, warmup, steps, budget_s):
+    """Full, unscaled control steps of the reference's quantized-Linear
+    arithmetic on the host cores: the whole policy (16 VLM layers, 16 DiT
+    blocks, 4 Euler steps) with every Linear on the oracle, `warmup` untimed
+    steps, then timed steps until `steps` are done or `budget_s` has passed
+    (at least one).  Returns (ms_per_step, steps_timed, cores, seconds)."""
+    from threadpoolctl import threadpool_limits
+
+    from oracle.model import install_oracle_linears
+    from pir2_b200 import harness
+
+    cores = len(os.sched_getaffinity(0)) or 1
+    torch.set_num_threads(cores)
+    with threadpool_limits(limits=cores, user_api="blas"), torch.inference_mode():
+        policy = harness.build_policy("cpu")
+        install_oracle_linears(policy, args.precision)
+        inputs = harness.synthetic_inputs(args.batch, "cpu")
+        for _ in range(warmup):
+            policy(*inputs)
+        done, start = 0, time.perf_counter()
+        while done < max(steps, 1):
+            policy(*inputs)
+            done += 1
+            if time.perf_counter() - start >= budget_s:
+                break
+        elapsed = time.perf_counter() - start
+    return 1e3 * elapsed / done, done, cores, elapsed
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    ms, cores, sample = cpu_oracle_step(args, budget_s=max(2.0, args.cpu_sample_seconds / max(args.steps, 1)))
+    warmup = min(args.warmup, 1)
+    ms, done, cores, elapsed = cpu_full_steps(args, warmup, args.steps, args.cpu_budget_seconds)
+    sample = (
+        f"{done} full control step(s) timed back to back ({elapsed:.1f} s) after {warmup} untimed, batch "
+        f"{args.batch}: the whole policy with every Linear on the oracle's {args.precision.upper()} "
+        "arithmetic, torch CPU norms/attention; nothing scaled"
+    )
     line = {
         "metric": METRIC,
         "value": round(ms, 3),
         "unit": "ms",
         "impl": "reference",
         "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
+        "steps": done,
+        "warmup": warmup,
+        "requested_steps": args.steps,
+        "requested_warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": False,
-        "scaling": "weak",
+        "scaling": "weak" if args.robots is None else "strong",
         "vs_baseline": None,
         "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1", "fp8": "e4m3"}[args.precision],
         "data": "synthetic",
-        "config": {
-            "workload": f"GR00T-shaped control step, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
-            "precision": args.precision,
-            "batch_per_gpu": args.batch,
-        },
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -475,15 +521,8 @@ def run_ours(args, world, rank, local):
             "vs_baseline": None,
             "dtype": {"w8a8": "int8", "w4a4": "int4", "fp4": "e2m1", "fp8": "e4m3"}[args.precision],
             "data": "synthetic",
-            "config": {
-                "workload": f"GR00T-shaped control step per GPU, {args.batch} robot(s): VLM prefill 544 tokens x 16 layers + DiT 16 blocks x 4 Euler steps",
-                "precision": args.precision,
-                "batch_per_gpu": args.batch,
-                "robots_total": args.batch * world,
-                "parallelism": f"independent robots, dp{world}, no collective",
-                "graph": not args.no_graph,
-                "l2": "each step streams ~1.4 GB of packed weights (> 126 MB L2); no flush",
-            },
+            "config": workload_config(args, world),
+            "graph": not args.no_graph,
             "e2e": {
                 "value": round(e2e_ms, 4),
                 "unit": "ms",
