@@ -25,6 +25,9 @@ __all__ = [
     "gemm_epilogue",
     "linear_w8a8",
     "rms_norm_pack",
+    "torch_row_mean_config",
+    "torch_row_mean",
+    "rms_norm_tail_pack",
     "layer_norm_pack",
     "modulation_pack",
     "residual_norm_modulation_pack",
@@ -244,6 +247,68 @@ def rms_norm_values(x_bits, gamma_bits, eps):
     inv = _rsqrt((var + F32(eps)).astype(F32))
     n = bf16_round((x * inv[:, None]).astype(F32))
     return bf16_round((n * bf16_bits_to_f32(gamma_bits)[None, :]).astype(F32))
+
+
+def torch_row_mean_config(rows, k):
+    """Threads per row (bw) and the fp32 mean factor of torch's CUDA row mean
+    over a contiguous fp32 [rows, k] tensor (ATen/native/cuda/Reduce.cuh,
+    setReduceConfig with 4-float input vectors), the reduction the reference's
+    B200 RMS statistics use (rms_statistics.py:171-190: squares, then
+    `squared.mean(-1)`).  None when torch would split a row across warps."""
+
+    def last_pow2(n):
+        return 1 << (int(n).bit_length() - 1)
+
+    if k < 128 or k % 4 or rows < 1:
+        return None
+    dim0, dim1 = k // 4, rows
+    d0 = last_pow2(dim0) if dim0 < 512 else 512
+    d1 = last_pow2(dim1) if dim1 < 512 else 512
+    bw = min(d0, 32)
+    bh = min(d1, 512 // bw)
+    bw = min(d0, 512 // bh)
+    if -(-k // bw) >= min(bh * 16, 256):
+        return None
+    return bw, F32(F32(rows) / F32(rows * k))
+
+
+def torch_row_mean(sq, bw, factor):
+    """Row means of fp32 [rows, k] in the order of torch's CUDA reduction for
+    that launch shape: virtual thread t of bw adds the 4-float vectors
+    t, t + bw, ... into four accumulators (element i of each vector into
+    accumulator i), combines them as ((a0 + a1) + a2) + a3, and the bw
+    partials are added pairwise with halving offsets (bw/2, ..., 1); the
+    mean is that sum times `factor`."""
+    sq = np.asarray(sq, F32)
+    rows, k = sq.shape
+    vec = sq.reshape(rows, k // 4, 4)
+    nvec = k // 4
+    part = np.zeros((rows, bw), F32)
+    for t in range(bw):
+        acc = np.zeros((rows, 4), F32)
+        for idx in range(t, nvec, bw):
+            acc = (acc + vec[:, idx, :]).astype(F32)
+        part[:, t] = (((acc[:, 0] + acc[:, 1]).astype(F32) + acc[:, 2]).astype(F32) + acc[:, 3]).astype(F32)
+    width = bw
+    while width > 1:
+        half = width // 2
+        part[:, :half] = (part[:, :half] + part[:, half:width]).astype(F32)
+        width = half
+    return (part[:, 0] * F32(factor)).astype(F32)
+
+
+def rms_norm_tail_values(x_bits, gamma_bits, var, inv):
+    """`_rms_tail_pack` (producers.py:19-53) given the row variance and its
+    inverse root rsqrt(var + eps) as the device computes them:
+    n = bf16(x * inv); v = bf16(n * gamma)."""
+    x = bf16_bits_to_f32(x_bits)
+    inv = np.asarray(inv, F32)
+    n = bf16_round((x * inv[:, None]).astype(F32))
+    return bf16_round((n * bf16_bits_to_f32(gamma_bits)[None, :]).astype(F32))
+
+
+def rms_norm_tail_pack(x_bits, gamma_bits, var, inv, bits):
+    return _pack_values(rms_norm_tail_values(x_bits, gamma_bits, var, inv), bits)
 
 
 def layer_norm_values(x_f32, eps):

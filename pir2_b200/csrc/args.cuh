@@ -37,6 +37,11 @@ struct NormArgs {
   int k;
   int kpad;
   float eps;
+  // RMSNorm statistics in torch's row-mean order (integer outputs): the
+  // threads per row torch's reduction uses for this [rows, k] shape, and
+  // its fp32 factor rows / (rows * k).
+  int rms_bw;
+  float rms_factor;
 };
 
 struct GemmArgs {

@@ -175,6 +175,42 @@ static int make_out_map(CUtensorMap *map, const void *base, uint64_t cols,
   return PIR2B_OK;
 }
 
+// ------------------------------------------------------------------ RMS order
+// The launch shape torch's fp32 row mean (x.float() ** 2).mean(-1) takes for
+// a contiguous [rows, k] input (ATen Reduce.cuh, setReduceConfig): input
+// vectorised by 4 floats (k >= 128), block width bw and height bh from
+// 512 threads, one warp-row per output unless the per-thread value count
+// reaches min(16 bh, 256) (then torch splits a row across warps, which this
+// kernel does not reproduce).  Also returns torch's mean factor, the fp32
+// quotient rows / (rows * k).
+static int64_t last_pow2(int64_t n) {
+  n |= n >> 1;
+  n |= n >> 2;
+  n |= n >> 4;
+  n |= n >> 8;
+  n |= n >> 16;
+  n |= n >> 32;
+  return std::max<int64_t>(1, n - (n >> 1));
+}
+
+static bool torch_row_mean_config(int64_t rows, int64_t k, int *bw_out, float *factor) {
+  if (k < 128 || k % 4 != 0 || rows < 1)
+    return false;
+  const int64_t max_threads = 512;
+  const int64_t dim0 = k / 4, dim1 = rows;
+  const int64_t dim0_pow2 = dim0 < max_threads ? last_pow2(dim0) : max_threads;
+  const int64_t dim1_pow2 = dim1 < max_threads ? last_pow2(dim1) : max_threads;
+  int64_t bw = std::min<int64_t>(dim0_pow2, 32);
+  const int64_t bh = std::min<int64_t>(dim1_pow2, max_threads / bw);
+  bw = std::min<int64_t>(dim0_pow2, max_threads / bh);
+  const int64_t values_per_thread = (k + bw - 1) / bw;
+  if (values_per_thread >= std::min<int64_t>(bh * 16, 256))
+    return false;
+  *bw_out = int(bw);
+  *factor = float(rows) / float(rows * k);
+  return true;
+}
+
 // ------------------------------------------------------------------ GEMM plan
 struct GemmPlan {
   int bn, mtiles, splits, stages;
@@ -667,10 +703,21 @@ int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
     return fail(PIR2B_EALIGN, "scale/smoothing pointer alignment not met");
   if (res && norm_kind == PIR2B_NORM_NONE)
     return fail(PIR2B_EINVAL, "a residual input needs a norm");
+  int rms_bw = 0;
+  float rms_factor = 0.f;
+  if (norm_kind == PIR2B_NORM_RMS && out_format != PIR2B_OUT_NVFP4) {
+    if (!torch_row_mean_config(rows, k, &rms_bw, &rms_factor))
+      return fail(PIR2B_EINVAL,
+                  "RMSNorm pack: rows=%lld k=%lld is outside the row-mean order this kernel "
+                  "reproduces (k >= 128 and fewer than 16 values per thread-row step)",
+                  (long long)rows, (long long)k);
+  }
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
   NormArgs a;
+  a.rms_bw = rms_bw;
+  a.rms_factor = rms_factor;
   a.x = static_cast<const __nv_bfloat16 *>(x);
   a.y_in = static_cast<const __nv_bfloat16 *>(y_in);
   a.gate = static_cast<const __nv_bfloat16 *>(gate);

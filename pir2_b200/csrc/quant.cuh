@@ -409,16 +409,74 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
       v[j][i] = (c0 + i < a.k) ? __bfloat162float(xv[i]) : 0.f;
   }
   const float kf = float(a.k);
-  if (kNorm == 1) {
+  if constexpr (kNorm == 1) {
     // RMSNorm: var = mean(x^2); n = bf16(x * rsqrt(var + eps)); v = bf16(n*g)
-    float ss = 0.f;
+    float var;
+    if constexpr (kOut != 16) {
+      // The integer producer's variance is the reference's B200 path
+      // (producers.py:19-53 via rms_statistics.py:171-190): fp32 squares,
+      // then torch's fp32 row mean, whose order this reproduces (ATen
+      // Reduce.cuh, vectorised input of 4 floats): virtual thread t of
+      // rms_bw sums the vectors t, t + bw, t + 2 bw, ... in four
+      // accumulators (one per vector element), combines them as
+      // ((a0 + a1) + a2) + a3, and the bw partials meet in a pairwise tree
+      // with halving offsets (shared memory down to 32, then the warp);
+      // the mean is that sum times rows / (rows * k).
+      __shared__ float4 sq4[2048];   // k <= 8192
+      __shared__ float part[512];
 #pragma unroll
-    for (int j = 0; j < kCpt; ++j)
+      for (int j = 0; j < kCpt; ++j) {
+        const int chunk = threadIdx.x + j * blockDim.x;
+        if (chunk < nchunks && chunk * 8 < a.k) {
+          const float *e = v[j];
+          sq4[2 * chunk] = make_float4(__fmul_rn(e[0], e[0]), __fmul_rn(e[1], e[1]),
+                                       __fmul_rn(e[2], e[2]), __fmul_rn(e[3], e[3]));
+          sq4[2 * chunk + 1] = make_float4(__fmul_rn(e[4], e[4]), __fmul_rn(e[5], e[5]),
+                                           __fmul_rn(e[6], e[6]), __fmul_rn(e[7], e[7]));
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const int bw = a.rms_bw;
+        const int nvec = a.k >> 2;
+        for (int t = lane; t < bw; t += 32) {
+          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+          for (int idx = t; idx < nvec; idx += bw) {
+            const float4 q4 = sq4[idx];
+            a0 = __fadd_rn(a0, q4.x);
+            a1 = __fadd_rn(a1, q4.y);
+            a2 = __fadd_rn(a2, q4.z);
+            a3 = __fadd_rn(a3, q4.w);
+          }
+          part[t] = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+        }
+        __syncwarp();
+        for (int off = bw >> 1; off >= 32; off >>= 1) {
+          for (int t = lane; t < off; t += 32)
+            part[t] = __fadd_rn(part[t], part[t + off]);
+          __syncwarp();
+        }
+        float s = lane < bw ? part[lane] : 0.f;
+        for (int off = min(bw, 32) >> 1; off > 0; off >>= 1)
+          s = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, off));
+        if (lane == 0)
+          red[0] = __fmul_rn(s, a.rms_factor);
+      }
+      __syncthreads();
+      var = red[0];
+      __syncthreads();   // red is reused by the row maximum below
+    } else {
+      float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        ss = __fadd_rn(ss, __fmul_rn(v[j][i], v[j][i]));
-    ss = block_sum(ss, red);
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, kf), a.eps));
+      for (int j = 0; j < kCpt; ++j)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          ss = __fadd_rn(ss, __fmul_rn(v[j][i], v[j][i]));
+      ss = block_sum(ss, red);
+      var = __fdiv_rn(ss, kf);
+    }
+    const float inv = rsqrtf(__fadd_rn(var, a.eps));
 #pragma unroll
     for (int j = 0; j < kCpt; ++j) {
       const int chunk = threadIdx.x + j * blockDim.x;
@@ -432,7 +490,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
                                  : 0.f;
       }
     }
-  } else if (kNorm == 2) {
+  } else if constexpr (kNorm == 2) {
     // Non-affine LayerNorm: mean, centred variance, n = bf16(c * rsqrt(var+eps))
     float sum = 0.f;
 #pragma unroll

@@ -200,16 +200,47 @@ def codes(q, bits):
 
 
 @pytest.mark.parametrize("bits", [8, 4])
-def test_rmsnorm_producer_within_one_code(bits):
-    g = torch.Generator().manual_seed(21)
-    x = randn_bf16(g, 544, 2048, outliers=True)
+@pytest.mark.parametrize("rows", [544, 1088, 1, 5, 17])
+def test_rmsnorm_producer_bitwise_vs_torch_row_mean(bits, rows):
+    """The integer RMSNorm pack is bit-exact against the reference's B200
+    path: fp32 squares, torch's row mean on the device (the variance bytes
+    of rms_statistics.py:171-190), rsqrt(var + eps) on the device, then the
+    `_rms_tail_pack` arithmetic (producers.py:19-53).  The oracle's
+    restatement of torch's reduction order is pinned to torch here too."""
+    g = torch.Generator().manual_seed(21 + rows)
+    x = randn_bf16(g, rows, 2048, outliers=True)
     gamma = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
-    q, s, _ = ops.norm_quant_rows(x.cuda(), bits, norm=_lib.NORM_RMS, eps=1e-6, gamma=gamma.cuda())
-    rq, rs = oracle.rms_norm_pack(bits_of(x), bits_of(gamma), 1e-6, bits)
-    assert np.allclose(s.cpu().numpy(), rs, rtol=2 ** -7, atol=0)
-    assert np.abs(codes(q, bits) - codes(rq, bits)).max() <= 1
-    # Most codes are identical: the difference is only reduction order.
-    assert np.mean(codes(q, bits) == codes(rq, bits)) > 0.99
+    xd = x.cuda()
+    sq = xd.float() * xd.float()
+    var = sq.mean(-1)
+    inv = torch.rsqrt(var + 1e-6)
+    bw, factor = oracle.torch_row_mean_config(rows, 2048)
+    assert np.array_equal(oracle.torch_row_mean(sq.cpu().numpy(), bw, factor), var.cpu().numpy())
+    q, s, _ = ops.norm_quant_rows(xd, bits, norm=_lib.NORM_RMS, eps=1e-6, gamma=gamma.cuda())
+    rq, rs = oracle.rms_norm_tail_pack(bits_of(x), bits_of(gamma), var.cpu().numpy(), inv.cpu().numpy(), bits)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(q.cpu().numpy(), rq)
+
+
+def test_rmsnorm_residual_producer_bitwise():
+    """The decoder's fused residual + RMSNorm pack: r = bf16(x + y) is written
+    out and packed exactly as RMSNorm of r."""
+    g = torch.Generator().manual_seed(5)
+    x, y = randn_bf16(g, 544, 2048), randn_bf16(g, 544, 2048, outliers=True)
+    gamma = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    q, s, r = ops.norm_quant_rows(x.cuda(), 8, norm=_lib.NORM_RMS, eps=1e-6, gamma=gamma.cuda(), y=y.cuda())
+    rsum = (x.cuda().float() + y.cuda().float()).to(torch.bfloat16)
+    assert torch.equal(r, rsum)
+    var = (rsum.float() * rsum.float()).mean(-1)
+    inv = torch.rsqrt(var + 1e-6)
+    rq, rs = oracle.rms_norm_tail_pack(bits_of(rsum.cpu()), bits_of(gamma), var.cpu().numpy(), inv.cpu().numpy(), 8)
+    assert np.array_equal(s.cpu().numpy(), rs) and np.array_equal(q.cpu().numpy(), rq)
+
+
+def test_rmsnorm_pack_refuses_rows_outside_the_reproduced_order():
+    x = torch.zeros(32, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="row-mean order"):
+        ops.norm_quant_rows(x, 8, norm=_lib.NORM_RMS, eps=1e-6, gamma=torch.ones(64, dtype=torch.bfloat16, device="cuda"))
 
 
 @pytest.mark.parametrize("bits", [8, 4])
