@@ -49,7 +49,9 @@ import triton  # noqa: E402
 import triton.language as tl  # noqa: E402
 from triton.runtime import interpreter as _interp  # noqa: E402
 
-REFERENCE = os.environ.get("PIR2_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("PIR2_REFERENCE")
+if not REFERENCE:
+    raise SystemExit("set PIR2_REFERENCE to a checkout of the piR2 repository")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden.npz")
 
 _original_convert = _interp._convert_float

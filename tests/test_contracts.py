@@ -20,7 +20,9 @@ from pir2_b200.session import GrootOptimizations, selected_component
 from pir2_b200.tactics import apply_tactics, read_shape_tactics
 
 ROOT = Path(__file__).resolve().parents[1]
-REFERENCE = Path("/root/reference")
+# A checkout of the piR2 repository, for the test that loads its shipped
+# configuration presets (skipped when the variable is unset).
+REFERENCE = Path(os.environ["PIR2_REFERENCE"]) if os.environ.get("PIR2_REFERENCE") else None
 
 
 # ----------------------------------------------------------------- config
@@ -124,7 +126,7 @@ def test_shape_tactics_reject_duplicates_and_unbound_profiles(tmp_path):
     assert read_shape_tactics(path, backend_evidence=evidence) == {(8, 41, 130, 64, True): 2}
 
 
-@pytest.mark.skipif(not REFERENCE.exists(), reason="reference configs not mounted")
+@pytest.mark.skipif(REFERENCE is None or not REFERENCE.exists(), reason="PIR2_REFERENCE not set")
 def test_reference_presets_load_through_the_public_tactic_interface():
     preset = REFERENCE / "configs/quantization/groot-libero10-ada"
     coverage = json.loads((preset / "coverage.json").read_text())["linears"]
