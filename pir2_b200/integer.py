@@ -331,6 +331,11 @@ class IntegerProjectionGroup(torch.nn.Module):
         self._input = self._output = None
         self._remaining = set()
 
+    def forget(self):
+        """Drops the cached group output (the next project() recomputes)."""
+        self._input = self._output = None
+        self._remaining = set()
+
     def project(self, x, index):
         if self._input is not x or index not in self._remaining:
             self._input = x
