@@ -332,6 +332,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   // griddepcontrol.wait, which waits for this grid to complete.
   pdl_launch_dependents();
 
+  // Split-K epilogue constants of an epilogue thread (token tiles of at most
+  // 64 rows): the scales and bias of its four channels of the rank's slice
+  // and the residual values of the tokens it writes.  They are loaded while
+  // the main loop runs, so no load is outstanding at the cluster barrier.
+  constexpr int kPreTok = 8;   // 64 / (smallest token stride, 8)
+  float ep_sw[4] = {0.f, 0.f, 0.f, 0.f}, ep_b[4] = {0.f, 0.f, 0.f, 0.f};
+  __nv_bfloat162 ep_res[kPreTok][2];   // bf16 pairs: channels (0, 1), (2, 3)
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
@@ -437,6 +445,33 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Token scales of this tile, once, while the main loop runs.
       for (int j = et; j < bn; j += 128)
         s_sa[j] = (m0 + j < args.m) ? __ldg(args.sa + m0 + j) : 0.f;
+    }
+    if (!kWide && args.splits > 1) {
+      const int slice = kTileN / args.splits;
+      const int tpt = slice / 4;
+      const int cc = n0 + int(cluster_ctarank()) * slice + (et % tpt) * 4;
+      const int first = et / tpt, tstride = 128 / tpt;
+      const int valid_m = min(bn, args.m - m0);
+      const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
+      __nv_bfloat16 res[kPreTok][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bool in_range = cc + i < args.n_store;
+        ep_sw[i] = in_range ? __ldg(args.sw + cc + i) : 0.f;
+        ep_b[i] = (args.bias_mode == 2 && in_range) ? __bfloat162float(args.bias[cc + i]) : 0.f;
+#pragma unroll
+        for (int u = 0; u < kPreTok; ++u) {
+          const int j = first + u * tstride;
+          res[u][i] = (args.residual != nullptr && in_range && j < valid_m)
+                          ? args.residual[int64_t(m0 + j) * args.ldr + cc + i]
+                          : zero;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kPreTok; ++u) {
+        ep_res[u][0] = __halves2bfloat162(res[u][0], res[u][1]);
+        ep_res[u][1] = __halves2bfloat162(res[u][2], res[u][3]);
+      }
     }
     named_barrier(1, 128);
     if (kBits == 4) {
@@ -604,8 +639,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         in_range[i] = cc + i < args.n_store;
-        sw[i] = in_range[i] ? __ldg(args.sw + cc + i) : 0.f;
-        b[i] = (args.bias_mode == 2 && in_range[i]) ? __bfloat162float(args.bias[cc + i]) : 0.f;
+        if (kWide) {
+          sw[i] = in_range[i] ? __ldg(args.sw + cc + i) : 0.f;
+          b[i] = (args.bias_mode == 2 && in_range[i]) ? __bfloat162float(args.bias[cc + i]) : 0.f;
+        } else {
+          sw[i] = ep_sw[i];
+          b[i] = ep_b[i];
+        }
       }
       const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
       const uint32_t part_addr = smem_u32(smem) + uint32_t(cq * 4);
@@ -615,7 +655,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         peer_base[p] = p < splits ? map_peer(part_addr, uint32_t(p)) : 0u;
       // Staging tile [bn][slice] bf16 after the partial sums.
       __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(smem + size_t(bn) * kTileN * 4);
-      const bool tma = args.tma_store != 0;
+      // Small token tiles write their rows directly (8 bytes per thread and
+      // token; nothing to wait for before exit) unless the per-16-channel
+      // maxima are wanted, which are taken from the staged tile.
+      const bool tma = args.tma_store != 0 && (kWide || args.max_out != nullptr);
+      const bool vec8 = args.ldo % 4 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 7) == 0;
       const bool with_res = args.residual != nullptr;
       const int jend = tma ? bn : valid_m;
       const int first = et / tpt;
@@ -632,6 +676,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           __nv_bfloat162 *d = reinterpret_cast<__nv_bfloat162 *>(stage + j * slice + cl);
           d[0] = __halves2bfloat162(o[0], o[1]);
           d[1] = __halves2bfloat162(o[2], o[3]);
+        } else if (vec8 && in_range[3]) {
+          const __nv_bfloat162 lo = __halves2bfloat162(o[0], o[1]), hi = __halves2bfloat162(o[2], o[3]);
+          *reinterpret_cast<uint2 *>(args.out + int64_t(m0 + j) * args.ldo + cc) =
+              make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
         } else {
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -641,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       // Sums the peers' partials of token j (and loads its residual values
       // alongside the distributed-shared-memory loads).
-      auto gather = [&](int j, int (&acc)[4], float (&res)[4]) {
+      auto gather = [&](int j, int (&acc)[4], float (&res)[4], bool load_res) {
         const uint32_t off = uint32_t(j * kTileN * 4);
         int4 v[8];
 #pragma unroll
@@ -651,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           res[i] = 0.f;
-          if (with_res && in_range[i] && j < valid_m)
+          if (load_res && with_res && in_range[i] && j < valid_m)
             res[i] = __bfloat162float(args.residual[int64_t(m0 + j) * args.ldr + cc + i]);
         }
         acc[0] = acc[1] = acc[2] = acc[3] = 0;
@@ -745,11 +793,28 @@ __global__ void __launch_bounds__(kThreads, 2)
         rounds(std::integral_constant<int, 2>());
       } else if (kWide && splits == 4) {
         rounds(std::integral_constant<int, 4>());
+      } else if (!kWide) {
+        // At most kPreTok tokens per thread; residual values preloaded.
+#pragma unroll
+        for (int u = 0; u < kPreTok; ++u) {
+          const int j = first + u * tstride;
+          if (j < jend) {
+            int acc[4];
+            float res[4];
+            gather(j, acc, res, false);
+            const float2 r01 = __bfloat1622float2(ep_res[u][0]), r23 = __bfloat1622float2(ep_res[u][1]);
+            res[0] = r01.x;
+            res[1] = r01.y;
+            res[2] = r23.x;
+            res[3] = r23.y;
+            finish(j, acc, res);
+          }
+        }
       } else {
         for (int j = first; j < jend; j += tstride) {
           int acc[4];
           float res[4];
-          gather(j, acc, res);
+          gather(j, acc, res, true);
           finish(j, acc, res);
         }
       }

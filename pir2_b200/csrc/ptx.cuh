@@ -284,9 +284,13 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src,
       : "memory");
 }
 
+// Commits this thread's bulk stores and waits until they have finished
+// reading shared memory, so the staging tile may be reused and the CTA may
+// exit.  The global writes complete asynchronously; a grid that waits for
+// this one (griddepcontrol.wait, stream order) sees them.
 __device__ __forceinline__ void tma_store_commit_and_wait() {
   asm volatile("cp.async.bulk.commit_group;\n\t"
-               "cp.async.bulk.wait_group 0;" ::
+               "cp.async.bulk.wait_group.read 0;" ::
                    : "memory");
 }
 

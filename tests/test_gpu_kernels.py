@@ -643,3 +643,30 @@ def test_dit_ffn_back_to_back_calls_on_one_workspace(m, d, f):
         assert torch.equal(out, ref)
     assert not torch.equal(got[0], got[1])
     assert_status_clean()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_quant_codes_at_half_integer_boundaries(bits):
+    """Rows whose values sit exactly on the rounding boundaries of the codes
+    (v / s within an ulp of k + 1/2, ties to even): the packs multiply by the
+    row's reciprocal and fall back to the IEEE division near a boundary, and
+    must still equal rint(RN(v / s)) bit for bit."""
+    limit = 127 if bits == 8 else 7
+    halves = np.arange(-limit, limit, dtype=np.float32) + np.float32(0.5)
+    rows = []
+    for scale in (1.0, 0.5, 3.0, 2.0 ** -7, 1.5):
+        row = np.concatenate([halves, [np.float32(limit)]]) * np.float32(scale)
+        rows.append(np.resize(row, 1536))
+    # Neighbours one bf16 step either side of each boundary.
+    x = torch.from_numpy(np.stack(rows).astype(np.float32)).to(torch.bfloat16)
+    up = torch.from_numpy(np.nextafter(np.stack(rows), np.float32(np.inf)).astype(np.float32)).to(torch.bfloat16)
+    x = torch.cat([x, up, -x])
+    q, s = ops.quant_rows(x.cuda(), bits)
+    rq, rs = oracle.quant_rows(bits_of(x), bits)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(q.cpu().numpy(), rq)
+    # The fused producers share the quantizer (modulation pack, zero shift).
+    zero = torch.zeros(x.shape[0], 1536, dtype=torch.bfloat16)
+    q2, s2, _ = ops.norm_quant_rows(x.cuda(), bits, scale=zero.cuda(), shift=zero.cuda(), tokens=1)
+    rq2, rs2 = oracle.modulation_pack(bits_of(x), bits_of(zero), bits_of(zero), 1, bits)
+    assert np.array_equal(q2.cpu().numpy(), rq2) and np.array_equal(s2.cpu().numpy(), rs2)
