@@ -65,6 +65,12 @@ def parse():
         default=None,
         help="total robots sharded over the GPUs (batched config: B=64 -> 64/N per GPU, strong scaling)",
     )
+    p.add_argument(
+        "--batched-robots",
+        type=int,
+        default=64,
+        help="robots of the batched record (split over the GPUs, strong scaling); 0 skips it",
+    )
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--cpu-sample-seconds", type=float, default=20.0,
                    help="host time of the CPU baseline sample in our arm's line")
@@ -506,6 +512,8 @@ def run_ours(args, world, rank, local):
     launches = count_launches(engine)
     phases = phase_breakdown(engine)
     engine.release()
+    coexec = coexec_b1_record(engine.policy, args, world, local)
+    batched = batched_record(engine.policy, args, world, local) if args.batched_robots else None
     session.close()
     if rank == 0:
         line = {
@@ -531,12 +539,97 @@ def run_ours(args, world, rank, local):
             },
             "gpu_launches": launches,
             "phases": phases,
+            "coexec_b1": coexec,
+            "batched": batched,
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clock_summary,
             "device_status": status,
         }
         print(json.dumps(line), flush=True)
+
+
+def _timed_steps(step, stream, steps, warmup, world):
+    """Device time per step of `step()` replayed `steps` times on `stream`
+    after `warmup` untimed calls, bracketed by a barrier and a device
+    synchronize on both sides; the max over ranks."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+
+def batched_record(policy, args, world, local):
+    """BASELINE's batched configuration: `--batched-robots` independent robots
+    split evenly over the GPUs (strong scaling, no collective).  Each GPU
+    times its share two ways: the serial control step (VLM prefill then the
+    4-step DiT, one graph) and the co-executed step (DiT on the previous
+    features while the VLM prefills the next observation on a second stream,
+    as piR2's S1/S2 run).  Max over ranks; throughput is whole-job robot
+    steps per second."""
+    from pir2_b200 import harness
+    from pir2_b200.engine import CoExecutionStep, ControlStep
+
+    robots = args.batched_robots
+    if robots % world:
+        raise SystemExit(f"--batched-robots {robots} does not split over {world} GPUs")
+    share = robots // world
+    device = torch.device("cuda", local)
+    steps, warmup = min(args.steps, 20), min(max(args.warmup, 3), 5)
+    inputs = harness.synthetic_inputs(share, device, seed=3)
+    serial = ControlStep(policy, share, device=device)
+    serial.load(inputs)
+    serial.capture()
+    serial_ms = _timed_steps(serial.replay, serial.stream, steps, warmup, world)
+    serial.release()
+    del serial
+    coexec = CoExecutionStep(policy, share, device=device)
+    coexec.prime(inputs)
+    coexec.capture()
+    coexec_ms = _timed_steps(coexec.replay, coexec.stream, steps, warmup, world)
+    coexec.release()
+    del coexec
+    torch.cuda.empty_cache()
+    return {
+        "robots_total": robots,
+        "robots_per_gpu": share,
+        "n_gpus": world,
+        "scaling": "strong",
+        "steps": steps,
+        "warmup": warmup,
+        "serial_ms_per_step": round(serial_ms, 4),
+        "coexec_ms_per_step": round(coexec_ms, 4),
+        "robot_steps_per_s": round(robots / (coexec_ms * 1e-3), 1),
+        "robot_steps_per_s_serial": round(robots / (serial_ms * 1e-3), 1),
+        "coexec": "VLM prefill of observation k on a second stream while the 4-step DiT acts on observation k-1's features",
+        "note": "each GPU holds the full packed weights; no collective; time is the max over ranks",
+    }
+
+
+def coexec_b1_record(policy, args, world, local):
+    """The B=1 control loop with VLM and DiT co-executed (S1/S2): per-step
+    device time, max over ranks, next to the serial headline."""
+    from pir2_b200 import harness
+    from pir2_b200.engine import CoExecutionStep
+
+    device = torch.device("cuda", local)
+    steps, warmup = min(args.steps, 50), min(max(args.warmup, 3), 5)
+    engine = CoExecutionStep(policy, args.batch, device=device)
+    engine.prime(harness.synthetic_inputs(args.batch, device))
+    engine.capture()
+    ms = _timed_steps(engine.replay, engine.stream, steps, warmup, world)
+    engine.release()
+    return {"ms_per_step": round(ms, 4), "steps": steps, "batch_per_gpu": args.batch,
+            "what": "DiT on the previous features while the VLM prefills the next observation on a second stream"}
 
 
 def phase_breakdown(engine, reps=50):

@@ -356,7 +356,9 @@ class ActionHead(nn.Module):
     def velocity(self, state_tokens, actions, features, t):
         x = torch.cat((state_tokens, self.action_encoder(actions)), dim=1) + self.position_embedding
         y = self.model(x, features, t)
-        return self.action_decoder(y[:, 1:])
+        # Decode the whole sequence, then keep the action tokens (as GR00T
+        # slices the decoder's output), so the decoder reads whole rows.
+        return self.action_decoder(y)[:, 1:]
 
     def get_action(self, features, state, noise):
         """4-step Euler integration of the flow from N(0, 1) actions."""
