@@ -82,6 +82,8 @@ def parse():
         help="time one quantized GEMM shape alone (for kernel profiling), not the step",
     )
     p.add_argument("--kernel-weights-mb", type=float, default=600.0, help="rotating weight copies for --kernel")
+    p.add_argument("--sweep", action="store_true",
+                   help="BASELINE configs 2/3: time every (precision, M, K, N) GEMM point against its roofline")
     p.add_argument("--kernel-residual", action="store_true", help="--kernel with the bf16 residual epilogue")
     return p.parse_args()
 
@@ -705,6 +707,108 @@ def count_launches(engine):
     return sum(counts.values())
 
 
+SWEEP_M = (1, 16, 64, 256, 1024)
+SWEEP_SHAPES = ((2048, 4096), (2048, 2048), (2048, 12288), (6144, 2048))
+
+
+def _time_graph_launches(launch, count, warmup):
+    """Median over 5 replays of a CUDA graph of `count` launches, in us per
+    launch."""
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(max(warmup, 1)):
+            launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(count):
+            launch(i)
+    for _ in range(max(warmup, 1)):
+        graph.replay()
+    torch.cuda.synchronize()
+    times = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(5):
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3 / count)
+    del graph
+    return sorted(times)[2]
+
+
+def sweep_point(precision, m, k, n, weights_mb, warmup):
+    """One (precision, M, K, N) point of BASELINE configs 2 and 3: the GEMM
+    alone (activation pack excluded), back to back in a CUDA graph over
+    rotating weight copies totalling ~weights_mb so each launch streams its
+    weights from DRAM.  Returns the time and both rooflines: algorithmic
+    bytes (weights, packed activations, scales, bf16 output) over the
+    measured HBM copy bandwidth, and 2MNK over the tensor peak; `bound` is
+    the one with the longer ideal time."""
+    from pir2_b200 import ops
+
+    hbm, _ = peaks()
+    g = torch.Generator(device="cuda").manual_seed(m + k + n)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    if precision == "nvfp4":
+        wbytes = n * k // 2 + n * k // 16
+        copies = max(1, min(64, int(weights_mb * 1e6 // wbytes)))
+        ws = [ops.pack_nvfp4((torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16))
+              for _ in range(copies)]
+        pa, sa = ops.pack_nvfp4(torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16))
+        launch = lambda i: ops.gemm_nvfp4(pa, sa, ws[i % copies][0], ws[i % copies][1], n=n, out=out)  # noqa: E731
+        algo = wbytes + m * k // 2 + m * k // 16 + 2 * m * n
+        peak_tops = FP4_NOMINAL_TOPS
+    else:
+        bits = 8 if precision == "w8a8" else 4
+        kp, npd = ops.kpad(k), ops.npad(n)
+        cols = kp if bits == 8 else kp // 2
+        dtype = torch.int8 if bits == 8 else torch.uint8
+        lo, hi = (-127, 128) if bits == 8 else (0, 256)
+        wbytes = npd * cols
+        copies = max(1, min(64, int(weights_mb * 1e6 // wbytes)))
+        ws = [torch.randint(lo, hi, (npd, cols), device="cuda", dtype=dtype, generator=g) for _ in range(copies)]
+        qa = torch.randint(lo, hi, (m, cols), device="cuda", dtype=dtype, generator=g)
+        sa = torch.rand(m, device="cuda", generator=g)
+        sw = torch.rand(npd, device="cuda", generator=g)
+        launch = lambda i: ops.gemm(qa, sa, ws[i % copies], sw, None, bits, n_store=n, out=out)  # noqa: E731
+        algo = wbytes + m * cols + 4 * m + 4 * npd + 2 * m * n
+        peak_tops = INT8_PEAK_TOPS
+    us = _time_graph_launches(launch, max(copies, 20), warmup)
+    ops_ = 2.0 * m * n * k
+    gbs = algo / us / 1e3
+    tops = ops_ / us / 1e6
+    bound = "hbm" if algo / (hbm * 1e3) >= ops_ / (peak_tops * 1e6) else "tensor"
+    return {
+        "precision": precision, "m": m, "k": k, "n": n, "us": round(us, 3),
+        "GBs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+        "TOPS": round(tops, 1), "tensor_frac": round(tops / peak_tops, 4),
+        "bound": bound, "frac": round(gbs / hbm if bound == "hbm" else tops / peak_tops, 4),
+    }
+
+
+def run_sweep(args):
+    """BASELINE configs 2/3: M x (K, N) for W8A8, W4A4 and NVFP4, one JSON
+    line per point plus a summary line."""
+    rows = []
+    for precision in ("w8a8", "w4a4", "nvfp4"):
+        for k, n in SWEEP_SHAPES:
+            for m in SWEEP_M:
+                row = sweep_point(precision, m, k, n, args.kernel_weights_mb, args.warmup)
+                rows.append(row)
+                print(json.dumps(row), flush=True)
+    hbm, kind = peaks()
+    print(json.dumps({
+        "sweep": "BASELINE configs 2/3 (GEMM alone, back to back, weights streamed from DRAM)",
+        "points": len(rows), "hbm_peak_gbs": hbm, "hbm_peak_kind": kind,
+        "int8_peak_tops": INT8_PEAK_TOPS, "fp4_peak_tops": FP4_NOMINAL_TOPS,
+        "small_m_hbm_frac_median": sorted(r["hbm_frac"] for r in rows if r["bound"] == "hbm")[
+            len([r for r in rows if r["bound"] == "hbm"]) // 2] if any(r["bound"] == "hbm" for r in rows) else None,
+    }), flush=True)
+
+
 def run_kernel(args):
     """Times one quantized GEMM shape (activation pack excluded): rotating
     weight copies totalling ~--kernel-weights-mb keep each launch's weights
@@ -771,6 +875,10 @@ def main():
     if args.kernel:
         torch.cuda.set_device(0)
         run_kernel(args)
+        return
+    if args.sweep:
+        torch.cuda.set_device(0)
+        run_sweep(args)
         return
     if args.impl == "reference":
         # Rank 0 alone times the host path; no process group is needed.

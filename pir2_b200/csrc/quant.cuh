@@ -422,7 +422,9 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
       // ((a0 + a1) + a2) + a3, and the bw partials meet in a pairwise tree
       // with halving offsets (shared memory down to 32, then the warp);
       // the mean is that sum times rows / (rows * k).
-      __shared__ float4 sq4[2048];   // k <= 8192
+      // The squares of the row ([k / 4] float4, dynamic shared memory
+      // sized by the launch) and the partial sums of the virtual threads.
+      extern __shared__ float4 sq4[];
       __shared__ float part[512];
 #pragma unroll
       for (int j = 0; j < kCpt; ++j) {
@@ -590,11 +592,12 @@ static inline int pick_threads(int nchunks, int cpt) {
 // launch enabled, so its prologue may overlap the previous kernel's tail.
 template <typename Args>
 static cudaError_t launch_rows(void (*kernel)(Args), const Args &a,
-                               int64_t rows, int threads, cudaStream_t st) {
+                               int64_t rows, int threads, cudaStream_t st,
+                               size_t smem = 0) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(rows), 1, 1);
   cfg.blockDim = dim3(unsigned(threads), 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -665,8 +668,10 @@ template <int kOut, int kCpt, int kNorm, bool kMod, bool kRes>
 static cudaError_t launch_norm4(const NormArgs &a, int64_t rows,
                                 cudaStream_t st) {
   const int threads = pick_threads(a.kpad / 8, kCpt);
+  // Integer RMSNorm keeps the row's squares in dynamic shared memory.
+  const size_t smem = (kNorm == 1 && kOut != 16) ? size_t(a.k) * 4 : 0;
   return launch_rows(norm_quant_kernel<kOut, kCpt, kNorm, kMod, kRes>, a, rows,
-                     threads, st);
+                     threads, st, smem);
 }
 
 template <int kOut, int kCpt>

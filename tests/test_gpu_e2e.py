@@ -39,7 +39,8 @@ VLM = harness.VLMConfig(layers=2, vocab=2048)
 DIT = harness.DiTConfig(layers=2)
 
 # Relative-L2 bounds on the actions: (fused vs oracle policy, vs bf16).
-TOLERANCE = {"w8a8": (0.05, 0.10), "w4a4": (0.50, 0.80), "fp4": (0.10, 0.60), "fp8": (0.05, 0.30)}
+# W4A4: about twice the measured fused-vs-oracle distance (0.14).
+TOLERANCE = {"w8a8": (0.05, 0.10), "w4a4": (0.28, 0.80), "fp4": (0.10, 0.60), "fp8": (0.05, 0.30)}
 
 
 def _rel_l2(a, b):
