@@ -267,7 +267,13 @@ static bool plan_small_m(int bits, int64_t m, int ntiles, int num_kb, int max_sm
       break;
   }
   const int kb_per = (num_kb + chosen - 1) / chosen;
-  const int stages = std::max(2, std::min(smax, kb_per));
+  int stages = std::max(2, std::min(smax, kb_per));
+  // More CTAs than SMs: keep two per SM (one wave) rather than the whole K
+  // slice of each in flight (N=12288 K=2048: 192 CTAs of 6 stages instead
+  // of 1.3 waves of 8).
+  if (ntiles * chosen > 148)
+    while (stages > 2 && gemm_smem(bits, bn, stages) > size_t(std::min(max_smem, kCoResidentSmem)))
+      --stages;
   const size_t smem = gemm_smem(bits, bn, stages);
   if (smem > size_t(max_smem))
     return false;
@@ -353,8 +359,11 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
   // step, where each GEMM shares its SMs with the programmatically launched
   // kernels around it, than this combined one.
   double best_cost = 1e30;
+  // Token tiles: the fewest of at most 256 rows and up to three more (M=256
+  // as 2-4 tiles of 128-64 rows gives the channel tiles more CTAs than one
+  // 256-row tile with split-K over large partial tiles).
   const int mt0 = int((m + 255) / 256);
-  const int mt1 = m <= 256 ? mt0 : mt0 + 3;
+  const int mt1 = mt0 + 3;
   for (int mt = mt0; mt <= mt1; ++mt) {
     int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
     if (bn > 256 || bn < 16)
