@@ -273,6 +273,24 @@ def roofline(engine, hbm_peak, peak_kind, precision):
     peak_tops = {"fp4": FP4_NOMINAL_TOPS, "fp8": FP8_NOMINAL_TOPS}.get(precision, INT8_PEAK_TOPS)
     achieved = small["bytes"] / (small["t"] * 1e-3) / 1e9 if small["t"] else 0.0
     tops = large["ops"] / (large["t"] * 1e-3) / 1e12 if large["t"] else 0.0
+    in_step = {
+        "method": "each GEMM of one step bracketed by CUDA-event nodes in a captured graph of the step "
+                  "(the event nodes break programmatic dependent launch: about +5 us per small-M launch)",
+        "achieved": round(achieved, 1),
+        "frac": round(achieved / hbm_peak, 4),
+        "avg_launch_us": round(small["t"] * 1e3 / max(small["n"], 1), 2),
+        "large_m_achieved_tops": round(tops, 1),
+        "large_m_frac": round(tops / peak_tops, 4),
+    }
+    if precision in ("w8a8", "w4a4"):
+        chain_small, chain_large = chain_roofline([s for _, _, s in timer.records], precision, hbm_peak, peak_tops)
+        achieved, small_avg = chain_small["achieved"], chain_small["avg_launch_us"]
+        tops = chain_large["achieved_tops"]
+        method = ("the step's GEMM shapes, each back to back in a CUDA graph over rotating weight copies "
+                  "(weights from DRAM), weighted by launch count; CUDA events around the graph replays")
+    else:
+        small_avg = round(small["t"] * 1e3 / max(small["n"], 1), 2)
+        method = in_step["method"]
     return {
         "_gemm_ms_small": small["t"],
         "kernel": {"fp4": "gemm_fp4_kernel", "fp8": "gemm_i8_kernel<9> (kind::f8f6f4)"}.get(
@@ -289,9 +307,13 @@ def roofline(engine, hbm_peak, peak_kind, precision):
         "traffic_unit": "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, one-kernel capture)",
         "algorithmic_bytes_per_launch": round(small["bytes"] / max(small["n"], 1)),
         "launches": small["n"],
-        "avg_launch_us": round(small["t"] * 1e3 / max(small["n"], 1), 2),
+        "avg_launch_us": small_avg,
+        "method": method,
+        "in_step_event_timed": in_step,
         "share_of_gemm_time": round(small["t"] / total, 3) if total else None,
         "large_m": {
+            "kernel": "gemm_pair_kernel (2-SM tiles) where the planner picks them, else gemm_i8_kernel"
+            if precision in ("w8a8", "w4a4") else None,
             "bound": "tensor",
             "launches": large["n"],
             "achieved_tops": round(tops, 1),
@@ -303,6 +325,70 @@ def roofline(engine, hbm_peak, peak_kind, precision):
             }.get(precision, "measured int8 kind::i8 issue-rate probe"),
         },
     }
+
+
+def chain_roofline(records, precision, hbm_peak, peak_tops, weights_mb=300.0, warmup=3):
+    """The step's integer GEMM launches re-timed without event nodes: every
+    distinct shape (M, K, N, epilogue) runs back to back in a CUDA graph over
+    rotating weight copies (weights streamed from DRAM, as in the step),
+    weighted by its launch count in the step.  Returns (small-M: algorithmic
+    bytes / time, large-M: 2MNK / time) as dicts."""
+    from collections import Counter
+
+    from pir2_b200 import ops
+
+    counts = Counter(
+        (s["bits"], s["m"], s["k"], s["npad"], s.get("out_n", s["n"]), s["n"], bool(s.get("residual")),
+         bool(s.get("bias")))
+        for s in records
+        if s["bits"] in (4, 8) and s.get("input") != "rows"
+    )
+    small = {"t": 0.0, "bytes": 0.0, "n": 0}
+    large = {"t": 0.0, "ops": 0.0, "n": 0}
+    g = torch.Generator(device="cuda").manual_seed(11)
+    for (b, m, k, npad, out_n, n, residual, bias), count in counts.items():
+        swiglu = out_n != n
+        cols = k if b == 8 else k // 2
+        dtype = torch.int8 if b == 8 else torch.uint8
+        lo, hi = (-127, 128) if b == 8 else (0, 256)
+        copies = max(1, min(32, int(weights_mb * 1e6 // (npad * cols))))
+        ws = [torch.randint(lo, hi, (npad, cols), device="cuda", dtype=dtype, generator=g) for _ in range(copies)]
+        qa = torch.randint(lo, hi, (m, cols), device="cuda", dtype=dtype, generator=g)
+        sa = torch.rand(m, device="cuda", generator=g)
+        sw = torch.rand(npad, device="cuda", generator=g)
+        bvec = torch.zeros(npad, device="cuda", dtype=torch.bfloat16) if bias else None
+        res = torch.zeros(m, out_n, device="cuda", dtype=torch.bfloat16) if residual else None
+        out = torch.empty(m, out_n, device="cuda", dtype=torch.bfloat16)
+        if swiglu:
+            from pir2_b200.fused import prepare_silu
+
+            lut = prepare_silu(torch.device("cuda"))
+            launch = lambda i: ops.gemm_swiglu(qa, sa, ws[i % copies], sw, bvec, lut, half_n=out_n, out=out)  # noqa: E731
+        else:
+            launch = lambda i: ops.gemm(qa, sa, ws[i % copies], sw, bvec, b, n_store=out_n, out=out,  # noqa: E731
+                                        residual=res)
+        us = _time_graph_launches(launch, max(copies, 16), warmup)
+        shape = {"bits": b, "m": m, "k": k, "n": n, "npad": npad, "out_n": out_n, "residual": residual,
+                 "bias": bias}
+        if m <= 64:
+            small["t"] += count * us
+            small["bytes"] += count * gemm_bytes(shape)
+            small["n"] += count
+        else:
+            large["t"] += count * us
+            large["ops"] += count * 2.0 * m * n * k
+            large["n"] += count
+        del ws
+    torch.cuda.empty_cache()
+    gbs = small["bytes"] / (small["t"] * 1e3) if small["t"] else 0.0
+    tops = large["ops"] / (large["t"] * 1e6) if large["t"] else 0.0
+    return (
+        {"achieved": round(gbs, 1), "frac": round(gbs / hbm_peak, 4), "launches": small["n"],
+         "avg_launch_us": round(small["t"] / max(small["n"], 1), 3),
+         "algorithmic_bytes_per_launch": round(small["bytes"] / max(small["n"], 1))},
+        {"achieved_tops": round(tops, 1), "frac": round(tops / peak_tops, 4), "launches": large["n"],
+         "avg_launch_us": round(large["t"] / max(large["n"], 1), 3)},
+    )
 
 
 def workload_config(args, world):

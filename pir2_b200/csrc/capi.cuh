@@ -85,7 +85,9 @@ static int device_info(DeviceInfo **out) {
         reinterpret_cast<const void *>(gemm_i8_kernel<4, false>),
         reinterpret_cast<const void *>(gemm_i8_kernel<4, true>),
         reinterpret_cast<const void *>(gemm_i8_kernel<9, false>),
-        reinterpret_cast<const void *>(gemm_i8_kernel<9, true>)};
+        reinterpret_cast<const void *>(gemm_i8_kernel<9, true>),
+        reinterpret_cast<const void *>(gemm_pair_kernel<1>),
+        reinterpret_cast<const void *>(gemm_pair_kernel<2>)};
     e = cudaSuccess;
     for (const void *f : gemms)
       if (e == cudaSuccess)
@@ -216,6 +218,7 @@ struct GemmPlan {
   int bn, mtiles, splits, stages;
   size_t smem;
   int wt = 1;          // 128-channel weight tiles per CTA
+  int pair = 0;        // 1: 2-SM tiles (gemm_pair_kernel), bn tokens per pair
 };
 
 static size_t gemm_smem(int bits, int bn, int stages, int wt = 1) {
@@ -328,11 +331,65 @@ static bool plan_fused(int64_t m, int ntiles, int num_kb, int max_smem, FusedInp
   return true;
 }
 
+// Shared memory of a 2-SM pair CTA: the stage ring (wt weight tiles and
+// half the token tile per stage), token scales, barriers, the TMEM slot.
+static size_t pair_smem(int bn, int stages, int wt) {
+  return 1024 + size_t(stages) * (16384 * size_t(wt) + size_t(bn) * 64) + 1024 + (2 * stages + 1) * 8 + 16;
+}
+
+// Best 2-SM plan (int8, more than 64 tokens, no split-K) under the cost
+// model of plan_gemm, with these differences: a CTA stages half of the token
+// tile per K block, and the tensor cores of the pair's two SMs take one
+// 256 x BN MMA together, so per K block a CTA pays max(347, 2 BN) cycles per
+// weight tile while its token bytes halve.  Returns the modelled cost in SM
+// cycles (1e30 when no plan fits).  SwiGLU needs two weight tiles per CTA.
+static double plan_pair(int64_t m, int64_t npad, int num_kb, int sms, int max_smem, bool swiglu,
+                        GemmPlan *out) {
+  double best_cost = 1e30;
+  if (m <= 64)
+    return best_cost;
+  const int mt0 = int((m + 255) / 256);
+  for (int wt = swiglu ? 2 : 1; wt <= 2; ++wt) {
+    const int64_t npairs = (npad + 256 * wt - 1) / (256 * wt);
+    for (int mt = mt0; mt <= mt0 + 3; ++mt) {
+      const int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
+      if (bn > 256 || bn < 32 || int64_t(mt - 1) * bn >= m)
+        continue;
+      int st = 8;
+      while (st > 2 && pair_smem(bn, st, wt) > size_t(max_smem))
+        --st;
+      const size_t smem = pair_smem(bn, st, wt);
+      const size_t stage = 16384 * size_t(wt) + size_t(bn) * 64;
+      // The epilogue stages each 128 x BN output tile in the idle ring.
+      if (smem > size_t(max_smem) || size_t(st) * stage < size_t(swiglu ? 1 : wt) * bn * 256)
+        continue;
+      const int acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+      const int per_sm = (smem <= 113 * 1024 && acc_cols * wt <= 256) ? 2 : 1;
+      const int64_t ctas = 2 * npairs * mt;
+      const int slots = (sms / 2) * 2 * per_sm;
+      const int64_t waves = (ctas + slots - 1) / slots;
+      const int active = int(std::min<int64_t>(ctas, slots));
+      const double w_bw = std::min(128.0, (mt == 1 ? 3400.0 : 9000.0) / active);
+      const double a_bw = std::min(128.0, 9000.0 / active);
+      const double per_kb = std::max(std::max(wt * std::max(347.0, 2.0 * bn), 2700.0 / st),
+                                     16384.0 * wt / w_bw + 64.0 * bn / a_bw);
+      const double cost = double(waves) * (num_kb * per_kb + 3000.0);
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        GemmPlan p{bn, mt, 1, st, smem, wt};
+        p.pair = 1;
+        *out = p;
+      }
+    }
+  }
+  return best_cost;
+}
+
 // Picks the token tile, the number of token tiles, the split-K cluster size,
 // the stage count and the weight tiles per CTA (small M: plan_small_m;
 // larger M: the cost model below).
 static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
-                          int sms, int max_smem) {
+                          int sms, int max_smem, bool allow_pair = false) {
   const int ntiles = int((npad + 127) / 128);
   const int num_kb = int(kpad / 128);
   GemmPlan best{0, 0, 0, 0, 0};   // smem == 0 marks "no plan"
@@ -405,6 +462,13 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
       }
     }
   }
+  // 2-SM tiles when the model prefers them (int8, TMA-stored output).
+  if (allow_pair && bits == 8 && best.smem != 0) {
+    GemmPlan pair;
+    const double pair_cost = plan_pair(m, npad, num_kb, sms, max_smem, false, &pair);
+    if (pair_cost < best_cost)
+      return pair;
+  }
   // A plan that needs more than one wave of CTAs runs in one wave with two
   // weight tiles per CTA (twice the MMA work per staged token byte): on
   // isolated launches M=544 N=12288 K=2048 takes 20.6 instead of 29.2 us,
@@ -432,7 +496,8 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
 // all of the opt-in shared memory for stages (M=544 gate|up: 4 stages of
 // 56 KB instead of 3 under the 200 KB chain cap, VLM prefill 2.021 ->
 // 2.009 ms in the control step).
-static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, int max_smem) {
+static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, int max_smem,
+                               bool allow_pair = false) {
   const int ntw = int((npad + 255) / 256);
   const int num_kb = int(kpad / 128);
   GemmPlan best{0, 0, 0, 0, 0};
@@ -457,8 +522,17 @@ static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, i
       best = GemmPlan{bn, mt, 1, st, smem, 2};
     }
   }
+  if (allow_pair && best.smem != 0) {
+    GemmPlan pair;
+    if (plan_pair(m, npad, num_kb, sms, max_smem, true, &pair) < 1e30)
+      return pair;
+  }
   return best;
 }
+
+// The epilogue stages output tiles in shared memory and writes them with TMA
+// stores when the output rows are 16-byte aligned.
+static bool tma_out(const void *out, int64_t ldo) { return ldo % 8 == 0 && aligned(out, 16); }
 
 // Tensor maps, arguments and launch of one planned integer GEMM.  `n_store`
 // is the number of output columns (half the weight rows for SwiGLU).
@@ -478,8 +552,9 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
                        box_cols, 128u, byte_operands))
     return r;
   if (fin == nullptr) {
+    // A pair CTA loads half of the token tile.
     if (int r = make_map(&tm_a, qa, row_bytes, uint64_t(m), row_bytes, box_cols,
-                         uint32_t(plan.bn), byte_operands))
+                         uint32_t(plan.pair ? plan.bn / 2 : plan.bn), byte_operands))
       return r;
   }
   GemmArgs args;
@@ -524,7 +599,12 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   // The epilogue stages the tile (or, with split-K, each cluster rank's
   // channel slice) in shared memory and writes it with one TMA store when
   // the output rows are 16-byte aligned; otherwise it stores directly.
-  args.tma_store = (ldo % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  args.tma_store = tma_out(out, ldo) ? 1 : 0;
+  // The 2-SM kernel stores through TMA only and has no split-K or fused pack.
+  if (plan.pair && (!args.tma_store || bits != 8 || fin != nullptr || plan.splits != 1 ||
+                    plan.bn < 32 || (silu_lut != nullptr && plan.wt != 2)))
+    return fail(PIR2B_EINVAL, "internal: 2-SM GEMM plan on an unsupported call (bn=%d wt=%d)",
+                plan.bn, plan.wt);
   CUtensorMap tm_out;
   memset(&tm_out, 0, sizeof(tm_out));
   if (args.tma_store) {
@@ -550,6 +630,16 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  if (plan.pair) {
+    const int64_t npairs = (npad + 256 * plan.wt - 1) / (256 * plan.wt);
+    cfg.gridDim = dim3(unsigned(2 * npairs), unsigned(plan.mtiles), 1u);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.z = 1;
+    const cudaError_t e = plan.wt == 2 ? cudaLaunchKernelEx(&cfg, gemm_pair_kernel<2>, tm_w, tm_a, tm_out, args)
+                                       : cudaLaunchKernelEx(&cfg, gemm_pair_kernel<1>, tm_w, tm_a, tm_out, args);
+    return cuda_status(e, "gemm (2-SM) launch");
+  }
   // Token tiles above 64 rows take the wide instantiation.
   const bool wide = plan.bn > 64;
   cudaError_t e =
@@ -792,7 +882,7 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
-  const GemmPlan plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem);
+  const GemmPlan plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem, tma_out(out, ldo));
   if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
       plan.smem > size_t(dev->max_smem))
     return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",
@@ -1082,7 +1172,7 @@ int pir2b_gemm_fused(const void *qa, const float *sa, const void *x, int64_t ldx
                                 "(m=%lld k=%lld npad=%lld)", (long long)m, (long long)k,
                   (long long)npad);
   } else {
-    plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem);
+    plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem, tma_out(out, ldo));
     if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
         plan.smem > size_t(dev->max_smem))
       return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",
@@ -1181,7 +1271,7 @@ int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const flo
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
-  const GemmPlan plan = plan_gemm_wide(m, 2 * half_n, kpad, dev->sms, dev->max_smem);
+  const GemmPlan plan = plan_gemm_wide(m, 2 * half_n, kpad, dev->sms, dev->max_smem, tma_out(out, ldo));
   if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m)
     return fail(PIR2B_EINVAL, "no SwiGLU tile plan fits m=%lld kpad=%lld", (long long)m,
                 (long long)kpad);
@@ -1377,8 +1467,10 @@ int pir2b_dit_ffn_static(const void *qa, const float *sa, const void *up_w, cons
 // header's contract; exported for diagnostics).
 int pir2b_gemm_plan(int bits, int64_t m, int64_t npad, int64_t kpad,
                     int sms, int *bn, int *mtiles, int *splits, int *stages,
-                    int64_t *smem, int *wt) {
-  const GemmPlan p = plan_gemm(bits, m, npad, kpad, sms, 232448);
+                    int64_t *smem, int *wt, int *pair) {
+  // The plan of a call with a TMA-aligned output (2-SM tiles allowed).
+  const GemmPlan p = plan_gemm(bits, m, npad, kpad, sms, 232448, true);
+  *pair = p.pair;
   *wt = p.wt;
   *bn = p.bn;
   *mtiles = p.mtiles;

@@ -118,9 +118,10 @@ __device__ __forceinline__ void unpack_int4_stage(const uint8_t *src,
 // Per-16-channel maxima of |y| over a staged bf16 output tile [rows][width]
 // (width a multiple of 16), written to max_out[m0 + j, group0 + g].
 __device__ __forceinline__ void store_group_max(const GemmArgs &args, const __nv_bfloat16 *stage,
-                                                int width, int rows, int m0, int group0, int et) {
+                                                int width, int rows, int m0, int group0, int et,
+                                                int nthreads = 128) {
   const int groups = width / 16;
-  for (int it = et; it < rows * groups; it += 128) {
+  for (int it = et; it < rows * groups; it += nthreads) {
     const int j = it / groups, g = it - j * groups;
     const uint4 *p = reinterpret_cast<const uint4 *>(stage + j * width + g * 16);
     float mx = 0.f;

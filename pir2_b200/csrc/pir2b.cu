@@ -2,6 +2,7 @@
 // one definition of the device status word without relocatable device code.
 #include "quant.cuh"
 #include "gemm_i8.cuh"
+#include "gemm_pair.cuh"
 #include "gemm_fp4.cuh"
 #include "dit_ffn.cuh"
 #include "pointwise.cuh"

@@ -342,6 +342,188 @@ def test_gemm_residual_epilogue_bitwise():
         assert np.array_equal(bits_of(out), ref)
 
 
+def _plan_of(m, n, k):
+    import ctypes
+
+    lib = _lib.lib()
+    out = [ctypes.c_int() for _ in range(4)] + [ctypes.c_int64(), ctypes.c_int(), ctypes.c_int()]
+    assert lib.pir2b_gemm_plan(8, m, n, k, 148, *[ctypes.byref(v) for v in out]) == 0
+    bn, mt, splits, stages, smem, wt, pair = [v.value for v in out]
+    return dict(bn=bn, mt=mt, splits=splits, stages=stages, wt=wt, pair=pair)
+
+
+# 2-SM tiles (one or two weight tiles per CTA), token tiles of 80-256 rows,
+# ragged channel counts (the odd CTA of the last pair partly or wholly past
+# N) and ragged last token tiles.
+PAIR_SHAPES = [
+    (65, 2048, 12288),
+    (256, 1536, 6144),
+    (544, 2048, 4096),
+    (700, 512, 9000),
+    (1088, 1536, 6000),
+    (2176, 2048, 4096),
+    (2100, 384, 1000),
+]
+
+
+@pytest.mark.parametrize("m,k,n", PAIR_SHAPES)
+@pytest.mark.parametrize("epilogue", ["bias", "lut", "residual", "max_out"])
+def test_gemm_pair_tiles_bitwise(m, k, n, epilogue):
+    """The 2-SM kernel (tcgen05.mma.cta_group::2, even CTA issuing for the
+    pair) against the oracle's exact product and epilogue, for every
+    epilogue variant the one-SM kernel has."""
+    g = torch.Generator().manual_seed(m + k + n)
+    _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, n, 8)
+    npad = qw.shape[0]
+    plan = _plan_of(m, npad, qw.shape[1])
+    assert plan["pair"] == 1, plan
+    y = oracle.gemm_epilogue(oracle.int_matmul(qa, qw), sa, sw, np.pad(bits_of(b), (0, npad - n)), 2,
+                             bits_of(device_lut("tanh").cpu()) if epilogue == "lut" else None)[:, :n]
+    args = dict(n_store=n)
+    if epilogue == "lut":
+        args["out_lut"] = device_lut("tanh")
+    if epilogue == "residual":
+        residual = randn_bf16(g, m, n)
+        args["residual"] = residual.cuda()
+        y = oracle.f32_to_bf16_bits(
+            (oracle.bf16_bits_to_f32(y) + oracle.bf16_bits_to_f32(bits_of(residual))).astype(np.float32))
+    if epilogue == "max_out":
+        args["max_out"] = torch.full((m, npad // 16), -1.0, device="cuda")
+    bias = torch.zeros(npad, dtype=torch.bfloat16)
+    bias[:n] = b
+    if epilogue == "max_out" and npad % 16:
+        # Per-16-channel maxima need whole groups of padded channels.
+        with pytest.raises(ValueError, match="npad % 16"):
+            ops.gemm(torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(qw).cuda(),
+                     torch.from_numpy(sw).cuda(), bias.cuda(), 8, **args)
+        return
+    out = ops.gemm(torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(qw).cuda(),
+                   torch.from_numpy(sw).cuda(), bias.cuda(), 8, **args)
+    got = bits_of(out)
+    mismatch = np.argwhere(got != y)
+    assert mismatch.size == 0, f"{len(mismatch)} mismatches, first at {mismatch[:4].tolist()}"
+    if epilogue == "max_out":
+        yf = np.abs(oracle.bf16_bits_to_f32(y))
+        groups = n // 16
+        want = yf[:, : groups * 16].reshape(m, groups, 16).max(-1)
+        assert np.array_equal(args["max_out"][:, :groups].cpu().numpy(), want)
+    assert_status_clean()
+
+
+def rounding_tie_problem(m, n, seed, traps_per_row=8):
+    """Int8 codes, scales and bias whose epilogue values sit exactly on bf16
+    rounding ties where a fused multiply-add (one rounding of acc*sa*sw + b)
+    would round the other way.  Token row r has codes (1, 127) in columns
+    (2r, 2r+1), so acc[r, c] = qw[c, 2r] + 127 qw[c, 2r+1] is free per
+    element; for `traps_per_row` columns of each row it is searched for such
+    a tie, elsewhere it is random.  Returns qa, sa, qw, sw, bias bits, acc,
+    the number of planted ties."""
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    kpad = (2 * m + 127) // 128 * 128
+    sa = rng.uniform(0.5, 2.0, m).astype(f32)
+    # acc * sa * sw of the order of the bias: ties where the bias cancels most
+    # of the product are the ones a fused multiply-add rounds differently.
+    sw = rng.uniform(1e-5, 3e-5, n).astype(f32)
+    bias = oracle.f32_to_bf16_bits(rng.normal(0.0, 0.05, n).astype(f32))
+    bf = oracle.bf16_bits_to_f32(bias)
+    acc = rng.integers(-16000, 16001, (m, n)).astype(np.int64)
+    cand = np.arange(-16000, 16001)
+    planted = 0
+    for r in range(m):
+        y1 = (cand.astype(f32) * sa[r]).astype(f32)
+        for t in range(traps_per_row):
+            c = (r * traps_per_row + t) % n
+            y3 = ((y1 * sw[c]).astype(f32) + bf[c]).astype(f32)
+            tie = (y3.view(np.uint32) & 0xFFFF) == 0x8000
+            fused = (y1.astype(np.float64) * np.float64(sw[c]) + np.float64(bf[c])).astype(f32)
+            idx = np.flatnonzero(tie & (oracle.f32_to_bf16_bits(fused) != oracle.f32_to_bf16_bits(y3)))
+            if idx.size:
+                acc[r, c] = cand[idx[rng.integers(idx.size)]]
+                planted += 1
+    hi = np.rint(acc / 127.0).astype(np.int64)
+    lo = acc - 127 * hi
+    qa = np.zeros((m, kpad), np.int8)
+    qw = np.zeros((n, kpad), np.int8)
+    rows = np.arange(m)
+    qa[rows, 2 * rows] = 1
+    qa[rows, 2 * rows + 1] = 127
+    qw[:, 2 * rows] = lo.T
+    qw[:, 2 * rows + 1] = hi.T
+    return qa, sa, qw, sw, bias, acc.astype(np.int32), planted
+
+
+@pytest.mark.parametrize("m", [16, 64, 100, 256])
+def test_gemm_epilogue_rounding_ties_bitwise(m):
+    """Planted bf16 rounding ties in the dequant + bias epilogue: every GEMM
+    plan (split-K small tiles, one-SM and 2-SM many-token tiles) must round
+    acc*sa*sw + bias in the reference's order (two multiplies, then the add,
+    each rounded), not as one fused multiply-add."""
+    n = 512
+    qa, sa, qw, sw, bias, acc, planted = rounding_tie_problem(m, n, seed=m)
+    assert planted >= m // 2
+    assert np.array_equal(oracle.int_matmul(qa, qw), acc)
+    ref = oracle.gemm_epilogue(acc, sa, sw, bias, 2)
+    out = ops.gemm(torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(qw).cuda(),
+                   torch.from_numpy(sw).cuda(), to_dev(bias), 8)
+    got = bits_of(out)
+    mismatch = np.argwhere(got != ref)
+    assert mismatch.size == 0, f"{len(mismatch)} of {planted} planted ties, first at {mismatch[:4].tolist()}"
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("m", [16, 100, 256])
+def test_gemm_swiglu_rounding_ties_bitwise(m):
+    """The same planted ties in the gate and up values of the SwiGLU
+    epilogue (gate|up interleaved in 128-row blocks)."""
+    from pir2_b200.fused import prepare_silu
+
+    half = 256
+    qa, sa, qw, sw, bias, acc, planted = rounding_tie_problem(m, 2 * half, seed=1000 + m)
+    assert planted >= m // 2
+    lut = prepare_silu(torch.device("cuda"))
+    y = oracle.gemm_epilogue(acc, sa, sw, bias, 2)
+    silu = oracle.bf16_bits_to_f32(bits_of(lut.cpu())[y[:, :half]])
+    up = oracle.bf16_bits_to_f32(y[:, half:])
+    ref = oracle.f32_to_bf16_bits((silu * up).astype(np.float32))
+    cat = lambda t: ops.interleave_gate_up(t, half)   # noqa: E731
+    out = ops.gemm_swiglu(
+        torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), cat(torch.from_numpy(qw).cuda()),
+        cat(torch.from_numpy(sw).cuda()), cat(to_dev(bias)), lut, half_n=half,
+    )
+    got = bits_of(out)
+    mismatch = np.argwhere(got != ref)
+    assert mismatch.size == 0, f"{len(mismatch)} mismatches, first at {mismatch[:4].tolist()}"
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("m,k,half", [(544, 2048, 6144), (1088, 1536, 3000), (130, 256, 640)])
+def test_gemm_swiglu_pair_tiles_bitwise(m, k, half):
+    """gate|up on 2-SM tiles: CTA r of pair p holds gate block 2p + r and its
+    up block; the value is bf16(silu_lut[gate] * up) of the exact outputs."""
+    from pir2_b200.fused import prepare_silu
+
+    half_pad = (half + 127) // 128 * 128
+    g = torch.Generator().manual_seed(m + k + half)
+    _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, 2 * half_pad, 8)
+    lut = prepare_silu(torch.device("cuda"))
+    y = oracle.gemm_epilogue(oracle.int_matmul(qa, qw), sa, sw, bits_of(b), 2)
+    silu = oracle.bf16_bits_to_f32(bits_of(lut.cpu())[y[:, :half]])
+    up = oracle.bf16_bits_to_f32(y[:, half_pad : half_pad + half])
+    ref = oracle.f32_to_bf16_bits((silu * up).astype(np.float32))
+    cat = lambda t: ops.interleave_gate_up(t, half_pad)   # noqa: E731
+    out = ops.gemm_swiglu(
+        torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), cat(torch.from_numpy(qw).cuda()),
+        cat(torch.from_numpy(sw).cuda()), cat(b.cuda()), lut, half_n=half_pad,
+    )[:, :half]
+    got = bits_of(out)
+    mismatch = np.argwhere(got != ref)
+    detail = [(int(r), int(c), hex(got[r, c]), hex(ref[r, c]), hex(y[r, c]), hex(y[r, half_pad + c]))
+              for r, c in mismatch[:4]]
+    assert mismatch.size == 0, f"{len(mismatch)} mismatches (row, col, got, want, gate, up): {detail}"
+    assert_status_clean()
+
+
 def _sdpa_rows(q, k, v, b, heads, d):
     """fp32 torch SDPA over [B*T, H*D] rows, result as rows."""
     t, s = q.shape[0] // b, k.shape[0] // b

@@ -58,7 +58,7 @@ def test_argument_errors_are_reported_without_touching_the_device():
 
 
 def _plan(lib, bits, m, npad, kpad):
-    out = [ctypes.c_int() for _ in range(4)] + [ctypes.c_int64(), ctypes.c_int()]
+    out = [ctypes.c_int() for _ in range(4)] + [ctypes.c_int64(), ctypes.c_int(), ctypes.c_int()]
     status = lib.pir2b_gemm_plan(bits, m, npad, kpad, 148, *[ctypes.byref(v) for v in out])
     return status, [v.value for v in out]
 
@@ -73,26 +73,38 @@ def test_gemm_planner_always_returns_a_launchable_plan():
         for m in (1, 2, 15, 16, 17, 33, 64, 65, 128, 200, 256, 257, 300, 544, 1024, 1088, 4096):
             for k in (128, 256, 1536, 2048, 6144):
                 for n in (8, 64, 520, 1536, 2048, 4096, 6144, 12288, 52224):
-                    status, (bn, mt, splits, stages, smem, wt) = _plan(lib, bits, m, n, k)
+                    status, (bn, mt, splits, stages, smem, wt, pair) = _plan(lib, bits, m, n, k)
                     assert status == 0, (bits, m, k, n)
                     assert bn % 16 == 0 and 16 <= bn <= 256
                     assert bn * mt >= m and bn * (mt - 1) < m
                     assert splits in (1, 2, 4, 8) and splits <= k // 128
                     assert 2 <= stages <= 12 and 0 < smem <= 232448
+                    if pair:
+                        # 2-SM tiles: int8, more than 64 tokens, no split-K,
+                        # each CTA stages half of the token tile, and the
+                        # output tiles fit the idle stage ring.
+                        assert bits == 8 and m > 64 and splits == 1 and bn >= 32 and wt in (1, 2)
+                        assert stages * (16384 * wt + bn * 64) >= wt * bn * 256
+                        continue
                     assert wt in (1, 2) and (wt == 1 or (bits == 8 and splits == 1 and stages >= 3))
                     if splits > 1:
                         assert stages * (16384 + bn * 128) >= bn * (512 + 128)
 
 
 def test_vlm_prefill_plans_fill_the_machine_in_one_wave():
-    """M = 544 projections of the VLM prefill: the cost model charges every K
-    block the TMA round trip over its stages, which gives 4 token tiles of
-    144 with 6 stages on 128 CTAs (measured faster in the control step than
-    3 tiles of 192 with 5 stages on 96 CTAs)."""
+    """M = 544 projections of the VLM prefill.  N = 2048 keeps the one-SM
+    tiles (4 token tiles of 144, split-K 2, 6 stages: 128 CTAs); the wider
+    ones take 2-SM tiles (each CTA of a pair stages half of the token tile),
+    measured 1.2x faster than their one-SM plans back to back."""
     lib = _lib.lib()
     lib.pir2b_gemm_plan.restype = ctypes.c_int
-    for k, n, splits_want in ((2048, 4096, 1), (2048, 2048, 2), (6144, 2048, 2)):
-        status, (bn, mt, splits, stages, smem, wt) = _plan(lib, 8, 544, n, k)
+    for k in (2048, 6144):
+        status, (bn, mt, splits, stages, smem, wt, pair) = _plan(lib, 8, 544, 2048, k)
         assert status == 0
-        assert (bn, mt, splits, stages, wt) == (144, 4, splits_want, 6, 1), (k, n)
-        assert (n // 128) * mt * splits == 128
+        assert (bn, mt, splits, stages, wt, pair) == (144, 4, 2, 6, 1, 0), k
+        assert (2048 // 128) * mt * splits == 128
+    for k, n in ((2048, 4096), (2048, 12288), (1536, 6144)):
+        status, (bn, mt, splits, stages, smem, wt, pair) = _plan(lib, 8, 544, n, k)
+        assert status == 0 and pair == 1 and splits == 1, (k, n)
+        ctas = 2 * ((n + 256 * wt - 1) // (256 * wt)) * mt
+        assert ctas <= 148, (k, n, ctas)
