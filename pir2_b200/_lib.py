@@ -111,3 +111,13 @@ def device_status(stream=None):
     handle = (stream or torch.cuda.current_stream()).cuda_stream
     check(lib().pir2b_device_status(ctypes.byref(value), handle), "device_status")
     return value.value
+
+
+def set_pair_mode(mode):
+    """Plan override for tests and measurement: 0 lets the GEMM planner
+    choose, 1 takes 2-SM tiles wherever they fit, 2 never takes them.
+    Returns the previous mode."""
+    previous = lib().pir2b_set_pair_mode(int(mode))
+    if previous < 0:
+        check(previous, "set_pair_mode")
+    return previous

@@ -62,6 +62,7 @@ struct GemmArgs {
   int splits;                       // cluster size along z (1,2,4,8)
   int tma_store;                    // 1: output tile leaves through TMA
   int wt;                           // 128-channel weight tiles per CTA (1, 2)
+  int npairs;                       // (2-SM kernel) CTA pairs along the channels
   // SwiGLU epilogue (wt == 2, no split-K): weight tile 0 holds 128 gate
   // channels and tile 1 the matching up channels; the CTA writes
   // bf16(silu_lut[gate] * up) for those 128 output channels.

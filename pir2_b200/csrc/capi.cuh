@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/pir2b.h"
@@ -54,6 +55,9 @@ struct DeviceInfo {
 };
 
 static std::mutex g_mutex;
+// Plan override for tests and measurement (pir2b_set_pair_mode): 0 lets the
+// planner choose, 1 takes 2-SM tiles wherever they fit, 2 never takes them.
+static std::atomic<int> g_pair_mode{0};
 static DeviceInfo g_devices[64];
 
 static int device_info(DeviceInfo **out) {
@@ -332,51 +336,57 @@ static bool plan_fused(int64_t m, int ntiles, int num_kb, int max_smem, FusedInp
 }
 
 // Shared memory of a 2-SM pair CTA: the stage ring (wt weight tiles and
-// half the token tile per stage), token scales, barriers, the TMEM slot.
+// half the token tile per stage), the 32 KB output staging ring, token
+// scales, barriers, the TMEM slot.
 static size_t pair_smem(int bn, int stages, int wt) {
-  return 1024 + size_t(stages) * (16384 * size_t(wt) + size_t(bn) * 64) + 1024 + (2 * stages + 1) * 8 + 16;
+  return 1024 + size_t(stages) * (16384 * size_t(wt) + size_t(bn) * 64) + size_t(kPairStagingBytes) + 1024 +
+         (2 * stages + 4) * 8 + 16;
 }
 
-// Best 2-SM plan (int8, more than 64 tokens, no split-K) under the cost
-// model of plan_gemm, with these differences: a CTA stages half of the token
-// tile per K block, and the tensor cores of the pair's two SMs take one
-// 256 x BN MMA together, so per K block a CTA pays max(347, 2 BN) cycles per
-// weight tile while its token bytes halve.  Returns the modelled cost in SM
-// cycles (1e30 when no plan fits).  SwiGLU needs two weight tiles per CTA.
+// Best 2-SM plan (int8, more than 64 tokens, no split-K) in SM cycles, on
+// the cost terms of plan_gemm: a CTA stages half of the token tile per K
+// block and the pair's two SMs take one 256 x BN MMA together, so a K block
+// costs max(347, 2 BN) cycles per weight tile while the token bytes halve.
+// The kernel is persistent (one CTA per SM, tiles strided over the
+// clusters); its epilogue (measured ~0.22 SM cycles per output value of a
+// CTA with eight epilogue warps) overlaps the next tile's main loop when
+// TMEM holds two accumulator sets (kWt x BN <= 256 columns), else follows
+// it.  Token tiles are multiples of 64 (the output staging groups).
+// Returns the modelled cost (1e30 when no plan fits).
 static double plan_pair(int64_t m, int64_t npad, int num_kb, int sms, int max_smem, bool swiglu,
                         GemmPlan *out) {
   double best_cost = 1e30;
   if (m <= 64)
     return best_cost;
-  const int mt0 = int((m + 255) / 256);
+  const int clusters_max = sms / 2;
   for (int wt = swiglu ? 2 : 1; wt <= 2; ++wt) {
     const int64_t npairs = (npad + 256 * wt - 1) / (256 * wt);
-    for (int mt = mt0; mt <= mt0 + 3; ++mt) {
-      const int bn = int(((m + mt - 1) / mt + 15) / 16 * 16);
-      if (bn > 256 || bn < 32 || int64_t(mt - 1) * bn >= m)
+    for (int bn = 64; bn <= 256; bn += 64) {
+      const int64_t mt = (m + bn - 1) / bn;
+      if (mt > 1 && (mt - 1) * bn >= m)
         continue;
       int st = 8;
       while (st > 2 && pair_smem(bn, st, wt) > size_t(max_smem))
         --st;
       const size_t smem = pair_smem(bn, st, wt);
-      const size_t stage = 16384 * size_t(wt) + size_t(bn) * 64;
-      // The epilogue stages each 128 x BN output tile in the idle ring.
-      if (smem > size_t(max_smem) || size_t(st) * stage < size_t(swiglu ? 1 : wt) * bn * 256)
+      if (smem > size_t(max_smem))
         continue;
-      const int acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
-      const int per_sm = (smem <= 113 * 1024 && acc_cols * wt <= 256) ? 2 : 1;
-      const int64_t ctas = 2 * npairs * mt;
-      const int slots = (sms / 2) * 2 * per_sm;
-      const int64_t waves = (ctas + slots - 1) / slots;
-      const int active = int(std::min<int64_t>(ctas, slots));
+      const int64_t tiles = npairs * mt;
+      const int64_t clusters = std::min<int64_t>(tiles, clusters_max);
+      const int64_t per_cluster = (tiles + clusters - 1) / clusters;
+      const int active = int(2 * clusters);
       const double w_bw = std::min(128.0, (mt == 1 ? 3400.0 : 9000.0) / active);
       const double a_bw = std::min(128.0, 9000.0 / active);
       const double per_kb = std::max(std::max(wt * std::max(347.0, 2.0 * bn), 2700.0 / st),
                                      16384.0 * wt / w_bw + 64.0 * bn / a_bw);
-      const double cost = double(waves) * (num_kb * per_kb + 3000.0);
+      const double main = num_kb * per_kb;
+      const double epi = 0.22 * 128.0 * double(swiglu ? 1 : wt) * bn * (swiglu ? 2.0 : 1.0);
+      const bool two_sets = wt * bn <= 256;
+      const double cost = two_sets ? 3000.0 + main + epi + double(per_cluster - 1) * std::max(main, epi)
+                                   : 3000.0 + double(per_cluster) * (main + epi);
       if (cost < best_cost * 0.999) {
         best_cost = cost;
-        GemmPlan p{bn, mt, 1, st, smem, wt};
+        GemmPlan p{bn, int(mt), 1, st, smem, wt};
         p.pair = 1;
         *out = p;
       }
@@ -462,12 +472,20 @@ static GemmPlan plan_gemm(int bits, int64_t m, int64_t npad, int64_t kpad,
       }
     }
   }
-  // 2-SM tiles when the model prefers them (int8, TMA-stored output).
-  if (allow_pair && bits == 8 && best.smem != 0) {
+  // 2-SM tiles for int8 with more than 64 tokens and a TMA-stored output
+  // (back to back on B200 they beat the one-SM plans 1.04-1.9x from M=128
+  // to M=34816), except where the one-SM plan splits a long K (>= 32 K
+  // blocks) over a cluster and the pair grid would have at most 64 CTAs:
+  // M=128/256 K=6144 N=2048 measured 15.5 vs 10.5 and 15.6 vs 12.3 us.
+  const int pair_mode = g_pair_mode.load(std::memory_order_relaxed);
+  if (allow_pair && bits == 8 && best.smem != 0 && pair_mode != 2) {
     GemmPlan pair;
-    const double pair_cost = plan_pair(m, npad, num_kb, sms, max_smem, false, &pair);
-    if (pair_cost < best_cost)
-      return pair;
+    if (plan_pair(m, npad, num_kb, sms, max_smem, false, &pair) < 1e30) {
+      const int64_t tiles = int64_t((npad + 256 * pair.wt - 1) / (256 * pair.wt)) * pair.mtiles;
+      const int64_t ctas = 2 * std::min<int64_t>(tiles, sms / 2);
+      if (pair_mode == 1 || !(best.splits > 1 && num_kb >= 32 && ctas <= 64))
+        return pair;
+    }
   }
   // A plan that needs more than one wave of CTAs runs in one wave with two
   // weight tiles per CTA (twice the MMA work per staged token byte): on
@@ -522,7 +540,7 @@ static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, i
       best = GemmPlan{bn, mt, 1, st, smem, 2};
     }
   }
-  if (allow_pair && best.smem != 0) {
+  if (allow_pair && best.smem != 0 && g_pair_mode.load(std::memory_order_relaxed) != 2) {
     GemmPlan pair;
     if (plan_pair(m, npad, num_kb, sms, max_smem, true, &pair) < 1e30)
       return pair;
@@ -602,14 +620,15 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   args.tma_store = tma_out(out, ldo) ? 1 : 0;
   // The 2-SM kernel stores through TMA only and has no split-K or fused pack.
   if (plan.pair && (!args.tma_store || bits != 8 || fin != nullptr || plan.splits != 1 ||
-                    plan.bn < 32 || (silu_lut != nullptr && plan.wt != 2)))
+                    plan.bn % kPairGroup != 0 || (silu_lut != nullptr && plan.wt != 2)))
     return fail(PIR2B_EINVAL, "internal: 2-SM GEMM plan on an unsupported call (bn=%d wt=%d)",
                 plan.bn, plan.wt);
   CUtensorMap tm_out;
   memset(&tm_out, 0, sizeof(tm_out));
   if (args.tma_store) {
+    // The 2-SM kernel stores 64-token groups.
     if (int r = make_out_map(&tm_out, out, uint64_t(n_store), uint64_t(m),
-                             uint64_t(ldo), uint32_t(plan.bn),
+                             uint64_t(ldo), uint32_t(plan.pair ? kPairGroup : plan.bn),
                              uint32_t(128 / plan.splits)))
       return r;
   }
@@ -631,8 +650,14 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   if (plan.pair) {
+    // Persistent: one cluster of two CTAs per SM pair, tiles strided over them.
     const int64_t npairs = (npad + 256 * plan.wt - 1) / (256 * plan.wt);
-    cfg.gridDim = dim3(unsigned(2 * npairs), unsigned(plan.mtiles), 1u);
+    args.npairs = int(npairs);
+    DeviceInfo *dev = nullptr;
+    if (int r = device_info(&dev))
+      return r;
+    const int64_t clusters = std::min<int64_t>(npairs * plan.mtiles, std::max(1, dev->sms / 2));
+    cfg.gridDim = dim3(unsigned(2 * clusters), 1u, 1u);
     cfg.blockDim = dim3(kPairThreads, 1, 1);
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.z = 1;
@@ -1461,6 +1486,15 @@ int pir2b_dit_ffn_static(const void *qa, const float *sa, const void *up_w, cons
   return pir2b_dit_ffn(qa, sa, up_w, up_sw, up_bias, up_bias_mode, gelu_lut, down_w, down_sw,
                        down_bias, down_bias_mode, residual, ldr, m, d, f, out, ldo, scratch,
                        kFfnStaticBytes, stream);
+}
+
+// Plan override for tests and the benchmark (not part of the public
+// header's contract): 0 = the planner chooses, 1 = 2-SM tiles wherever they
+// fit, 2 = never.  Returns the previous mode.
+int pir2b_set_pair_mode(int mode) {
+  if (mode < 0 || mode > 2)
+    return fail(PIR2B_EINVAL, "pair mode must be 0, 1 or 2");
+  return g_pair_mode.exchange(mode);
 }
 
 // Plan introspection for tests and the benchmark (not part of the public

@@ -78,6 +78,24 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const void *tmap, ui
       : "memory");
 }
 
+// Remote arrive (release, cluster scope) on an mbarrier given by its
+// shared::cluster address (another CTA's barrier through mapa).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most one (read_1) or none (read_0) of this thread's
+// committed bulk-store groups is still reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // Threads of a pair CTA: warp 0 TMA, warp 1 TMEM and (even CTA) MMA issue,
 // warps 2..9 the epilogue.  Two epilogue warps per TMEM lane quarter (warp w
 // may read lanes 32 (w % 4) .. +31) split the token columns in 16-column
@@ -85,6 +103,11 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const void *tmap, ui
 // TMEM or shared memory.
 constexpr int kPairThreads = 320;
 constexpr int kPairEpiThreads = 256;
+// Output tiles leave in groups of 64 tokens x 128 channels (16 KB of bf16)
+// through a two-buffer staging ring of their own, so the stage ring keeps
+// loading the next tile meanwhile.  Token tiles are multiples of 64.
+constexpr int kPairGroup = 64;
+constexpr int kPairStagingBytes = 2 * kPairGroup * kTileN * 2;
 
 // Epilogue of 16 tokens (j0 .. j0 + 15) of one channel: the exact order of
 // epilogue_value, the two scale products two tokens per packed fp32
@@ -112,6 +135,12 @@ __device__ __forceinline__ void pair_values(const uint32_t (&r)[16], const float
   }
 }
 
+// Persistent over tiles: cluster c of the grid takes tiles c, c + clusters,
+// ... of the (token tile, pair) grid, token-tile major.  The stage ring
+// runs on across tiles; TMEM holds two accumulator sets when a tile needs
+// at most 256 columns (kWt x BN), so the MMAs of the next tile run while
+// the epilogue drains the previous one, else one set that the MMA warp
+// reuses once both CTAs' epilogues have read it.
 template <int kWt>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
@@ -120,36 +149,44 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   // Both CTAs round the same dynamic base up identically, so a stage sits at
   // the same shared-memory offset in both, as the pair's MMAs require.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int bn = args.bn;             // tokens of the pair's tile (multiple of 16)
+  const int bn = args.bn;             // tokens of a tile (multiple of 64)
   const int half = bn / 2;            // tokens this CTA loads
   const int stages = args.stages;
   const int a_bytes = kWt * kWeightTileBytes;
   const int stage_bytes = a_bytes + half * kBlockK;
-  float *s_sa = reinterpret_cast<float *>(smem + size_t(stages) * stage_bytes);
+  uint16_t *staging = reinterpret_cast<uint16_t *>(smem + size_t(stages) * stage_bytes);
+  float *s_sa = reinterpret_cast<float *>(smem + size_t(stages) * stage_bytes + kPairStagingBytes);
   uint64_t *bars = reinterpret_cast<uint64_t *>(s_sa + 256);
   uint64_t *full = bars;                  // (even CTA) both halves of a stage landed
   uint64_t *empty = bars + stages;        // the pair's MMAs are done with a stage
-  uint64_t *accum_full = bars + 2 * stages;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * stages + 1);
+  uint64_t *acc_full = bars + 2 * stages;       // [2] accumulator set ready (both CTAs)
+  uint64_t *acc_empty = bars + 2 * stages + 2;  // [2] (even CTA) both epilogues read it
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * stages + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int block = int(blockIdx.x);      // 2 p + r: this CTA's weight block
-  const int m0 = int(blockIdx.y) * bn;
-  const int w_row0 = block * kWt * kTileN;
+  const int cluster = int(blockIdx.x) >> 1;
+  const int clusters = int(gridDim.x) >> 1;
+  const int npairs = args.npairs;
+  const int ntiles = npairs * ((args.m + bn - 1) / bn);
   const bool swiglu = kWt == 2 && args.silu_lut != nullptr;
   const int nkb = args.num_kb;
-  const uint32_t acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
-  const uint32_t tmem_cols = acc_cols * uint32_t(kWt);
+  const uint32_t acc_cols = bn <= 64 ? 64 : (bn <= 128 ? 128 : 256);
+  const uint32_t set_cols = acc_cols * uint32_t(kWt);
+  const int nbuf = set_cols <= 256 ? 2 : 1;
+  const uint32_t tmem_cols = set_cols * uint32_t(nbuf);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * (kPairEpiThreads / 32));
+    }
     fence_barrier_init();
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_a);
@@ -162,7 +199,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   tc_fence_before();
   __syncthreads();
   // Both CTAs' barriers are initialised and their TMEM allocated before any
-  // copy completes on, or any commit arrives at, the other CTA.
+  // copy completes on, or any commit or arrive reaches, the other CTA.
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
@@ -171,201 +208,237 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     if (elect_one_sync()) {
-      const uint64_t wpolicy = gridDim.y == 1 ? policy_evict_first() : policy_evict_last();
+      const uint64_t wpolicy = policy_evict_last();
       const uint64_t apolicy = policy_evict_last();
       const uint32_t tx = uint32_t(2 * stage_bytes);   // both halves, counted on the even CTA
-      auto weights = [&](int i, int s) {
-        const uint32_t bar = map_peer(smem_u32(&full[s]), 0u);
+      const uint32_t full0 = map_peer(smem_u32(&full[0]), 0u);
+      auto weights = [&](int i, int s, int w_row0) {
         uint8_t *dst = smem + s * stage_bytes;
 #pragma unroll
         for (int w = 0; w < kWt; ++w)
-          tma_load_2d_pair(dst + w * kWeightTileBytes, &tm_w, bar, i * kBlockK, w_row0 + w * kTileN, wpolicy);
+          tma_load_2d_pair(dst + w * kWeightTileBytes, &tm_w, full0 + uint32_t(s) * 8u, i * kBlockK,
+                           w_row0 + w * kTileN, wpolicy);
       };
-      auto tokens = [&](int i, int s) {
-        const uint32_t bar = map_peer(smem_u32(&full[s]), 0u);
-        tma_load_2d_pair(smem + s * stage_bytes + a_bytes, &tm_a, bar, i * kBlockK, m0 + int(rank) * half,
-                         apolicy);
-      };
-      // The first ring pass of weights does not depend on the previous kernel.
-      const int pre = min(nkb, stages);
+      // The first ring pass of the first tile's weights does not depend on
+      // the previous kernel: it is issued before griddepcontrol.wait.
+      const int pre = cluster < ntiles ? min(nkb, stages) : 0;
       for (int i = 0; i < pre; ++i) {
         if (leader)
           mbar_arrive_expect_tx(&full[i], tx);
-        weights(i, i);
+        weights(i, i, (2 * (cluster % npairs) + int(rank)) * kWt * kTileN);
       }
       pdl_wait();
-      for (int i = 0; i < pre; ++i)
-        tokens(i, i);
-      for (int i = pre; i < nkb; ++i) {
-        const int s = i % stages;
-        const uint32_t phase = (i / stages) & 1;
-        if (!mbar_wait(&empty[s], phase ^ 1, kStatusTimeoutProducer))
-          break;
-        if (leader)
-          mbar_arrive_expect_tx(&full[s], tx);
-        weights(i, s);
-        tokens(i, s);
+      uint32_t kbg = 0;   // K blocks issued so far (all tiles)
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += clusters) {
+        const int p = t % npairs, m0 = (t / npairs) * bn;
+        const int w_row0 = (2 * p + int(rank)) * kWt * kTileN;
+        for (int i = 0; i < nkb; ++i, ++kbg) {
+          const int s = int(kbg % uint32_t(stages));
+          if (kbg >= uint32_t(pre)) {
+            if (kbg >= uint32_t(stages) &&
+                !mbar_wait(&empty[s], ((kbg / stages) & 1) ^ 1, kStatusTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            if (leader)
+              mbar_arrive_expect_tx(&full[s], tx);
+            weights(i, s, w_row0);
+          }
+          tma_load_2d_pair(smem + s * stage_bytes + a_bytes, &tm_a, full0 + uint32_t(s) * 8u, i * kBlockK,
+                           m0 + int(rank) * half, apolicy);
+        }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue (even CTA)
     if (leader && elect_one_sync()) {
       const uint32_t idesc = idesc_i8(2 * kTileN, uint32_t(bn));
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % stages;
-        const uint32_t phase = (i / stages) & 1;
-        if (!mbar_wait(&full[s], phase, kStatusTimeoutMma))
+      uint32_t kbg = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += clusters, ++it) {
+        const int b = it % nbuf, use = it / nbuf;
+        if (use > 0 && !mbar_wait(&acc_empty[b], (use - 1) & 1, kStatusTimeoutMma))
           break;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
-        const uint32_t b_addr = a_addr + uint32_t(a_bytes);
+        const uint32_t d = tmem_base + uint32_t(b) * set_cols;
+        for (int i = 0; i < nkb; ++i, ++kbg) {
+          const int s = int(kbg % uint32_t(stages));
+          if (!mbar_wait(&full[s], (kbg / stages) & 1, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
+          const uint32_t b_addr = a_addr + uint32_t(a_bytes);
 #pragma unroll
-        for (int k = 0; k < kBlockK / 32; ++k) {
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          for (int k = 0; k < kBlockK / 32; ++k) {
+            const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
 #pragma unroll
-          for (int w = 0; w < kWt; ++w)
-            mma_i8_pair(tmem_base + uint32_t(w) * acc_cols, smem_desc_sw128(a_addr + w * kWeightTileBytes + k * 32),
-                        smem_desc_sw128(b_addr + k * 32), idesc, acc);
+            for (int w = 0; w < kWt; ++w)
+              mma_i8_pair(d + uint32_t(w) * acc_cols, smem_desc_sw128(a_addr + w * kWeightTileBytes + k * 32),
+                          smem_desc_sw128(b_addr + k * 32), idesc, acc);
+          }
+          mma_commit_pair(&empty[s]);
         }
-        mma_commit_pair(&empty[s]);
+        // Signals both epilogues (also after a failed wait, so they do not
+        // wait out their own budget); orders every MMA of the tile.
+        mma_commit_pair(&acc_full[b]);
       }
-      // Always signal both epilogues; the commit also orders every MMA.
-      mma_commit_pair(accum_full);
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int et = threadIdx.x - 64;   // 0..255
-    pdl_wait();
-    for (int j = et; j < bn; j += kPairEpiThreads)
-      s_sa[j] = (m0 + j < args.m) ? __ldg(args.sa + m0 + j) : 0.f;
     const int quarter = warp & 3;
     const int sub = (warp - 2) >> 2;   // this warp's chunks: c % 2 == sub
     const int ch = quarter * 32 + lane;
     const int bias_mode = args.bias_mode;
-    // Scales and bias of this thread's weight row in each tile.
-    float sw[kWt], b[kWt];
-    bool in_range[kWt];
-#pragma unroll
-    for (int w = 0; w < kWt; ++w) {
-      const int wr = w_row0 + w * kTileN + ch;
-      // SwiGLU: both tiles feed output channel block * 128 + ch.
-      in_range[w] = (swiglu ? block * kTileN + ch : wr) < args.n_store;
-      sw[w] = in_range[w] ? __ldg(args.sw + wr) : 0.f;
-      b[w] = (bias_mode == 2 && in_range[w]) ? __bfloat162float(args.bias[wr]) : 0.f;
-    }
-    named_barrier(1, kPairEpiThreads);
-    const bool have_acc = mbar_wait(accum_full, 0, kStatusTimeoutEpilogue);
-    tc_fence_after();
-    const uint32_t lane_addr = tmem_base + (uint32_t(quarter * 32) << 16);
-    const int valid_m = min(bn, args.m - m0);
-    const int nchunks = bn / 16;
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);
     const uint16_t *silu = reinterpret_cast<const uint16_t *>(args.silu_lut);
     const bool with_res = args.residual != nullptr;
-    uint16_t *stage16 = reinterpret_cast<uint16_t *>(smem);   // [bn][128] per tile, ring idle
-    if (have_acc && swiglu) {
-      const int c0 = block * kTileN;
-      for (int c = sub; c < nchunks; c += 2) {
-        const int j0 = c * 16;
-        uint32_t rg[16], ru[16];
-        tmem_ld_16(lane_addr + j0, rg);
-        tmem_ld_16(lane_addr + acc_cols + j0, ru);
-        tmem_ld_wait_regs(rg);
-        tmem_ld_wait_regs(ru);
-        __nv_bfloat162 g[8], u[8];
-        pair_values(rg, s_sa, j0, sw[0], b[0], bias_mode, g);
-        pair_values(ru, s_sa, j0, sw[kWt - 1], b[kWt - 1], bias_mode, u);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float2 uf = __bfloat1622float2(u[t]);
-          const float2 sg = make_float2(
-              __bfloat162float(__ushort_as_bfloat16(__ldg(silu + __bfloat16_as_ushort(g[t].x)))),
-              __bfloat162float(__ushort_as_bfloat16(__ldg(silu + __bfloat16_as_ushort(g[t].y)))));
-          const __nv_bfloat162 h = __float22bfloat162_rn(__fmul2_rn(sg, uf));
-          stage16[(j0 + 2 * t) * kTileN + ch] = __bfloat16_as_ushort(h.x);
-          stage16[(j0 + 2 * t + 1) * kTileN + ch] = __bfloat16_as_ushort(h.y);
-        }
-      }
-      fence_proxy_async_smem();
-      named_barrier(1, kPairEpiThreads);
-      if (et == 0 && c0 < args.n_store) {
-        tma_store_2d(&tm_out, stage16, c0, m0);
-        tma_store_commit_and_wait();
-      }
-      if (args.max_out != nullptr)
-        store_group_max(args, reinterpret_cast<const __nv_bfloat16 *>(stage16), kTileN, valid_m, m0, c0 / 16,
-                        et, kPairEpiThreads);
-    } else if (have_acc) {
+    const uint32_t acc_empty0 = map_peer(smem_u32(&acc_empty[0]), 0u);
+    const int groups = bn / kPairGroup;
+    int gcount = 0;        // output groups staged so far (staging buffer gcount % 2)
+    bool stored = false;   // (et == 0) the previous group was stored
+    pdl_wait();
+    int it = 0;
+    for (int t = cluster; t < ntiles; t += clusters, ++it) {
+      const int b = it % nbuf, use = it / nbuf;
+      const int p = t % npairs, m0 = (t / npairs) * bn;
+      const int block = 2 * p + int(rank);
+      const int w_row0 = block * kWt * kTileN;
+      const int valid_m = min(bn, args.m - m0);
+      // The previous tile's last group barrier has passed: s_sa is free.
+      for (int j = et; j < bn; j += kPairEpiThreads)
+        s_sa[j] = (m0 + j < args.m) ? __ldg(args.sa + m0 + j) : 0.f;
+      float sw[kWt], bias[kWt];
+      bool in_range[kWt];
 #pragma unroll
       for (int w = 0; w < kWt; ++w) {
-        const int c = w_row0 + w * kTileN + ch;
-        uint16_t *stage = stage16 + size_t(w) * bn * kTileN;
-        const uint32_t acc_addr = lane_addr + uint32_t(w) * acc_cols;
-        // Writes the 16 tokens of chunk k from its accumulator registers.
-        auto finish = [&](int k, const uint32_t (&r)[16]) {
-          const int j0 = k * 16;
-          float res[16];
-          if (with_res) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              res[i] = (in_range[w] && j0 + i < valid_m)
-                           ? __bfloat162float(args.residual[int64_t(m0 + j0 + i) * args.ldr + c])
-                           : 0.f;
-          }
-          __nv_bfloat162 o[8];
-          pair_values(r, s_sa, j0, sw[w], b[w], bias_mode, o);
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            uint16_t lo = __bfloat16_as_ushort(o[t].x), hi = __bfloat16_as_ushort(o[t].y);
-            if (lut != nullptr) {
-              lo = __ldg(lut + lo);
-              hi = __ldg(lut + hi);
-            }
-            if (with_res) {
-              const __nv_bfloat162 v = __floats2bfloat162_rn(
-                  __fadd_rn(__bfloat162float(__ushort_as_bfloat16(lo)), res[2 * t]),
-                  __fadd_rn(__bfloat162float(__ushort_as_bfloat16(hi)), res[2 * t + 1]));
-              lo = __bfloat16_as_ushort(v.x);
-              hi = __bfloat16_as_ushort(v.y);
-            }
-            stage[(j0 + 2 * t) * kTileN + ch] = lo;
-            stage[(j0 + 2 * t + 1) * kTileN + ch] = hi;
-          }
-        };
-        // Chunks sub, sub + 2, ...: the next chunk's TMEM load is in flight
-        // while this one is finished.
-        uint32_t r0[16], r1[16];
-        int k = sub;
-        if (k < nchunks)
-          tmem_ld_16(acc_addr + k * 16, r0);
-        tmem_ld_wait_regs(r0);
-        while (k < nchunks) {
-          const int k1 = k + 2;
-          if (k1 < nchunks)
-            tmem_ld_16(acc_addr + k1 * 16, r1);
-          finish(k, r0);
-          tmem_ld_wait_regs(r1);
-          if (k1 >= nchunks)
-            break;
-          const int k2 = k1 + 2;
-          if (k2 < nchunks)
-            tmem_ld_16(acc_addr + k2 * 16, r0);
-          finish(k1, r1);
-          tmem_ld_wait_regs(r0);
-          k = k2;
-        }
-        fence_proxy_async_smem();
-        named_barrier(1, kPairEpiThreads);
-        const int t0 = w_row0 + w * kTileN;
-        if (et == 0 && t0 < args.n_store)
-          tma_store_2d(&tm_out, stage, t0, m0);
-        if (args.max_out != nullptr)
-          store_group_max(args, reinterpret_cast<const __nv_bfloat16 *>(stage), kTileN, valid_m, m0, t0 / 16,
-                          et, kPairEpiThreads);
+        const int wr = w_row0 + w * kTileN + ch;
+        // SwiGLU: both tiles feed output channel block * 128 + ch.
+        in_range[w] = (swiglu ? block * kTileN + ch : wr) < args.n_store;
+        sw[w] = in_range[w] ? __ldg(args.sw + wr) : 0.f;
+        bias[w] = (bias_mode == 2 && in_range[w]) ? __bfloat162float(args.bias[wr]) : 0.f;
       }
-      if (et == 0)
-        tma_store_commit_and_wait();
+      named_barrier(1, kPairEpiThreads);
+      if (!mbar_wait(&acc_full[b], use & 1, kStatusTimeoutEpilogue))
+        break;
+      tc_fence_after();
+      const uint32_t set = tmem_base + lane_off + uint32_t(b) * set_cols;
+      const int outs = swiglu ? 1 : kWt;   // output tiles of 128 channels
+#pragma unroll
+      for (int w = 0; w < kWt; ++w) {
+        if (w >= outs)
+          break;
+        const int c0 = swiglu ? block * kTileN : w_row0 + w * kTileN;   // first output channel
+        const int c = c0 + ch;
+#pragma unroll 1
+        for (int g = 0; g < groups; ++g, ++gcount) {
+          uint16_t *stage = staging + (gcount & 1) * (kPairGroup * kTileN);
+          // The store that last read this buffer (two groups ago) is done:
+          // at most the previous group's store may still be reading.
+          if (et == 0) {
+            if (stored)
+              bulk_wait_read_1();
+            else
+              bulk_wait_read_0();
+          }
+          named_barrier(1, kPairEpiThreads);
+          // This warp's two 16-token chunks of the group.
+          const int k0 = g * 4 + sub, k1 = k0 + 2;
+          uint32_t r0[16], r1[16];
+          tmem_ld_16(set + uint32_t(w) * acc_cols + k0 * 16, r0);
+          tmem_ld_16(set + uint32_t(w) * acc_cols + k1 * 16, r1);
+          if (swiglu) {
+            uint32_t u0[16], u1[16];
+            tmem_ld_16(set + acc_cols + k0 * 16, u0);
+            tmem_ld_16(set + acc_cols + k1 * 16, u1);
+            tmem_ld_wait_regs(r0);
+            tmem_ld_wait_regs(r1);
+            tmem_ld_wait_regs(u0);
+            tmem_ld_wait_regs(u1);
+            auto gated = [&](int k, const uint32_t (&rg)[16], const uint32_t (&ru)[16]) {
+              const int j0 = k * 16;
+              __nv_bfloat162 gv[8], uv[8];
+              pair_values(rg, s_sa, j0, sw[0], bias[0], bias_mode, gv);
+              pair_values(ru, s_sa, j0, sw[kWt - 1], bias[kWt - 1], bias_mode, uv);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float2 sg = make_float2(
+                    __bfloat162float(__ushort_as_bfloat16(__ldg(silu + __bfloat16_as_ushort(gv[q].x)))),
+                    __bfloat162float(__ushort_as_bfloat16(__ldg(silu + __bfloat16_as_ushort(gv[q].y)))));
+                const __nv_bfloat162 h = __float22bfloat162_rn(__fmul2_rn(sg, __bfloat1622float2(uv[q])));
+                const int jr = j0 - g * kPairGroup + 2 * q;
+                stage[jr * kTileN + ch] = __bfloat16_as_ushort(h.x);
+                stage[(jr + 1) * kTileN + ch] = __bfloat16_as_ushort(h.y);
+              }
+            };
+            gated(k0, r0, u0);
+            gated(k1, r1, u1);
+          } else {
+            tmem_ld_wait_regs(r0);
+            tmem_ld_wait_regs(r1);
+            auto plain = [&](int k, const uint32_t (&r)[16]) {
+              const int j0 = k * 16;
+              float res[16];
+              if (with_res) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  res[i] = (in_range[w] && j0 + i < valid_m)
+                               ? __bfloat162float(args.residual[int64_t(m0 + j0 + i) * args.ldr + c])
+                               : 0.f;
+              }
+              __nv_bfloat162 o[8];
+              pair_values(r, s_sa, j0, sw[w], bias[w], bias_mode, o);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                uint16_t lo = __bfloat16_as_ushort(o[q].x), hi = __bfloat16_as_ushort(o[q].y);
+                if (lut != nullptr) {
+                  lo = __ldg(lut + lo);
+                  hi = __ldg(lut + hi);
+                }
+                if (with_res) {
+                  const __nv_bfloat162 v = __floats2bfloat162_rn(
+                      __fadd_rn(__bfloat162float(__ushort_as_bfloat16(lo)), res[2 * q]),
+                      __fadd_rn(__bfloat162float(__ushort_as_bfloat16(hi)), res[2 * q + 1]));
+                  lo = __bfloat16_as_ushort(v.x);
+                  hi = __bfloat16_as_ushort(v.y);
+                }
+                const int jr = j0 - g * kPairGroup + 2 * q;
+                stage[jr * kTileN + ch] = lo;
+                stage[(jr + 1) * kTileN + ch] = hi;
+              }
+            };
+            plain(k0, r0);
+            plain(k1, r1);
+          }
+          if (w == outs - 1 && g == groups - 1) {
+            // Every TMEM read of this warp for the tile is complete: release
+            // the accumulator set to the even CTA's MMA warp.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+              mbar_arrive_cluster(acc_empty0 + uint32_t(b) * 8u);
+          }
+          fence_proxy_async_smem();
+          named_barrier(1, kPairEpiThreads);
+          const int gm0 = m0 + g * kPairGroup;
+          stored = et == 0 && c0 < args.n_store && gm0 < args.m;
+          if (stored) {
+            tma_store_2d(&tm_out, stage, c0, gm0);
+            bulk_commit();
+          }
+          if (args.max_out != nullptr && gm0 < args.m)
+            store_group_max(args, reinterpret_cast<const __nv_bfloat16 *>(stage), kTileN,
+                            min(kPairGroup, args.m - gm0), gm0, c0 / 16, et, kPairEpiThreads);
+        }
+      }
     }
+    if (et == 0)
+      bulk_wait_read_0();
   }
 
   // Both CTAs' epilogues have read their TMEM (and every MMA has completed)

@@ -363,15 +363,31 @@ PAIR_SHAPES = [
     (1088, 1536, 6000),
     (2176, 2048, 4096),
     (2100, 384, 1000),
+    (5000, 256, 4096),
+    (3000, 1024, 8192),
 ]
+
+
+@pytest.fixture
+def pair_mode():
+    """Sets the planner's 2-SM override for one test and restores it."""
+    previous = []
+
+    def set_mode(mode):
+        previous.append(_lib.set_pair_mode(mode))
+
+    yield set_mode
+    if previous:
+        _lib.set_pair_mode(previous[0])
 
 
 @pytest.mark.parametrize("m,k,n", PAIR_SHAPES)
 @pytest.mark.parametrize("epilogue", ["bias", "lut", "residual", "max_out"])
-def test_gemm_pair_tiles_bitwise(m, k, n, epilogue):
+def test_gemm_pair_tiles_bitwise(m, k, n, epilogue, pair_mode):
     """The 2-SM kernel (tcgen05.mma.cta_group::2, even CTA issuing for the
     pair) against the oracle's exact product and epilogue, for every
     epilogue variant the one-SM kernel has."""
+    pair_mode(1)
     g = torch.Generator().manual_seed(m + k + n)
     _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, n, 8)
     npad = qw.shape[0]
@@ -453,12 +469,13 @@ def rounding_tie_problem(m, n, seed, traps_per_row=8):
     return qa, sa, qw, sw, bias, acc.astype(np.int32), planted
 
 
-@pytest.mark.parametrize("m", [16, 64, 100, 256])
-def test_gemm_epilogue_rounding_ties_bitwise(m):
+@pytest.mark.parametrize("m,mode", [(16, 0), (64, 0), (100, 1), (100, 2), (256, 1), (256, 2)])
+def test_gemm_epilogue_rounding_ties_bitwise(m, mode, pair_mode):
     """Planted bf16 rounding ties in the dequant + bias epilogue: every GEMM
     plan (split-K small tiles, one-SM and 2-SM many-token tiles) must round
     acc*sa*sw + bias in the reference's order (two multiplies, then the add,
     each rounded), not as one fused multiply-add."""
+    pair_mode(mode)
     n = 512
     qa, sa, qw, sw, bias, acc, planted = rounding_tie_problem(m, n, seed=m)
     assert planted >= m // 2
@@ -472,12 +489,13 @@ def test_gemm_epilogue_rounding_ties_bitwise(m):
     assert_status_clean()
 
 
-@pytest.mark.parametrize("m", [16, 100, 256])
-def test_gemm_swiglu_rounding_ties_bitwise(m):
+@pytest.mark.parametrize("m,mode", [(16, 0), (100, 1), (100, 2), (256, 1), (256, 2)])
+def test_gemm_swiglu_rounding_ties_bitwise(m, mode, pair_mode):
     """The same planted ties in the gate and up values of the SwiGLU
     epilogue (gate|up interleaved in 128-row blocks)."""
     from pir2_b200.fused import prepare_silu
 
+    pair_mode(mode)
     half = 256
     qa, sa, qw, sw, bias, acc, planted = rounding_tie_problem(m, 2 * half, seed=1000 + m)
     assert planted >= m // 2
@@ -497,12 +515,13 @@ def test_gemm_swiglu_rounding_ties_bitwise(m):
     assert_status_clean()
 
 
-@pytest.mark.parametrize("m,k,half", [(544, 2048, 6144), (1088, 1536, 3000), (130, 256, 640)])
-def test_gemm_swiglu_pair_tiles_bitwise(m, k, half):
+@pytest.mark.parametrize("m,k,half", [(544, 2048, 6144), (1088, 1536, 3000), (130, 256, 640), (4400, 512, 1024)])
+def test_gemm_swiglu_pair_tiles_bitwise(m, k, half, pair_mode):
     """gate|up on 2-SM tiles: CTA r of pair p holds gate block 2p + r and its
     up block; the value is bf16(silu_lut[gate] * up) of the exact outputs."""
     from pir2_b200.fused import prepare_silu
 
+    pair_mode(1)
     half_pad = (half + 127) // 128 * 128
     g = torch.Generator().manual_seed(m + k + half)
     _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, 2 * half_pad, 8)

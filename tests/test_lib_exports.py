@@ -92,19 +92,17 @@ def test_gemm_planner_always_returns_a_launchable_plan():
 
 
 def test_vlm_prefill_plans_fill_the_machine_in_one_wave():
-    """M = 544 projections of the VLM prefill.  N = 2048 keeps the one-SM
-    tiles (4 token tiles of 144, split-K 2, 6 stages: 128 CTAs); the wider
-    ones take 2-SM tiles (each CTA of a pair stages half of the token tile),
-    measured 1.2x faster than their one-SM plans back to back."""
+    """Many-token int8 GEMMs take 2-SM tiles (each CTA of a pair stages half
+    of the token tile; persistent over tiles): every M = 544 projection of
+    the VLM prefill, and the batched M = 34816 ones.  A long K that the
+    one-SM plan splits over a cluster keeps the one-SM plan when the pair
+    grid would have at most 64 CTAs (M = 128 / 256, K = 6144, N = 2048)."""
     lib = _lib.lib()
     lib.pir2b_gemm_plan.restype = ctypes.c_int
-    for k in (2048, 6144):
-        status, (bn, mt, splits, stages, smem, wt, pair) = _plan(lib, 8, 544, 2048, k)
-        assert status == 0
-        assert (bn, mt, splits, stages, wt, pair) == (144, 4, 2, 6, 1, 0), k
-        assert (2048 // 128) * mt * splits == 128
-    for k, n in ((2048, 4096), (2048, 12288), (1536, 6144)):
-        status, (bn, mt, splits, stages, smem, wt, pair) = _plan(lib, 8, 544, n, k)
-        assert status == 0 and pair == 1 and splits == 1, (k, n)
-        ctas = 2 * ((n + 256 * wt - 1) // (256 * wt)) * mt
-        assert ctas <= 148, (k, n, ctas)
+    for m in (544, 34816):
+        for k, n in ((2048, 4096), (2048, 2048), (2048, 12288), (6144, 2048), (1536, 6144)):
+            status, (bn, mt, splits, stages, smem, wt, pair) = _plan(lib, 8, m, n, k)
+            assert status == 0 and pair == 1 and splits == 1 and bn % 64 == 0, (m, k, n)
+    for m in (128, 256):
+        status, (bn, mt, splits, stages, smem, wt, pair) = _plan(lib, 8, m, 2048, 6144)
+        assert status == 0 and pair == 0 and splits > 1, m
