@@ -85,6 +85,9 @@ def parse():
     p.add_argument("--sweep", action="store_true",
                    help="BASELINE configs 2/3: time every (precision, M, K, N) GEMM point against its roofline")
     p.add_argument("--kernel-residual", action="store_true", help="--kernel with the bf16 residual epilogue")
+    p.add_argument("--step-gemms", action="store_true",
+                   help="record the step's GEMM shapes, then launch every small-M (M <= 64) shape twice "
+                        "inside the NVTX range pir2b_step_gemms (one-kernel ncu traffic captures)")
     return p.parse_args()
 
 
@@ -229,10 +232,11 @@ def gemm_bytes(s):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
-# small-M W8A8 GEMM, from one ncu capture of gemm_i8_kernel<8, 0> on the
-# DiT's M=17 shapes (the command and the per-shape figures are in the ncu
-# summary of that kernel under profiles/); None for the other precisions.
-SMALL_M_TRAFFIC_BYTES = {"w8a8": 7296690}
+# small-M W8A8 GEMM, weighted over the step's 281 small-M launches: one-kernel
+# ncu captures of every small-M shape of the step (`bench.py --step-gemms`;
+# per-shape figures in profiles/gemm_i8_small_m_step_shapes_traffic.md).
+# None for the other precisions.
+SMALL_M_TRAFFIC_BYTES = {"w8a8": 7306041}
 
 
 def roofline(engine, hbm_peak, peak_kind, precision):
@@ -946,8 +950,18 @@ def run_kernel(args):
     us = sorted(times)[2]
     algo = wbytes + m * cols + 4 * m + 4 * npd + 2 * m * n * (2 if res is not None else 1)
     hbm, _ = peaks()
+    import ctypes
+
+    from pir2_b200 import _lib
+
+    plan = [ctypes.c_int() for _ in range(4)] + [ctypes.c_int64(), ctypes.c_int(), ctypes.c_int()]
+    _lib.lib().pir2b_gemm_plan(bits, m, npd, kp, torch.cuda.get_device_properties(0).multi_processor_count,
+                               *[ctypes.byref(v) for v in plan])
+    bn, mtiles, splits, stages, _, wt, pair = [v.value for v in plan]
     print(json.dumps({
-        "kernel": f"gemm_i8_kernel<{bits}>", "m": m, "k": k, "n": n, "residual": res is not None,
+        "kernel": "gemm_pair_kernel (2-SM)" if pair else f"gemm_i8_kernel<{bits}>",
+        "plan": {"bn": bn, "token_tiles": mtiles, "splits": splits, "stages": stages, "weight_tiles": wt},
+        "m": m, "k": k, "n": n, "residual": res is not None,
         "us_per_launch": round(us, 3),
         "algorithmic_bytes": algo, "GBs": round(algo / us / 1e3, 1), "hbm_frac": round(algo / us / 1e3 / hbm, 4),
         "TOPS": round(2 * m * n * k / us / 1e6, 1), "int8_frac": round(2 * m * n * k / us / 1e6 / INT8_PEAK_TOPS, 4),
@@ -956,8 +970,66 @@ def run_kernel(args):
     }), flush=True)
 
 
+def run_step_gemms(args):
+    """Records the GEMM launches of one eager control step (the bench's
+    configuration), then launches each distinct small-M packed-input integer
+    shape twice with random codes inside the NVTX range `pir2b_step_gemms`,
+    printing one JSON line per shape with its launch count in the step."""
+    from collections import Counter
+
+    from pir2_b200 import ops
+
+    engine, session, _ = build_engine(args, 0)
+
+    class Recorder:
+        def __init__(self):
+            self.shapes = []
+
+        def before(self, device):
+            pass
+
+        def after(self, device, **shape):
+            self.shapes.append(shape)
+
+    rec = Recorder()
+    ops.launch_recorder = rec
+    try:
+        with torch.inference_mode(), torch.cuda.stream(engine.stream):
+            engine.policy(*engine.static)
+    finally:
+        ops.launch_recorder = None
+    torch.cuda.synchronize()
+    counts = Counter(json.dumps(s, sort_keys=True) for s in rec.shapes)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    torch.cuda.nvtx.range_push("pir2b_step_gemms")
+    for key, count in counts.most_common():
+        s = json.loads(key)
+        if s["m"] > 64 or s["bits"] not in (4, 8) or s.get("input") == "rows" or s.get("out_n"):
+            continue
+        b, m, k, npad, n = s["bits"], s["m"], s["k"], s["npad"], s["n"]
+        cols = k if b == 8 else k // 2
+        dtype = torch.int8 if b == 8 else torch.uint8
+        lo, hi = (-127, 128) if b == 8 else (0, 256)
+        w = torch.randint(lo, hi, (npad, cols), device="cuda", dtype=dtype, generator=g)
+        qa = torch.randint(lo, hi, (m, cols), device="cuda", dtype=dtype, generator=g)
+        sa = torch.rand(m, device="cuda", generator=g)
+        sw = torch.rand(npad, device="cuda", generator=g)
+        bias = torch.zeros(npad, device="cuda", dtype=torch.bfloat16) if s.get("bias") else None
+        res = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16) if s.get("residual") else None
+        for _ in range(2):
+            ops.gemm(qa, sa, w, sw, bias, b, n_store=n, residual=res)
+        torch.cuda.synchronize()
+        print(json.dumps({"shape": s, "launches_in_step": count, "algorithmic_bytes": gemm_bytes(s)}), flush=True)
+    torch.cuda.nvtx.range_pop()
+    session.__exit__(None, None, None)
+
+
 def main():
     args = parse()
+    if args.step_gemms:
+        torch.cuda.set_device(0)
+        run_step_gemms(args)
+        return
     if args.kernel:
         torch.cuda.set_device(0)
         run_kernel(args)
