@@ -58,6 +58,9 @@ static std::mutex g_mutex;
 // Plan override for tests and measurement (pir2b_set_pair_mode): 0 lets the
 // planner choose, 1 takes 2-SM tiles wherever they fit, 2 never takes them.
 static std::atomic<int> g_pair_mode{0};
+// Split-K override of the small-M plans for measurement
+// (pir2b_set_small_m_splits): 0 lets the planner choose, else 1/2/4/8.
+static std::atomic<int> g_small_m_splits{0};
 static DeviceInfo g_devices[64];
 
 static int device_info(DeviceInfo **out) {
@@ -273,6 +276,9 @@ static bool plan_small_m(int bits, int64_t m, int ntiles, int num_kb, int max_sm
     if (kb_per <= smax && ntiles * s >= 144)
       break;
   }
+  const int forced = g_small_m_splits.load(std::memory_order_relaxed);
+  if (forced > 0 && forced <= num_kb)
+    chosen = forced;
   const int kb_per = (num_kb + chosen - 1) / chosen;
   int stages = std::max(2, std::min(smax, kb_per));
   // More CTAs than SMs: keep two per SM (one wave) rather than the whole K
@@ -1495,6 +1501,15 @@ int pir2b_set_pair_mode(int mode) {
   if (mode < 0 || mode > 2)
     return fail(PIR2B_EINVAL, "pair mode must be 0, 1 or 2");
   return g_pair_mode.exchange(mode);
+}
+
+// Split-K override of the small-M (one token tile of <= 64 rows) plans for
+// measurement (not part of the public header's contract): 0 = the planner
+// chooses, 1/2/4/8 = that many K slices.  Returns the previous value.
+int pir2b_set_small_m_splits(int splits) {
+  if (splits != 0 && splits != 1 && splits != 2 && splits != 4 && splits != 8)
+    return fail(PIR2B_EINVAL, "small-M splits must be 0, 1, 2, 4 or 8");
+  return g_small_m_splits.exchange(splits);
 }
 
 // Plan introspection for tests and the benchmark (not part of the public
