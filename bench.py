@@ -298,7 +298,7 @@ def roofline(engine, hbm_peak, peak_kind, precision):
     return {
         "_gemm_ms_small": small["t"],
         "kernel": {"fp4": "gemm_fp4_kernel", "fp8": "gemm_i8_kernel<9> (kind::f8f6f4)"}.get(
-            precision, f"gemm_i8_kernel<{precision[1:2]}>"
+            precision, f"gemm_few_kernel<{precision[1:2]}> (M<=32; gemm_i8_kernel for 33-64 rows)"
         )
         + " small-M (M<=64) launches",
         "bound": "hbm",

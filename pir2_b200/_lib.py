@@ -121,3 +121,13 @@ def set_pair_mode(mode):
     if previous < 0:
         check(previous, "set_pair_mode")
     return previous
+
+
+def set_few_mode(mode):
+    """Plan override for tests and measurement: 0 lets the planner choose
+    the few-token kernel, 1 takes it for every GEMM of at most 32 token
+    rows, 2 never.  Returns the previous mode."""
+    previous = lib().pir2b_set_few_mode(int(mode))
+    if previous < 0:
+        check(previous, "set_few_mode")
+    return previous

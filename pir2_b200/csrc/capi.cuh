@@ -61,6 +61,9 @@ static std::atomic<int> g_pair_mode{0};
 // Split-K override of the small-M plans for measurement
 // (pir2b_set_small_m_splits): 0 lets the planner choose, else 1/2/4/8.
 static std::atomic<int> g_small_m_splits{0};
+// Few-token kernel override (pir2b_set_few_mode): 0 lets the planner
+// choose, 1 takes gemm_few_kernel for every M <= 32, 2 never.
+static std::atomic<int> g_few_mode{0};
 static DeviceInfo g_devices[64];
 
 static int device_info(DeviceInfo **out) {
@@ -554,6 +557,77 @@ static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, i
   return best;
 }
 
+// Whether a packed-input integer GEMM of m token rows runs the few-token
+// kernel (gemm_few.cuh).
+static bool use_few(int bits, int64_t m) {
+  const int mode = g_few_mode.load(std::memory_order_relaxed);
+  if ((bits != 8 && bits != 4) || m > kFewMaxRows || mode == 2)
+    return false;
+  return true;
+}
+
+// Launch of the few-token kernel: one CTA per 16 output channels, token
+// tiles of 8 rows (1-4), programmatic dependent launch.
+static int launch_few(const void *qa, const float *sa, const void *qw, const float *sw, const void *bias,
+                      int bias_mode, const void *out_lut, const void *residual, int64_t ldr, int bits, int64_t m,
+                      int64_t npad, int64_t kpad, void *out, int64_t ldo, int64_t n_store, float *max_out,
+                      void *stream) {
+  FewArgs a;
+  memset(&a, 0, sizeof(a));
+  a.qa = qa;
+  a.lda = bits == 8 ? kpad : kpad / 2;
+  a.sa = sa;
+  a.qw = qw;
+  a.ldw = a.lda;
+  a.sw = sw;
+  a.bias = bias_mode == PIR2B_BIAS_ADD ? static_cast<const __nv_bfloat16 *>(bias) : nullptr;
+  a.bias_mode = bias_mode;
+  a.out_lut = static_cast<const __nv_bfloat16 *>(out_lut);
+  a.residual = static_cast<const __nv_bfloat16 *>(residual);
+  a.ldr = ldr;
+  a.out = static_cast<__nv_bfloat16 *>(out);
+  a.ldo = ldo;
+  a.max_out = max_out;
+  a.max_parts = int(npad / 16);
+  a.m = int(m);
+  a.npad = int(npad);
+  a.n_store = int(n_store);
+  a.chunks = int(kpad / 128);
+  if (m < 1 || m > kFewMaxRows)
+    return fail(PIR2B_EINVAL, "internal: few-token GEMM with m=%lld", (long long)m);
+  const int tiles = int((m + 7) / 8);
+  // Long K (>= 32 chunks of 128) splits over 16 warps: twice the weight
+  // loads in flight per CTA when Npad / 16 CTAs are few.
+  const bool wide = a.chunks >= 32 && tiles <= 3;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(unsigned((npad + kFewChannels - 1) / kFewChannels), 1u, 1u);
+  cfg.blockDim = dim3(wide ? 512 : 256, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+#define PIR2B_FEW(B, T, W) cudaLaunchKernelEx(&cfg, gemm_few_kernel<B, T, W>, a)
+  if (wide)
+    e = bits == 8 ? (tiles == 1 ? PIR2B_FEW(8, 1, 16) : tiles == 2 ? PIR2B_FEW(8, 2, 16) : PIR2B_FEW(8, 3, 16))
+                  : (tiles == 1 ? PIR2B_FEW(4, 1, 16) : tiles == 2 ? PIR2B_FEW(4, 2, 16) : PIR2B_FEW(4, 3, 16));
+  else if (bits == 8)
+    e = tiles == 1   ? PIR2B_FEW(8, 1, 8)
+        : tiles == 2 ? PIR2B_FEW(8, 2, 8)
+        : tiles == 3 ? PIR2B_FEW(8, 3, 8)
+                     : PIR2B_FEW(8, 4, 8);
+  else
+    e = tiles == 1   ? PIR2B_FEW(4, 1, 8)
+        : tiles == 2 ? PIR2B_FEW(4, 2, 8)
+        : tiles == 3 ? PIR2B_FEW(4, 3, 8)
+                     : PIR2B_FEW(4, 4, 8);
+#undef PIR2B_FEW
+  return cuda_status(e, "gemm (few tokens) launch");
+}
+
 // The epilogue stages output tiles in shared memory and writes them with TMA
 // stores when the output rows are 16-byte aligned.
 static bool tma_out(const void *out, int64_t ldo) { return ldo % 8 == 0 && aligned(out, 16); }
@@ -913,6 +987,9 @@ int pir2b_gemm(const void *qa, const float *sa, const void *qw,
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
+  if (use_few(bits, m))
+    return launch_few(qa, sa, qw, sw, bias, bias_mode, out_lut, residual, ldr, bits, m, npad, kpad, out, ldo,
+                      n_store, nullptr, stream);
   const GemmPlan plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem, tma_out(out, ldo));
   if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
       plan.smem > size_t(dev->max_smem))
@@ -1203,6 +1280,9 @@ int pir2b_gemm_fused(const void *qa, const float *sa, const void *x, int64_t ldx
                                 "(m=%lld k=%lld npad=%lld)", (long long)m, (long long)k,
                   (long long)npad);
   } else {
+    if (use_few(bits, m))
+      return launch_few(qa, sa, qw, sw, bias, bias_mode, out_lut, residual, ldr, bits, m, npad, kpad, out, ldo,
+                        n_store, max_out, stream);
     plan = plan_gemm(bits, m, npad, kpad, dev->sms, dev->max_smem, tma_out(out, ldo));
     if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
         plan.smem > size_t(dev->max_smem))
@@ -1501,6 +1581,15 @@ int pir2b_set_pair_mode(int mode) {
   if (mode < 0 || mode > 2)
     return fail(PIR2B_EINVAL, "pair mode must be 0, 1 or 2");
   return g_pair_mode.exchange(mode);
+}
+
+// Few-token kernel override for tests and measurement (not part of the
+// public header's contract): 0 = the planner chooses, 1 = always for
+// M <= 32, 2 = never.  Returns the previous mode.
+int pir2b_set_few_mode(int mode) {
+  if (mode < 0 || mode > 2)
+    return fail(PIR2B_EINVAL, "few mode must be 0, 1 or 2");
+  return g_few_mode.exchange(mode);
 }
 
 // Split-K override of the small-M (one token tile of <= 64 rows) plans for

@@ -3,6 +3,7 @@
 #include "quant.cuh"
 #include "gemm_i8.cuh"
 #include "gemm_pair.cuh"
+#include "gemm_few.cuh"
 #include "gemm_fp4.cuh"
 #include "dit_ffn.cuh"
 #include "pointwise.cuh"

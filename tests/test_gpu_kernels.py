@@ -469,13 +469,77 @@ def rounding_tie_problem(m, n, seed, traps_per_row=8):
     return qa, sa, qw, sw, bias, acc.astype(np.int32), planted
 
 
-@pytest.mark.parametrize("m,mode", [(16, 0), (64, 0), (100, 1), (100, 2), (256, 1), (256, 2)])
-def test_gemm_epilogue_rounding_ties_bitwise(m, mode, pair_mode):
+@pytest.fixture
+def few_mode():
+    """Sets the few-token kernel override for one test and restores it."""
+    previous = []
+
+    def set_mode(mode):
+        previous.append(_lib.set_few_mode(mode))
+
+    yield set_mode
+    if previous:
+        _lib.set_few_mode(previous[0])
+
+
+FEW_SHAPES = [(1, 1536, 1536), (17, 1536, 6144), (17, 6144, 1536), (16, 2048, 2048), (32, 2048, 4096),
+              (5, 128, 520), (17, 8192, 264)]
+
+
+@pytest.mark.parametrize("kernel", ["few", "tcgen05"])
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("m,k,n", FEW_SHAPES)
+@pytest.mark.parametrize("epilogue", ["bias", "lut", "residual", "max_out"])
+def test_few_row_gemm_both_kernels_bitwise(m, k, n, bits, epilogue, kernel, few_mode):
+    """GEMMs of at most 32 token rows on the few-token kernel (warp-level
+    integer MMAs, K split over the CTA's warps) and on the tcgen05 split-K
+    kernel, against the oracle's exact product and epilogue: bias, output
+    table, residual, per-16-channel maxima; K from 128 to 8192 (1-64 K
+    chunks over 8 or 16 warps), ragged channel counts."""
+    few_mode(1 if kernel == "few" else 2)
+    g = torch.Generator().manual_seed(m * 3 + k + n + bits)
+    _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, n, bits)
+    npad = qw.shape[0]
+    bias = torch.zeros(npad, dtype=torch.bfloat16)
+    bias[:n] = b
+    args = dict(n_store=n)
+    lut_bits = None
+    if epilogue == "lut":
+        lut = device_lut("tanh")
+        args["out_lut"], lut_bits = lut, bits_of(lut.cpu())
+    ua = oracle.unpack_int4(qa) if bits == 4 else qa
+    uw = oracle.unpack_int4(qw) if bits == 4 else qw
+    y = oracle.gemm_epilogue(oracle.int_matmul(ua, uw), sa, sw, bits_of(bias), 2, lut_bits)[:, :n]
+    if epilogue == "residual":
+        residual = randn_bf16(g, m, n)
+        args["residual"] = residual.cuda()
+        y = oracle.f32_to_bf16_bits(
+            (oracle.bf16_bits_to_f32(y) + oracle.bf16_bits_to_f32(bits_of(residual))).astype(np.float32))
+    if epilogue == "max_out":
+        if npad % 16:
+            pytest.skip("per-16-channel maxima need npad % 16 == 0")
+        args["max_out"] = torch.full((m, npad // 16), -1.0, device="cuda")
+    out = ops.gemm(torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), torch.from_numpy(qw).cuda(),
+                   torch.from_numpy(sw).cuda(), bias.cuda(), bits, **args)
+    got = bits_of(out)
+    mismatch = np.argwhere(got != y)
+    assert mismatch.size == 0, f"{len(mismatch)} mismatches, first at {mismatch[:4].tolist()}"
+    if epilogue == "max_out":
+        groups = n // 16
+        want = np.abs(oracle.bf16_bits_to_f32(y))[:, : groups * 16].reshape(m, groups, 16).max(-1)
+        assert np.array_equal(args["max_out"][:, :groups].cpu().numpy(), want)
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("m,mode,few", [(16, 0, 1), (16, 0, 2), (32, 0, 1), (64, 0, 0), (100, 1, 0), (100, 2, 0),
+                                        (256, 1, 0), (256, 2, 0)])
+def test_gemm_epilogue_rounding_ties_bitwise(m, mode, few, pair_mode, few_mode):
     """Planted bf16 rounding ties in the dequant + bias epilogue: every GEMM
     plan (split-K small tiles, one-SM and 2-SM many-token tiles) must round
     acc*sa*sw + bias in the reference's order (two multiplies, then the add,
     each rounded), not as one fused multiply-add."""
     pair_mode(mode)
+    few_mode(few)
     n = 512
     qa, sa, qw, sw, bias, acc, planted = rounding_tie_problem(m, n, seed=m)
     assert planted >= m // 2
