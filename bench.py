@@ -234,9 +234,9 @@ def gemm_bytes(s):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # small-M W8A8 GEMM, weighted over the step's 281 small-M launches: one-kernel
 # ncu captures of every small-M shape of the step (`bench.py --step-gemms`;
-# per-shape figures in profiles/gemm_i8_small_m_step_shapes_traffic.md).
+# per-shape figures in profiles/gemm_small_m_step_shapes_traffic.md).
 # None for the other precisions.
-SMALL_M_TRAFFIC_BYTES = {"w8a8": 7306041}
+SMALL_M_TRAFFIC_BYTES = {"w8a8": 7234785}
 
 
 def roofline(engine, hbm_peak, peak_kind, precision):
@@ -958,8 +958,9 @@ def run_kernel(args):
     _lib.lib().pir2b_gemm_plan(bits, m, npd, kp, torch.cuda.get_device_properties(0).multi_processor_count,
                                *[ctypes.byref(v) for v in plan])
     bn, mtiles, splits, stages, _, wt, pair = [v.value for v in plan]
+    few = m <= 32   # the planner's few-token rule for packed int8/int4 inputs
     print(json.dumps({
-        "kernel": "gemm_pair_kernel (2-SM)" if pair else f"gemm_i8_kernel<{bits}>",
+        "kernel": f"gemm_few_kernel<{bits}>" if few else ("gemm_pair_kernel (2-SM)" if pair else f"gemm_i8_kernel<{bits}>"),
         "plan": {"bn": bn, "token_tiles": mtiles, "splits": splits, "stages": stages, "weight_tiles": wt},
         "m": m, "k": k, "n": n, "residual": res is not None,
         "us_per_launch": round(us, 3),
