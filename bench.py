@@ -44,8 +44,10 @@ if ROOT not in sys.path:
 
 METRIC = "GR00T step latency ms (VLM+4-step DiT) B=1"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
-# int8 dense tensor peak measured on this pool's B200 by a kind::i8 issue-rate
-# probe (8188 MAC/clk/SM x 148 SMs at the sampled clock): 4.5 POPS.
+# int8 dense tensor peak measured on this pool's B200 by the kind::i8
+# issue-rate probe (`bench.py --int8-peak`): 8190 MAC/clk/SM x 148 SMs,
+# 4513 TOPS from CUDA events (the SMs averaged ~1.86 GHz over the probe;
+# 4.76 POPS would need 1965 MHz throughout).
 INT8_PEAK_TOPS = 4520.0
 FP4_NOMINAL_TOPS = 9000.0
 FP8_NOMINAL_TOPS = 4500.0
@@ -85,6 +87,8 @@ def parse():
     p.add_argument("--sweep", action="store_true",
                    help="BASELINE configs 2/3: time every (precision, M, K, N) GEMM point against its roofline")
     p.add_argument("--kernel-residual", action="store_true", help="--kernel with the bf16 residual epilogue")
+    p.add_argument("--int8-peak", action="store_true",
+                   help="measure the int8 tensor-core issue rate (tcgen05 kind::i8 probe) behind INT8_PEAK_TOPS")
     p.add_argument("--step-gemms", action="store_true",
                    help="record the step's GEMM shapes, then launch every small-M (M <= 64) shape twice "
                         "inside the NVTX range pir2b_step_gemms (one-kernel ncu traffic captures)")
@@ -971,6 +975,53 @@ def run_kernel(args):
     }), flush=True)
 
 
+def run_int8_peak(args):
+    """INT8_PEAK_TOPS: every SM issues 128 x 256 x 32 kind::i8 MMAs back to
+    back into a TMEM accumulator (pir2b_int8_peak_probe); reports MAC per
+    clock per SM from the SM cycle counters, TOPS from CUDA events, and the
+    SM clocks sampled meanwhile."""
+    import ctypes
+
+    from pir2_b200 import _lib
+
+    lib = _lib.lib()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    cycles = torch.zeros(sms, dtype=torch.int64, device="cuda")
+    iters = 4096
+    stream = torch.cuda.current_stream()
+
+    def launch():
+        _lib.check(lib.pir2b_int8_peak_probe(iters, sms, ctypes.c_void_p(cycles.data_ptr()),
+                                             ctypes.c_void_p(stream.cuda_stream)), "pir2b_int8_peak_probe")
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    times, per_clk = [], []
+    with ClockSampler(0) as sampler:
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            launch()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e-3)
+            per_clk.append(iters * 4 * 128 * 256 * 32 / float(cycles.max().item()))
+    clocks = sampler.summary()
+    macs = float(sms) * iters * 4 * 128 * 256 * 32
+    mac_clk = sorted(per_clk)[2]
+    print(json.dumps({
+        "int8_peak_probe": "tcgen05.mma.kind::i8 M=128 N=256 K=32, back to back, operands in shared memory",
+        "sms": sms,
+        "mac_per_clk_per_sm": round(mac_clk, 1),
+        "tops_events": round(2 * macs / sorted(times)[2] / 1e12, 1),
+        "tops_at_max_clock": round(2 * mac_clk * sms * (clocks["sm_max_mhz"] or 1965.0) * 1e6 / 1e12, 1),
+        "bench_int8_peak_tops": INT8_PEAK_TOPS,
+        "clocks": clocks,
+        "device_status": _lib.device_status(),
+    }), flush=True)
+
+
 def run_step_gemms(args):
     """Records the GEMM launches of one eager control step (the bench's
     configuration), then launches each distinct small-M packed-input integer
@@ -1027,6 +1078,10 @@ def run_step_gemms(args):
 
 def main():
     args = parse()
+    if args.int8_peak:
+        torch.cuda.set_device(0)
+        run_int8_peak(args)
+        return
     if args.step_gemms:
         torch.cuda.set_device(0)
         run_step_gemms(args)

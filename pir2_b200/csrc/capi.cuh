@@ -1590,6 +1590,25 @@ int pir2b_set_pair_mode(int mode) {
   return g_pair_mode.exchange(mode);
 }
 
+// Issue-rate probe of the int8 tensor cores (not part of the public
+// header's contract; measurement): one CTA per SM issues iters x 4 MMAs of
+// 128 x 256 x 32 back to back; cycles[sm] (device buffer of `ctas` int64)
+// receives each CTA's SM clock cycles from first issue to completion.
+int pir2b_int8_peak_probe(int iters, int ctas, long long *cycles, void *stream) {
+  if (iters < 1 || ctas < 1 || cycles == nullptr || !aligned(cycles, 8))
+    return fail(PIR2B_EINVAL, "peak probe needs iters >= 1, ctas >= 1 and an 8-byte aligned cycle buffer");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  const size_t smem = 1024 + kProbeA + kProbeB + 64;
+  cudaError_t e = cudaFuncSetAttribute(mma_peak_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess) {
+    mma_peak_probe_kernel<<<ctas, 128, smem, static_cast<cudaStream_t>(stream)>>>(iters, cycles);
+    e = cudaGetLastError();
+  }
+  return cuda_status(e, "peak probe launch");
+}
+
 // Few-token kernel override for tests and measurement (not part of the
 // public header's contract): 0 = the planner chooses, 1 = always for
 // M <= 32, 2 = never.  Returns the previous mode.

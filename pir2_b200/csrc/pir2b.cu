@@ -4,6 +4,7 @@
 #include "gemm_i8.cuh"
 #include "gemm_pair.cuh"
 #include "gemm_few.cuh"
+#include "probe.cuh"
 #include "gemm_fp4.cuh"
 #include "dit_ffn.cuh"
 #include "pointwise.cuh"
