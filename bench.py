@@ -74,6 +74,8 @@ def parse():
         help="robots of the batched record (split over the GPUs, strong scaling); 0 skips it",
     )
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--fp-grouped", action="store_true",
+                   help="fp8/fp4: merged sibling projections (one GEMM, fp_grouped) instead of shared packs")
     p.add_argument("--cpu-sample-seconds", type=float, default=20.0,
                    help="host time of the CPU baseline sample in our arm's line")
     p.add_argument("--cpu-budget-seconds", type=float, default=60.0,
@@ -301,7 +303,8 @@ def roofline(engine, hbm_peak, peak_kind, precision):
         method = in_step["method"]
     return {
         "_gemm_ms_small": small["t"],
-        "kernel": {"fp4": "gemm_fp4_kernel", "fp8": "gemm_i8_kernel<9> (kind::f8f6f4)"}.get(
+        "kernel": {"fp4": "gemm_fp4_kernel",
+                   "fp8": "gemm_few_kernel<9> (M<=32, e4m3 warp MMAs; gemm_i8_kernel<9> kind::f8f6f4 for 33-64 rows)"}.get(
             precision, f"gemm_few_kernel<{precision[1:2]}> (M<=32; gemm_i8_kernel for 33-64 rows)"
         )
         + " small-M (M<=64) launches",
@@ -534,7 +537,14 @@ def build_engine(args, local):
     device = torch.device("cuda", local)
     policy = harness.build_policy(device)
     if args.precision in ("fp4", "fp8"):
-        config = OptimizationConfig(precision=args.precision, scope="all", fp_shared_inputs=True)
+        # Every floating producer piR2 wires for fp8 / fp4: one pack per
+        # shared input, SwiGLU / GELU / RMSNorm producers, the DiT LayerNorm
+        # + AdaLN and residual + LayerNorm producers, cross-attention kernel.
+        config = OptimizationConfig(
+            precision=args.precision, scope="all", fp_shared_inputs=not args.fp_grouped,
+            fp_grouped=args.fp_grouped, fp_swiglu=True, fp_gelu=True, fp_rmsnorm=True, fusion=True,
+            norm_modulation_quant=True, residual_norm_quant=True,
+        )
     else:
         config = OptimizationConfig(
             precision=args.precision,
@@ -910,8 +920,8 @@ def run_kernel(args):
     from pir2_b200 import ops
 
     m, k, n = (int(v) for v in args.kernel.split(","))
-    if args.precision not in ("w8a8", "w4a4"):
-        raise SystemExit("--kernel times the integer GEMM (--precision w8a8 or w4a4)")
+    if args.precision in ("fp8", "fp4"):
+        return run_kernel_floating(args, m, k, n)
     bits = 8 if args.precision == "w8a8" else 4
     kp, npd = ops.kpad(k), ops.npad(n)
     wbytes = npd * kp * bits // 8
@@ -970,6 +980,78 @@ def run_kernel(args):
         "us_per_launch": round(us, 3),
         "algorithmic_bytes": algo, "GBs": round(algo / us / 1e3, 1), "hbm_frac": round(algo / us / 1e3 / hbm, 4),
         "TOPS": round(2 * m * n * k / us / 1e6, 1), "int8_frac": round(2 * m * n * k / us / 1e6 / INT8_PEAK_TOPS, 4),
+        "weight_copies": copies, "launches": iters,
+        "note": "median of 5 replays of a CUDA graph of back-to-back launches",
+    }), flush=True)
+
+
+def run_kernel_floating(args, m, k, n):
+    """--kernel for the E4M3 (fp8) and NVFP4 (fp4) GEMMs: weights and tokens
+    are packed once from seeded bf16 by this library's own packs, then timed
+    like the integer GEMM (rotating weight copies, one graph of back-to-back
+    launches, median of 5 replays)."""
+    from pir2_b200 import ops
+
+    fp8 = args.precision == "fp8"
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    if fp8:
+        qw, _, sw = ops.quant_fp8(w, replicate=n, weights=True)
+        qa, _, sa = ops.quant_fp8(x)
+        wbytes = qw.numel() + 4 * n
+        abytes = qa.numel() + 4 * m
+    else:
+        qw, sw = ops.pack_nvfp4(w)
+        qa, sa = ops.pack_nvfp4(x)
+        wbytes = n * k // 2 + n * k // 16
+        abytes = m * k // 2 + m * k // 16
+    copies = max(1, min(64, int(args.kernel_weights_mb * 1e6 // wbytes)))
+    weights = [(qw.clone(), sw.clone()) for _ in range(copies)]
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    res = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16) if args.kernel_residual else None
+    if res is not None and not fp8:
+        raise SystemExit("--kernel-residual: the NVFP4 GEMM has no residual epilogue")
+
+    def launch(i):
+        cw, cs = weights[i % copies]
+        if fp8:
+            ops.gemm_fp8(qa, sa, cw, cs, None, n=n, residual=res, out=out)
+        else:
+            ops.gemm_nvfp4(qa, sa, cw, cs, None, n=n, out=out)
+
+    iters = max(args.steps, copies)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 1)):
+            launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(iters):
+            launch(i)
+    for _ in range(max(args.warmup, 1)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(5):
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3 / iters)
+    us = sorted(times)[2]
+    algo = wbytes + abytes + 2 * m * n * (2 if res is not None else 1)
+    hbm, _ = peaks()
+    print(json.dumps({
+        "kernel": (("gemm_few_kernel<9>" if m <= 32 else "gemm_i8_kernel<9>") if fp8 else "gemm_fp4_kernel"),
+        "precision": args.precision,
+        "m": m, "k": k, "n": n, "residual": res is not None,
+        "us_per_launch": round(us, 3),
+        "algorithmic_bytes": algo, "GBs": round(algo / us / 1e3, 1), "hbm_frac": round(algo / us / 1e3 / hbm, 4),
+        "TFLOPS": round(2 * m * n * k / us / 1e6, 1),
         "weight_copies": copies, "launches": iters,
         "note": "median of 5 replays of a CUDA graph of back-to-back launches",
     }), flush=True)

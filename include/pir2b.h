@@ -52,6 +52,9 @@ extern "C" {
 #define PIR2B_OUT_INT8 8
 #define PIR2B_OUT_INT4 4
 #define PIR2B_OUT_NVFP4 16
+/* First pass of the FP8 producers: bf16 values + the row's maximum finite
+ * |value| (fp32), cast to E4M3 by pir2b_fp8_cast. */
+#define PIR2B_OUT_FP8_VALUES 32
 
 /* Library version (major * 100 + minor). */
 int pir2b_version(void);
@@ -91,6 +94,39 @@ int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
                      int64_t rows, int64_t k, void *q, float *scales,
                      void *stream);
 
+/* The values of pir2b_quant_rows (plain, LUT activation, SiLU * up; the
+ * optional SmoothQuant division) to the floating formats of the piR2 Thor
+ * producers:
+ *   coexecution/optimization/backends/thor/packing.py:84-107 (_swiglu_pack,
+ *     prepare_swiglu), :314-349 (_smooth_pack, prepare_smoothed), :352-392
+ *     (_gelu_pack, prepare_gelu_packed), with _store_producer :57-82
+ * out_format PIR2B_OUT_NVFP4: q = packed E2M1 [rows, k/2], scales = the
+ *   swizzled UE4M3 block-16 factors (layout of pir2b_pack_nvfp4), k % 32 == 0;
+ * out_format PIR2B_OUT_FP8_VALUES: q = bf16 values [rows, k], scales = fp32
+ *   [rows] maximum finite |value| per row, k % 16 == 0; pir2b_fp8_cast
+ *   finishes the E4M3 pack (packing.py:180-199).  q may be NULL here: the
+ *   row maxima alone, the first pass of a plain per-tensor quantization
+ *   whose cast reads x in place.
+ * 16 <= k <= 8192; q 16-byte aligned. */
+int pir2b_floating_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
+                        const void *lut, const float *smooth, int mode, int out_format,
+                        int64_t rows, int64_t k, void *q, void *scales, void *stream);
+
+/* Second pass of the FP8 producers and of the two-pass per-tensor
+ * quantizer: the scale from the row maxima of a PIR2B_OUT_FP8_VALUES pass
+ * and the E4M3 cast,
+ *   coexecution/optimization/backends/thor/packing.py:180-199, :461-482
+ *   (_finish_producer, _fp8_scale_and_cast), fast != 0:
+ *     scale = max(max_r row_max[r] * (1/448), 1e-12);
+ *     q = e4m3(clamp(v / scale, +-448)) with round-to-nearest division;
+ *   fp8_cutlass_linear.cu:61-120 (quantize_bf16), fast == 0:
+ *     scale = max(amax / 448, 1e-12); q = e4m3(clamp(v * (1 / scale), +-448)).
+ * v: bf16 rows of stride ldv (elements, % 8 == 0), k % 8 == 0; q: [rows, k]
+ * bytes; the scale is written to scale[0] and to scale_rep[0..n_rep) (null
+ * when n_rep == 0). */
+int pir2b_fp8_cast(const void *v, int64_t ldv, const float *row_max, int64_t rows, int64_t k, int fast,
+                   void *q, float *scale, float *scale_rep, int64_t n_rep, void *stream);
+
 /* Fused norm (+ AdaLN modulation) (+ gated residual) + quantize/pack.
  * Replaces the Triton producers of
  *   coexecution/kernels/ampere_ada/modulation.py:14-239 (modulation,
@@ -108,8 +144,12 @@ int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
  *   smooth:   optional SmoothQuant divisor as in pir2b_quant_rows
  *   out_format INT8 / INT4: symmetric-row-v1 q + scales;
  *   out_format NVFP4: q = packed E2M1 [rows, k/2], scales = swizzled UE4M3
- *             block-16 factors (layout of pir2b_pack_nvfp4).
- * 8 <= k <= 8192, k % 8 == 0 (k % 32 == 0 for NVFP4); pointers 16-byte
+ *             block-16 factors (layout of pir2b_pack_nvfp4);
+ *   out_format FP8_VALUES: q = bf16 values [rows, k], scales = fp32 [rows]
+ *             maximum finite |value| (then pir2b_fp8_cast).  The floating
+ *             outputs take the Thor producers' RMS variance, sum(x^2) / k
+ *             (packing.py:396-415).
+ * 8 <= k <= 8192, k % 8 == 0 (k % 32 == 0 for NVFP4, % 16 for FP8_VALUES); pointers 16-byte
  * aligned.  (The reference RMS producer has the same k <= 8192 bound,
  * producers.py:295.) */
 int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,

@@ -42,6 +42,9 @@ __all__ = [
     "quant_fp8",
     "e4m3_decode",
     "fp8_gemm",
+    "floating_values",
+    "row_finite_max",
+    "fp8_producer",
 ]
 
 F32 = np.float32
@@ -529,3 +532,37 @@ def fp8_gemm(qa, sa, qw, sw, bias_bits=None):
     if bias_bits is not None:
         y = y + bf16_bits_to_f32(np.asarray(bias_bits, dtype=np.uint16)).astype(np.float64)
     return y
+
+
+# ----------------------------------------------------------------- FP8 producers
+def floating_values(x_bits, *, lut_bits=None, up_bits=None, smooth=None):
+    """The bf16 values the Thor producers store before packing
+    (thor/packing.py:57-82 `_store_producer`, :84-107 `_swiglu_pack`,
+    :314-328 `_smooth_pack`, :352-369 `_gelu_pack`): v = f32(x), or
+    f32(lut[x]), or bf16(f32(lut[x]) * f32(up)); then with `smooth`
+    v = bf16(v / s) (IEEE division).  Returns fp32 (bf16-exact) [rows, k]."""
+    x_bits = np.asarray(x_bits, dtype=np.uint16)
+    if lut_bits is None:
+        v = bf16_bits_to_f32(x_bits)
+    else:
+        v = bf16_bits_to_f32(np.asarray(lut_bits, dtype=np.uint16)[x_bits])
+        if up_bits is not None:
+            v = bf16_round((v * bf16_bits_to_f32(up_bits)).astype(F32))
+    if smooth is not None:
+        v = bf16_round((bf16_round(v) / np.asarray(smooth, F32)[None, :]).astype(F32))
+    return v.astype(F32)
+
+
+def row_finite_max(v):
+    """Each row's maximum finite |value| (packing.py:76-78; 0 for a row with
+    none)."""
+    a = np.abs(np.asarray(v, F32))
+    return np.where(np.isfinite(a), a, F32(0)).max(axis=1).astype(F32)
+
+
+def fp8_producer(values):
+    """Second pass of the FP8 producers (`_finish_producer` with
+    `_fp8_scale_and_cast`, packing.py:180-199, :461-482): the per-tensor
+    scale from the row maxima and the E4M3 cast, i.e. prepare_fp8's
+    arithmetic on the bf16 values.  Returns (codes, scale)."""
+    return quant_fp8(f32_to_bf16_bits(np.asarray(values, F32)), fast=True)

@@ -19,6 +19,7 @@ MODE_PLAIN, MODE_GATED, MODE_LUT = 0, 1, 2
 BIAS_NONE, BIAS_ZERO, BIAS_ADD = 0, 1, 2
 NORM_NONE, NORM_RMS, NORM_LN = 0, 1, 2
 OUT_INT8, OUT_INT4, OUT_NVFP4 = 8, 4, 16
+OUT_FP8_VALUES = 32   # FP8 producers' first pass: bf16 values + fp32 row maxima
 STATUS_TIMEOUT_PROBE = 0x105   # device status word left by pir2b_wait_probe
 
 _P = ctypes.c_void_p
@@ -33,6 +34,8 @@ SIGNATURES = {
     "pir2b_device_status": [ctypes.POINTER(_I), _P],
     "pir2b_wait_probe": [_P, _P],
     "pir2b_quant_rows": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _P, _P, _P],
+    "pir2b_floating_rows": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _P, _P, _P],
+    "pir2b_fp8_cast": [_P, _I64, _P, _I64, _I64, _I, _P, _P, _P, _I64, _P],
     "pir2b_norm_quant_rows": [
         _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I, _F, _I, _I64, _I64, _P, _P, _P,
     ],

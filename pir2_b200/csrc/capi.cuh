@@ -557,11 +557,11 @@ static GemmPlan plan_gemm_wide(int64_t m, int64_t npad, int64_t kpad, int sms, i
   return best;
 }
 
-// Whether a packed-input integer GEMM of m token rows runs the few-token
-// kernel (gemm_few.cuh).
+// Whether a packed-input GEMM of m token rows (int8 / int4 codes, or E4M3
+// as bits 9) runs the few-token kernel (gemm_few.cuh).
 static bool use_few(int bits, int64_t m) {
   const int mode = g_few_mode.load(std::memory_order_relaxed);
-  if ((bits != 8 && bits != 4) || m > kFewMaxRows || mode == 2)
+  if ((bits != 8 && bits != 4 && bits != 9) || m > kFewMaxRows || mode == 2)
     return false;
   return true;
 }
@@ -575,7 +575,7 @@ static int launch_few(const void *qa, const float *sa, const void *qw, const flo
   FewArgs a;
   memset(&a, 0, sizeof(a));
   a.qa = qa;
-  a.lda = bits == 8 ? kpad : kpad / 2;
+  a.lda = bits == 4 ? kpad / 2 : kpad;
   a.sa = sa;
   a.qw = qw;
   a.ldw = a.lda;
@@ -618,9 +618,16 @@ static int launch_few(const void *qa, const float *sa, const void *qw, const flo
   cfg.numAttrs = 1;
   cudaError_t e;
 #define PIR2B_FEW(B, T, W) cudaLaunchKernelEx(&cfg, gemm_few_kernel<B, T, W>, a)
-  if (wide)
+  if (wide && bits == 9)
+    e = tiles == 1 ? PIR2B_FEW(9, 1, 16) : tiles == 2 ? PIR2B_FEW(9, 2, 16) : PIR2B_FEW(9, 3, 16);
+  else if (wide)
     e = bits == 8 ? (tiles == 1 ? PIR2B_FEW(8, 1, 16) : tiles == 2 ? PIR2B_FEW(8, 2, 16) : PIR2B_FEW(8, 3, 16))
                   : (tiles == 1 ? PIR2B_FEW(4, 1, 16) : tiles == 2 ? PIR2B_FEW(4, 2, 16) : PIR2B_FEW(4, 3, 16));
+  else if (bits == 9)
+    e = tiles == 1   ? PIR2B_FEW(9, 1, 8)
+        : tiles == 2 ? PIR2B_FEW(9, 2, 8)
+        : tiles == 3 ? PIR2B_FEW(9, 3, 8)
+                     : PIR2B_FEW(9, 4, 8);
   else if (bits == 8)
     e = tiles == 1   ? PIR2B_FEW(8, 1, 8)
         : tiles == 2 ? PIR2B_FEW(8, 2, 8)
@@ -870,6 +877,80 @@ int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
       "quant_rows launch");
 }
 
+int pir2b_floating_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
+                        const void *lut, const float *smooth, int mode, int out_format,
+                        int64_t rows, int64_t k, void *q, void *scales, void *stream) {
+  if (out_format != PIR2B_OUT_NVFP4 && out_format != PIR2B_OUT_FP8_VALUES)
+    return fail(PIR2B_EINVAL, "out_format must be 16 (NVFP4) or 32 (FP8 values), got %d", out_format);
+  if (mode < 0 || mode > 2)
+    return fail(PIR2B_EINVAL, "mode must be 0, 1 or 2, got %d", mode);
+  const int align_k = out_format == PIR2B_OUT_NVFP4 ? 32 : 16;
+  if (k < 16 || k > 8192 || k % align_k != 0)
+    return fail(PIR2B_EINVAL, "floating producer needs 16 <= k <= 8192 and k %% %d == 0 (k=%lld)", align_k,
+                (long long)k);
+  if (rows < 0 || rows > 0x7fffffffLL)
+    return fail(PIR2B_EINVAL, "row count %lld out of range", (long long)rows);
+  if (rows == 0)
+    return PIR2B_OK;
+  if (x == nullptr || scales == nullptr || (q == nullptr && out_format != PIR2B_OUT_FP8_VALUES))
+    return fail(PIR2B_EINVAL, "x, q and scales must be non-null (q may be null for FP8 values)");
+  if (ldx < k || (mode == 1 && ldu < k))
+    return fail(PIR2B_EINVAL, "row stride smaller than the row width");
+  if (mode != 0 && lut == nullptr)
+    return fail(PIR2B_EINVAL, "mode %d needs a 65536-entry bf16 lookup table", mode);
+  if (mode == 1 && up == nullptr)
+    return fail(PIR2B_EINVAL, "mode 1 needs the multiplier rows (up)");
+  if (!aligned(x, 2) || (up && !aligned(up, 2)) || (q && !aligned(q, 16)) || !aligned(scales, 4) ||
+      (lut && !aligned(lut, 2)) || (smooth && !aligned(smooth, 4)))
+    return fail(PIR2B_EALIGN, "pointer alignment not met");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  QuantArgs a;
+  a.x = static_cast<const __nv_bfloat16 *>(x);
+  a.ldx = ldx;
+  a.up = mode == 1 ? static_cast<const __nv_bfloat16 *>(up) : nullptr;
+  a.ldu = ldu;
+  a.lut = static_cast<const uint16_t *>(lut);
+  a.smooth = smooth;
+  a.q = static_cast<uint8_t *>(q);
+  a.scales = static_cast<float *>(scales);
+  a.k = int(k);
+  a.kpad = int(k);
+  a.mode = mode;
+  const bool vec = (ldx % 8 == 0) && aligned(x, 16) && (mode != 1 || ((ldu % 8 == 0) && aligned(up, 16)));
+  return cuda_status(run_quant_rows(a, out_format, rows, vec, static_cast<cudaStream_t>(stream)),
+                     "floating_rows launch");
+}
+
+int pir2b_fp8_cast(const void *v, int64_t ldv, const float *row_max, int64_t rows, int64_t k, int fast, void *q,
+                   float *scale, float *scale_rep, int64_t n_rep, void *stream) {
+  if (rows < 1 || k < 8 || k % 8 != 0 || k > (1 << 20) || rows > (int64_t(1) << 33) / k || n_rep < 0 ||
+      ldv < k || ldv % 8 != 0)
+    return fail(PIR2B_EINVAL, "fp8_cast needs rows >= 1, k %% 8 == 0, ldv >= k, ldv %% 8 == 0 and n_rep >= 0");
+  if (v == nullptr || row_max == nullptr || q == nullptr || scale == nullptr ||
+      (n_rep > 0 && scale_rep == nullptr))
+    return fail(PIR2B_EINVAL, "fp8_cast operands must be non-null");
+  if (!aligned(v, 16) || !aligned(q, 8) || !aligned(row_max, 4) || !aligned(scale, 4) ||
+      (scale_rep && !aligned(scale_rep, 4)))
+    return fail(PIR2B_EALIGN, "fp8_cast: v 16-byte, q 8-byte, scales 4-byte aligned");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  Fp8CastArgs a;
+  a.v = static_cast<const __nv_bfloat16 *>(v);
+  a.ldv = ldv;
+  a.row_max = row_max;
+  a.rows = rows;
+  a.k = int(k);
+  a.fast = fast ? 1 : 0;
+  a.q = static_cast<uint8_t *>(q);
+  a.scale = scale;
+  a.scale_rep = n_rep > 0 ? scale_rep : nullptr;
+  a.n_rep = n_rep;
+  return cuda_status(run_fp8_cast(a, dev->sms, static_cast<cudaStream_t>(stream)), "fp8_cast launch");
+}
+
 int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
                           void *res_out, const void *gamma, const void *scale,
                           const void *shift, int64_t ld_mod, int64_t tokens,
@@ -877,8 +958,8 @@ int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
                           int out_format, int64_t rows, int64_t k, void *q,
                           void *scales, void *stream) {
   if (out_format != PIR2B_OUT_INT8 && out_format != PIR2B_OUT_INT4 &&
-      out_format != PIR2B_OUT_NVFP4)
-    return fail(PIR2B_EINVAL, "out_format must be 8, 4 or 16, got %d",
+      out_format != PIR2B_OUT_NVFP4 && out_format != PIR2B_OUT_FP8_VALUES)
+    return fail(PIR2B_EINVAL, "out_format must be 8, 4, 16 or 32, got %d",
                 out_format);
   if (norm_kind < 0 || norm_kind > 2)
     return fail(PIR2B_EINVAL, "norm_kind must be 0, 1 or 2");
@@ -888,6 +969,9 @@ int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
                 (long long)k);
   if (out_format == PIR2B_OUT_NVFP4 && k % 32 != 0)
     return fail(PIR2B_EINVAL, "NVFP4 output needs k %% 32 == 0 (k=%lld)",
+                (long long)k);
+  if (out_format == PIR2B_OUT_FP8_VALUES && k % 16 != 0)
+    return fail(PIR2B_EINVAL, "FP8 producer output needs k %% 16 == 0 (k=%lld)",
                 (long long)k);
   if (rows < 0 || rows > 0x7fffffffLL)
     return fail(PIR2B_EINVAL, "row count out of range");
@@ -920,7 +1004,8 @@ int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
     return fail(PIR2B_EINVAL, "a residual input needs a norm");
   int rms_bw = 0;
   float rms_factor = 0.f;
-  if (norm_kind == PIR2B_NORM_RMS && out_format != PIR2B_OUT_NVFP4) {
+  const bool floating = out_format == PIR2B_OUT_NVFP4 || out_format == PIR2B_OUT_FP8_VALUES;
+  if (norm_kind == PIR2B_NORM_RMS && !floating) {
     if (!torch_row_mean_config(rows, k, &rms_bw, &rms_factor))
       return fail(PIR2B_EINVAL,
                   "RMSNorm pack: rows=%lld k=%lld is outside the row-mean order this kernel "
@@ -946,7 +1031,7 @@ int pir2b_norm_quant_rows(const void *x, const void *y_in, const void *gate,
   a.ld_mod = ld_mod;
   a.tokens = tokens;
   a.k = int(k);
-  a.kpad = out_format == PIR2B_OUT_NVFP4 ? int(k) : int((k + 127) / 128 * 128);
+  a.kpad = floating ? int(k) : int((k + 127) / 128 * 128);
   a.eps = eps;
   return cuda_status(run_norm_quant(a, out_format, rows, norm_kind, mod, res,
                                     static_cast<cudaStream_t>(stream)),
@@ -1352,6 +1437,9 @@ int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float 
     return fail(PIR2B_EALIGN, "FP8 GEMM alignment not met");
   if (residual != nullptr && ldr < n_store)
     return fail(PIR2B_EINVAL, "residual row stride ldr must be >= n_store");
+  if (use_few(9, m))
+    return launch_few(qa, sa, qw, sw, bias, bias_mode, nullptr, residual, ldr, 9, m, npad, kpad, out, ldo,
+                      n_store, nullptr, stream);
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;

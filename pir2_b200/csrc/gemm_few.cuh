@@ -1,4 +1,4 @@
-// Few-token W8A8 / W4A4 GEMM (M <= 32 token rows): the DiT's 17-row
+// Few-token W8A8 / W4A4 / E4M3 GEMM (M <= 32 token rows): the DiT's 17-row
 // projections, single-row encoders.
 //
 // Same arithmetic as gemm_i8_kernel: exact int32 sums, then
@@ -21,6 +21,10 @@
 //    the exact dot products;
 //  * the first K chunks of weights are loaded before griddepcontrol.wait:
 //    weights never depend on the previous kernel.
+// kBits == 9: E4M3 codes (the FP8 path) in the int8 byte layout, warp-level
+// e4m3 MMAs (m16n8k32, same fragments) with fp32 accumulators; the warps'
+// fp32 partial tiles are added in warp order, a fixed order, so results are
+// deterministic.
 #pragma once
 #include "args.cuh"
 #include "gemm_i8.cuh"
@@ -51,6 +55,17 @@ struct FewArgs {
   int chunks;                      // K chunks of 128 elements
 };
 
+// D (16 x 8, f32) += A (16 x 32, e4m3, row) * B (32 x 8, e4m3, col): the
+// same fragment layout as the s8 form.
+__device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // D (16 x 8, s32) += A (16 x 32, s8, row) * B (32 x 8, s8, col).
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
@@ -66,13 +81,13 @@ struct Row32 {
   uint32_t w[8];
 };
 
-// Loads K elements [k0, k0 + 32) of a row: 32 int8 bytes, or 16 packed
-// int4 bytes sign-extended to 32 int8 (low nibble = even element).  Rows
-// outside the matrix read as zeros.
+// Loads K elements [k0, k0 + 32) of a row: 32 int8 (or E4M3) bytes, or 16
+// packed int4 bytes sign-extended to 32 int8 (low nibble = even element).
+// Rows outside the matrix read as zeros.
 template <int kBits>
 __device__ __forceinline__ Row32 load_row32(const uint8_t *row, bool valid, int k0) {
   Row32 r;
-  if (kBits == 8) {
+  if (kBits != 4) {
     uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
     if (valid) {
       lo = __ldg(reinterpret_cast<const uint4 *>(row + k0));
@@ -120,14 +135,23 @@ __device__ __forceinline__ void few_load_tokens(FewChunk<kBits, kTiles> &c, cons
   }
 }
 
+// Accumulator type: exact int32 for integer codes, fp32 for E4M3.
+template <int kBits>
+using FewAcc = typename std::conditional<kBits == 9, float, int>::type;
+
 template <int kBits, int kTiles>
-__device__ __forceinline__ void few_mma_chunk(int (&acc)[kTiles][4], const FewChunk<kBits, kTiles> &c) {
+__device__ __forceinline__ void few_mma_chunk(FewAcc<kBits> (&acc)[kTiles][4], const FewChunk<kBits, kTiles> &c) {
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
 #pragma unroll
-    for (int t = 0; t < kTiles; ++t)
-      mma_s8_16832(acc[t], c.wg.w[2 * s], c.wg8.w[2 * s], c.wg.w[2 * s + 1], c.wg8.w[2 * s + 1],
-                   c.tok[t].w[2 * s], c.tok[t].w[2 * s + 1]);
+    for (int t = 0; t < kTiles; ++t) {
+      if constexpr (kBits == 9)
+        mma_e4m3_16832(acc[t], c.wg.w[2 * s], c.wg8.w[2 * s], c.wg.w[2 * s + 1], c.wg8.w[2 * s + 1],
+                       c.tok[t].w[2 * s], c.tok[t].w[2 * s + 1]);
+      else
+        mma_s8_16832(acc[t], c.wg.w[2 * s], c.wg8.w[2 * s], c.wg.w[2 * s + 1], c.wg8.w[2 * s + 1],
+                     c.tok[t].w[2 * s], c.tok[t].w[2 * s + 1]);
+    }
   }
 }
 
@@ -135,7 +159,8 @@ template <int kBits, int kTiles, int kWarps>
 __global__ void __launch_bounds__(kWarps * 32) gemm_few_kernel(const FewArgs a) {
   constexpr int kCols = 8 * kTiles;   // token columns of the CTA's tile
   constexpr int kThreads = kWarps * 32;
-  __shared__ int red[kWarps][kCols][kFewChannels];
+  using Acc = FewAcc<kBits>;
+  __shared__ Acc red[kWarps][kCols][kFewChannels];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int c0 = blockIdx.x * kFewChannels;
@@ -146,10 +171,10 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_few_kernel(const FewArgs a) 
   const bool vg = c0 + g < a.npad, vg8 = c0 + g + 8 < a.npad;
   const uint8_t *wrow_g = w + int64_t(vg ? c0 + g : 0) * a.ldw;
   const uint8_t *wrow_g8 = w + int64_t(vg8 ? c0 + g + 8 : 0) * a.ldw;
-  int acc[kTiles][4];
+  Acc acc[kTiles][4];
 #pragma unroll
   for (int t = 0; t < kTiles; ++t)
-    acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
+    acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = Acc(0);
 
   // Two chunks in flight: the weights of the first two are requested before
   // the previous kernel has finished (they do not depend on it).
@@ -195,7 +220,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_few_kernel(const FewArgs a) 
   for (int idx = threadIdx.x; idx < kCols * kFewChannels; idx += kThreads) {
     const int j = idx / kFewChannels, cl = idx % kFewChannels;
     const int c = c0 + cl;
-    int sum = 0;
+    Acc sum = Acc(0);
 #pragma unroll
     for (int wp = 0; wp < kWarps; ++wp)
       sum += red[wp][j][cl];
@@ -203,7 +228,8 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_few_kernel(const FewArgs a) 
     float mag = 0.f;
     if (live) {
       const float b = a.bias_mode == 2 ? __bfloat162float(a.bias[c]) : 0.f;
-      __nv_bfloat16 o = epilogue_value(__int2float_rn(sum), a.sa[j], a.sw[c], b, a.bias_mode, lut);
+      const float accf = kBits == 9 ? float(sum) : __int2float_rn(int(sum));
+      __nv_bfloat16 o = epilogue_value(accf, a.sa[j], a.sw[c], b, a.bias_mode, lut);
       if (a.residual != nullptr)
         o = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o), __bfloat162float(a.residual[int64_t(j) * a.ldr + c])));
       a.out[int64_t(j) * a.ldo + c] = o;

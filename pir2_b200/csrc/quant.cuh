@@ -11,6 +11,7 @@
 // producers is kept (see the per-function citations).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdint>
 
 #pragma once
@@ -123,8 +124,98 @@ __device__ __forceinline__ float row_scale(float m) {
   return m > 0.f ? __fmul_rn(m, inv) : 1.0f;
 }
 
+// ------------------------------------------------------------------ NVFP4
+// Per 16-element block: m = max|v|; s = m / 6 (1 if m == 0); e = e4m3_rn(min(s,
+// 448)); d = f32(e), or s when e decodes to 0; codes = e2m1_rn_satfinite(v *
+// (1 / d)).  thor/packing.py:24-54 (IEEE division variant).
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 p;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 p, %2, %1;\n\t"
+      "cvt.u32.u8 %0, p;\n\t}"
+      : "=r"(r)
+      : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cvt_e4m3(float v) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.f), "f"(v));
+  return r & 0xFFu;
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint32_t e) {
+  // e4m3fn: 1 sign, 4 exponent bits (bias 7), 3 mantissa bits; exact in fp32.
+  const uint32_t sign = (e & 0x80u) << 24, ex = (e >> 3) & 0xFu, man = e & 7u;
+  const float mag = ex == 0 ? __fmul_rn(float(man), 1.0f / 512.0f)
+                            : __uint_as_float(((ex + 120u) << 23) | (man << 20));
+  return __uint_as_float(__float_as_uint(mag) | sign);
+}
+
+__device__ __forceinline__ int64_t nvfp4_sf_offset(int64_t row, int64_t sf,
+                                                   int64_t blocks_k) {
+  // 128 rows x 4 factors per 512-byte atom (fp4_cutlass_linear.cu:686-690).
+  return ((row >> 7) * blocks_k << 9) + ((row & 31) << 4) +
+         (((row & 127) >> 5) << 2) + ((sf >> 2) << 9) + (sf & 3);
+}
+
+// One thread holds 8 values = half a 16-block; its neighbour lane holds the
+// other half (chunks 2b and 2b+1 belong to lanes 2l and 2l+1).
+__device__ __forceinline__ void store_nvfp4_chunk(const float (&v)[8],
+                                                  int64_t row, int chunk,
+                                                  int k, uint8_t *packed,
+                                                  uint8_t *sf) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    m = fmaxf(m, fabsf(v[i]));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  const float s = m > 0.f ? __fdiv_rn(m, 6.0f) : 1.0f;
+  const uint32_t e = cvt_e4m3(fminf(s, 448.0f));
+  float d = e4m3_to_f32(e);
+  if (!(d > 0.f))
+    d = s;
+  const float r = __fdiv_rn(1.0f, d);
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i += 2)
+    w |= cvt_e2m1x2(__fmul_rn(v[i], r), __fmul_rn(v[i + 1], r)) << (4 * i);
+  const int c0 = chunk * 8;
+  if (c0 < k) {
+    *reinterpret_cast<uint32_t *>(packed + row * (k / 2) + c0 / 2) = w;
+    if ((chunk & 1) == 0) {
+      const int64_t blocks_k = (k / 16 + 3) / 4;
+      sf[nvfp4_sf_offset(row, chunk / 2, blocks_k)] = uint8_t(e);
+    }
+  }
+}
+
+// Stores a thread's chunks of a row (values already bf16-exact) as bf16:
+// chunk c = threadIdx.x + j * blockDim.x covers columns [8c, 8c + 8).
+template <int kCpt>
+__device__ __forceinline__ void store_bf16_row(const float (&v)[kCpt][8], __nv_bfloat16 *out, int k,
+                                               int nchunks) {
+#pragma unroll
+  for (int j = 0; j < kCpt; ++j) {
+    const int chunk = threadIdx.x + j * blockDim.x;
+    if (chunk < nchunks && chunk * 8 < k) {
+      uint4 raw;
+      __nv_bfloat16 *p = reinterpret_cast<__nv_bfloat16 *>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        p[i] = __float2bfloat16_rn(v[j][i]);
+      *reinterpret_cast<uint4 *>(out + chunk * 8) = raw;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ quant_rows
-// integer.py:27-94 (_activation_values, _prepare).
+// integer.py:27-94 (_activation_values, _prepare).  The same values (plain,
+// LUT activation, SiLU * up, SmoothQuant division) also go to the floating
+// outputs of the piR2 Thor producers (thor/packing.py:57-107, :314-369):
+// kBits 16 writes NVFP4 (store_nvfp4_chunk), kBits 32 the bf16 values and
+// the row's maximum finite |value| (the first pass of the FP8 producers,
+// whose second pass is fp8_cast_kernel).
 template <int kBits, int kCpt, bool kVec>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantArgs a) {
   __shared__ float red[32];
@@ -161,10 +252,32 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantArgs a) {
       if (a.smooth != nullptr && c0 + i < a.k)
         t = bf16r(__fdiv_rn(bf16r(t), __ldg(a.smooth + c0 + i)));
       v[j][i] = t;
-      m = fmaxf(m, fabsf(t));
+      // Non-finite values do not enter the FP8 producers' maximum
+      // (packing.py:76-78); fmaxf already skips NaN.
+      if (kBits != 32 || fabsf(t) != INFINITY)
+        m = fmaxf(m, fabsf(t));
     }
   }
+  if constexpr (kBits == 16) {
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j) {
+      const int chunk = threadIdx.x + j * blockDim.x;
+      // Every lane takes part in the pairwise shuffle; stores are guarded.
+      store_nvfp4_chunk(v[j], row, chunk < nchunks ? chunk : nchunks, a.k, a.q,
+                        reinterpret_cast<uint8_t *>(a.scales));
+    }
+    return;
+  }
   m = block_max(m, red);
+  if constexpr (kBits == 32) {
+    if (threadIdx.x == 0)
+      a.scales[row] = m;
+    // q == null: the row maxima alone (the plain FP8 activation quantizer,
+    // whose cast reads x in place).
+    if (a.q != nullptr)
+      store_bf16_row(v, reinterpret_cast<__nv_bfloat16 *>(a.q) + int64_t(row) * a.k, a.k, nchunks);
+    return;
+  }
   const float s = row_scale<kBits>(m);
   if (threadIdx.x == 0)
     a.scales[row] = s;
@@ -295,76 +408,11 @@ __global__ void __launch_bounds__(256) quant_rows_cluster_kernel(const QuantArgs
   }
 }
 
-// ------------------------------------------------------------------ NVFP4
-// Per 16-element block: m = max|v|; s = m / 6 (1 if m == 0); e = e4m3_rn(min(s,
-// 448)); d = f32(e), or s when e decodes to 0; codes = e2m1_rn_satfinite(v *
-// (1 / d)).  thor/packing.py:24-54 (IEEE division variant).
-__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
-  uint32_t r;
-  asm("{\n\t.reg .b8 p;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 p, %2, %1;\n\t"
-      "cvt.u32.u8 %0, p;\n\t}"
-      : "=r"(r)
-      : "f"(lo), "f"(hi));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cvt_e4m3(float v) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.f), "f"(v));
-  return r & 0xFFu;
-}
-
-__device__ __forceinline__ float e4m3_to_f32(uint32_t e) {
-  // e4m3fn: 1 sign, 4 exponent bits (bias 7), 3 mantissa bits; exact in fp32.
-  const uint32_t sign = (e & 0x80u) << 24, ex = (e >> 3) & 0xFu, man = e & 7u;
-  const float mag = ex == 0 ? __fmul_rn(float(man), 1.0f / 512.0f)
-                            : __uint_as_float(((ex + 120u) << 23) | (man << 20));
-  return __uint_as_float(__float_as_uint(mag) | sign);
-}
-
-__device__ __forceinline__ int64_t nvfp4_sf_offset(int64_t row, int64_t sf,
-                                                   int64_t blocks_k) {
-  // 128 rows x 4 factors per 512-byte atom (fp4_cutlass_linear.cu:686-690).
-  return ((row >> 7) * blocks_k << 9) + ((row & 31) << 4) +
-         (((row & 127) >> 5) << 2) + ((sf >> 2) << 9) + (sf & 3);
-}
-
-// One thread holds 8 values = half a 16-block; its neighbour lane holds the
-// other half (chunks 2b and 2b+1 belong to lanes 2l and 2l+1).
-__device__ __forceinline__ void store_nvfp4_chunk(const float (&v)[8],
-                                                  int64_t row, int chunk,
-                                                  int k, uint8_t *packed,
-                                                  uint8_t *sf) {
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    m = fmaxf(m, fabsf(v[i]));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-  const float s = m > 0.f ? __fdiv_rn(m, 6.0f) : 1.0f;
-  const uint32_t e = cvt_e4m3(fminf(s, 448.0f));
-  float d = e4m3_to_f32(e);
-  if (!(d > 0.f))
-    d = s;
-  const float r = __fdiv_rn(1.0f, d);
-  uint32_t w = 0;
-#pragma unroll
-  for (int i = 0; i < 8; i += 2)
-    w |= cvt_e2m1x2(__fmul_rn(v[i], r), __fmul_rn(v[i + 1], r)) << (4 * i);
-  const int c0 = chunk * 8;
-  if (c0 < k) {
-    *reinterpret_cast<uint32_t *>(packed + row * (k / 2) + c0 / 2) = w;
-    if ((chunk & 1) == 0) {
-      const int64_t blocks_k = (k / 16 + 3) / 4;
-      sf[nvfp4_sf_offset(row, chunk / 2, blocks_k)] = uint8_t(e);
-    }
-  }
-}
-
 // ------------------------------------------------------------------ norm
 // modulation.py:86-219 (AdaLN, LayerNorm + AdaLN, residual + LayerNorm +
 // AdaLN), producers.py:19-53 (RMSNorm tail), thor/packing.py:109-150, :395-415
-// (the same producers to NVFP4).
+// (the same producers to NVFP4, kOut 16, and to FP8, kOut 32: bf16 values
+// and the row's maximum finite |value|, cast by fp8_cast_kernel).
 template <int kOut, int kCpt, int kNorm, bool kMod, bool kRes>
 __global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
   __shared__ float red[32];
@@ -412,7 +460,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
   if constexpr (kNorm == 1) {
     // RMSNorm: var = mean(x^2); n = bf16(x * rsqrt(var + eps)); v = bf16(n*g)
     float var;
-    if constexpr (kOut != 16) {
+    if constexpr (kOut != 16 && kOut != 32) {
       // The integer producer's variance is the reference's B200 path
       // (producers.py:19-53 via rms_statistics.py:171-190): fp32 squares,
       // then torch's fp32 row mean, whose order this reproduces (ATen
@@ -558,6 +606,19 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const NormArgs a) {
       store_nvfp4_chunk(v[j], row, chunk < nchunks ? chunk : nchunks, a.k,
                         a.q, a.scales);
     }
+  } else if constexpr (kOut == 32) {
+    // Maximum of the finite |value| (packing.py:76-78).
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < kCpt; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (fabsf(v[j][i]) != INFINITY)
+          m = fmaxf(m, fabsf(v[j][i]));
+    m = block_max(m, red);
+    if (threadIdx.x == 0)
+      reinterpret_cast<float *>(a.scales)[row] = m;
+    store_bf16_row(v, reinterpret_cast<__nv_bfloat16 *>(a.q) + row * a.k, a.k, nchunks);
   } else {
   float m = 0.f;
 #pragma unroll
@@ -640,6 +701,15 @@ static cudaError_t launch_quant_cluster(const QuantArgs &a, int64_t rows,
 cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
                            bool vec, cudaStream_t st) {
   const int nchunks = a.kpad / 8;
+  // Floating outputs (NVFP4, FP8 first pass): rows of at most 8192 values
+  // (1024 chunks) held in registers.
+  if (bits == 16 || bits == 32) {
+    if (nchunks > 1024)
+      return cudaErrorInvalidValue;
+    if (nchunks <= 256)
+      return bits == 16 ? launch_quant<16, 1>(a, rows, vec, st) : launch_quant<32, 1>(a, rows, vec, st);
+    return bits == 16 ? launch_quant<16, 4>(a, rows, vec, st) : launch_quant<32, 4>(a, rows, vec, st);
+  }
   // Few long rows: spread each row over a cluster of CTAs (<= 8, each with
   // 128 threads x 2 chunks) so the launch covers more of the 148 SMs.
   if (rows <= 64 && nchunks > 256) {
@@ -669,7 +739,7 @@ static cudaError_t launch_norm4(const NormArgs &a, int64_t rows,
                                 cudaStream_t st) {
   const int threads = pick_threads(a.kpad / 8, kCpt);
   // Integer RMSNorm keeps the row's squares in dynamic shared memory.
-  const size_t smem = (kNorm == 1 && kOut != 16) ? size_t(a.k) * 4 : 0;
+  const size_t smem = (kNorm == 1 && kOut != 16 && kOut != 32) ? size_t(a.k) * 4 : 0;
   return launch_rows(norm_quant_kernel<kOut, kCpt, kNorm, kMod, kRes>, a, rows,
                      threads, st, smem);
 }
@@ -708,6 +778,8 @@ cudaError_t run_norm_quant(const NormArgs &a, int out_format, int64_t rows,
     return launch_norm2<8>(a, rows, norm, mod, res, st);
   if (out_format == 4)
     return launch_norm2<4>(a, rows, norm, mod, res, st);
+  if (out_format == 32)
+    return launch_norm2<32>(a, rows, norm, mod, res, st);
   return launch_norm2<16>(a, rows, norm, mod, res, st);
 }
 
@@ -867,6 +939,84 @@ cudaError_t run_fp8_quant(const Fp8QuantArgs &a, int ranks, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, fp8_quant_kernel, a);
+}
+
+// Second pass of the FP8 producers (thor/packing.py:180-199 with
+// _fp8_scale_and_cast, :461-482) and of the per-tensor activation quantizer:
+// the first pass wrote each row's maximum finite |value|; every CTA reduces
+// those maxima (one fp32 per row, a few KB) to the scale and casts its
+// grid-stride share of 8-value chunks of v (rows of stride ldv):
+//  * fast (prepare_fp8 and the producers): scale = max(amax * (1/448),
+//    1e-12), q = e4m3_rn(clamp(v / scale, -448, 448)), IEEE division;
+//  * default (quantize_bf16, fp8_cutlass_linear.cu:61-120): scale =
+//    max(amax / 448, 1e-12), q = e4m3_rn(clamp(v * (1 / scale), -448, 448)).
+// CTA 0 writes the scale; the CTAs together write its replicated copy (the
+// per-row scale vector the E4M3 GEMM reads).
+struct Fp8CastArgs {
+  const __nv_bfloat16 *v;   // [rows, ldv]
+  int64_t ldv;
+  const float *row_max;     // [rows]
+  int64_t rows;
+  int k;                    // k % 8 == 0
+  int fast;
+  uint8_t *q;               // [rows, k]
+  float *scale;             // [1]
+  float *scale_rep;         // [n_rep] or null
+  int64_t n_rep;
+};
+
+constexpr int kFp8CastThreads = 256;
+
+__global__ void __launch_bounds__(kFp8CastThreads) fp8_cast_kernel(const Fp8CastArgs a) {
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_launch_dependents();
+  float m = 0.f;
+  for (int64_t r = threadIdx.x; r < a.rows; r += kFp8CastThreads)
+    m = fmaxf(m, __ldg(a.row_max + r));
+  m = block_max(m, red);
+  const float scale = a.fast ? fmaxf(__fmul_rn(m, 1.0f / kFp8Max), kFp8MinScale)
+                             : fmaxf(__fdiv_rn(m, kFp8Max), kFp8MinScale);
+  const float inv = __fdiv_rn(1.0f, scale);
+  const int nch = a.k / 8;
+  const int64_t chunks = a.rows * int64_t(nch);
+  const int64_t stride = int64_t(gridDim.x) * kFp8CastThreads;
+  for (int64_t i = int64_t(blockIdx.x) * kFp8CastThreads + threadIdx.x; i < chunks; i += stride) {
+    const int64_t row = i / nch;
+    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(a.v + row * a.ldv + (i - row * nch) * 8));
+    const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float x = __bfloat162float(e[j]);
+      f[j] = fminf(kFp8Max, fmaxf(-kFp8Max, a.fast ? __fdiv_rn(x, scale) : __fmul_rn(x, inv)));
+    }
+    uint2 out;
+    out.x = cvt_e4m3x2(f[0], f[1]) | (cvt_e4m3x2(f[2], f[3]) << 16);
+    out.y = cvt_e4m3x2(f[4], f[5]) | (cvt_e4m3x2(f[6], f[7]) << 16);
+    reinterpret_cast<uint2 *>(a.q)[i] = out;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    *a.scale = scale;
+  if (a.scale_rep != nullptr)
+    for (int64_t i = int64_t(blockIdx.x) * kFp8CastThreads + threadIdx.x; i < a.n_rep; i += stride)
+      a.scale_rep[i] = scale;
+}
+
+cudaError_t run_fp8_cast(const Fp8CastArgs &a, int sms, cudaStream_t st) {
+  const int64_t chunks = a.rows * int64_t(a.k / 8);
+  const int64_t want = (std::max<int64_t>(chunks, a.n_rep) + kFp8CastThreads - 1) / kFp8CastThreads;
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(sms) * 4)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid), 1, 1);
+  cfg.blockDim = dim3(kFp8CastThreads, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fp8_cast_kernel, a);
 }
 
 } // namespace pir2b

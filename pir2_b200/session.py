@@ -116,24 +116,9 @@ class GrootOptimizations:
             "categories": sorted(categories),
         }
         if self.config.precision in ("fp4", "fp8"):
-            from .floating import FloatingProjections
+            from .floating import FloatingProjections, aligned_for
 
             precision = self.config.precision
-            # piR2's floating fusions (grouped / shared-input projections,
-            # SwiGLU, GELU and RMSNorm packing, AdaLN connections) are not in
-            # this build's floating paths: refuse them instead of ignoring them.
-            unsupported = [
-                flag
-                for flag in ("fp_grouped", "fp_swiglu", "fp_gelu", "fp_rmsnorm")
-                if getattr(self.config, flag)
-            ]
-            if self.config.fusion or self.config.norm_modulation_quant:
-                unsupported.append("fusion")
-            if precision == "fp8" and self.config.fp_smoothquant is not None:
-                unsupported.append("fp_smoothquant")
-            if unsupported:
-                raise ValueError(f"Not implemented for {precision} in this build: {', '.join(unsupported)}")
-
             smoothing = None
             if self.config.fp_smoothquant is not None:
                 from .smoothquant import load_profile
@@ -142,12 +127,15 @@ class GrootOptimizations:
                 selected = {
                     n: (modules[n], *sites[n][1:])
                     for n in executed
-                    if modules[n].in_features % 256 == 0 and modules[n].out_features % 32 == 0
+                    if aligned_for(precision, modules[n].in_features, modules[n].out_features)
                 }
                 groups = inventory(model, expanded=expanded)[1]
                 smoothing, self.coverage["smoothquant"] = load_profile(
                     self.config.fp_smoothquant, selected, groups, self.config.precision
                 )
+            # coexecution/optimization/session.py:159-193: the floating
+            # projections with their producers, then the DiT norm / residual
+            # producers when norm_modulation_quant is set.
             self.floating = FloatingProjections(
                 model,
                 executed,
@@ -155,11 +143,32 @@ class GrootOptimizations:
                 precision=precision,
                 fast_fp8=self.config.fp8_fast_quant,
                 shared_inputs=self.config.fp_shared_inputs,
+                grouped=self.config.fp_grouped,
+                swiglu=self.config.fp_swiglu,
+                gelu=self.config.fp_gelu,
+                rmsnorm=self.config.fp_rmsnorm,
                 groups=inventory(model, expanded=expanded)[1],
             )
-            self.coverage["shared_input_groups"] = len(self.floating.groups)
             self.stack.callback(self.floating.close)
             self.floating.set()
+            self.coverage["shared_input_groups"] = len(self.floating.groups)
+            self.coverage["floating"] = self.floating.coverage
+            if self.config.norm_modulation_quant:
+                from .floating import FloatingConnections
+
+                connections = FloatingConnections(model, self.floating, residual=self.config.residual_norm_quant)
+                self.stack.callback(connections.close)
+                connections.set()
+                self.coverage["norm_quantization_fusion"] = {
+                    "attention_producers": len(connections.norms),
+                    "residual_ffn_producers": len(connections.blocks),
+                }
+            if self.config.fusion and self.config.fusion_mode == "all":
+                from .pointwise import DiTAttentionFusion
+
+                self.attention = DiTAttentionFusion(model.action_head.model)
+                self.stack.callback(self.attention.close)
+                self.attention.set()
             return
         from .connections import AdditionalConnections
         from .producers import QuantizationProducers

@@ -21,7 +21,12 @@ What it runs, unmodified, from the reference:
     `_norm_modulation_pack` with `_store_fp4_row`
     (coexecution/optimization/backends/thor/packing.py:24-54, :109-150,
     :314-349, :395-415) and the FP8 pair `_fp8_partial_amax` /
-    `_fp8_scale_and_cast` of `prepare_fp8` (packing.py:451-519).
+    `_fp8_scale_and_cast` of `prepare_fp8` (packing.py:451-519);
+  * the FP8 producers: `_swiglu_pack`, `_gelu_pack` (with SmoothQuant),
+    `_rmsnorm_pack` and `_norm_modulation_pack` (residual + LayerNorm +
+    AdaLN) with their FP8 store (FP4=False: bf16 values and row maxima,
+    `_store_producer` :57-82), then `_fp8_scale_and_cast` over the row
+    maxima as `_finish_producer` launches it (packing.py:180-199).
 
 The Triton kernels run under Triton's CPU interpreter (TRITON_INTERPRET=1).
 Two interpreter emulation gaps are closed first, so that the CPU run has the
@@ -248,6 +253,72 @@ def floating_cases(out):
     )
 
 
+def fp8_producer_cases(out):
+    """FP8 producers, first pass then `_fp8_scale_and_cast` with PARTS = rows
+    (packing.py:180-199), seeded apart from the other cases.  Keys fp8p_*:
+    inputs, the bf16 values, row maxima, E4M3 codes and the scale."""
+    g = torch.Generator().manual_seed(2)
+
+    def finish(name, output, auxiliary):
+        rows = output.shape[0]
+        packed = torch.zeros(output.shape, dtype=torch.float8_e4m3fn)
+        scale = torch.zeros((), dtype=torch.float32)
+        ref_packing._fp8_scale_and_cast[(triton.cdiv(output.numel(), 4096),)](
+            output, auxiliary, packed, scale, output.numel(), rows, triton.next_power_of_2(rows), 4096
+        )
+        out[f"fp8p_{name}_values"] = bits(output)
+        out[f"fp8p_{name}_rowmax"] = auxiliary.numpy().copy()
+        out[f"fp8p_{name}_q"] = packed.view(torch.uint8).numpy().copy()
+        out[f"fp8p_{name}_s"] = scale.numpy().copy()
+
+    # SwiGLU (17 DiT-like rows, K = 256) with one +inf gate: its value is left
+    # out of the maxima and clamps to 448 in the codes.
+    rows, k = 17, 256
+    gate = torch.randn(rows, k, generator=g)
+    gate[3, 5] = float("inf")
+    gate = gate.to(torch.bfloat16)
+    up = (torch.randn(rows, k, generator=g) * 2.0).to(torch.bfloat16)
+    output = torch.zeros((rows, k), dtype=torch.bfloat16)
+    auxiliary = torch.zeros(rows, dtype=torch.float32)
+    ref_packing._swiglu_pack[(rows,)](gate, up, silu_lut(), output, auxiliary, None, k, k, k,
+                                      triton.next_power_of_2(k), False, False)
+    out["fp8p_swiglu_gate"], out["fp8p_swiglu_up"] = bits(gate), bits(up)
+    finish("swiglu", output, auxiliary)
+    # GELU (tanh) with SmoothQuant channel division, K = 384.
+    rows, k = 9, 384
+    x = outliers(g, rows, k)
+    smooth = (0.5 + 1.5 * torch.rand(k, generator=g)).to(torch.float32)
+    output = torch.zeros((rows, k), dtype=torch.bfloat16)
+    auxiliary = torch.zeros(rows, dtype=torch.float32)
+    ref_packing._gelu_pack[(rows,)](x, gelu_lut("tanh"), output, auxiliary, smooth, k,
+                                    triton.next_power_of_2(k), False, True)
+    out["fp8p_gelu_x"], out["fp8p_gelu_smooth"] = bits(x), smooth.numpy().copy()
+    finish("gelu", output, auxiliary)
+    # RMSNorm (VLM width).
+    xr = outliers(g, 6, 2048)
+    gamma = (1.0 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    output = torch.zeros((6, 2048), dtype=torch.bfloat16)
+    auxiliary = torch.zeros(6, dtype=torch.float32)
+    ref_packing._rmsnorm_pack[(6,)](xr, gamma, output, auxiliary, None, 2048, 1e-6, 2048, False, False)
+    out["fp8p_rms_x"], out["fp8p_rms_gamma"] = bits(xr), bits(gamma)
+    finish("rms", output, auxiliary)
+    # Residual add + LayerNorm + per-batch AdaLN (DiT shape).
+    b, t, d = 2, 17, 1536
+    xl = torch.randn(b, t, d, generator=g).to(torch.bfloat16)
+    yl = torch.randn(b, t, d, generator=g).to(torch.bfloat16)
+    scale = (torch.randn(b, d, generator=g) * 0.5).to(torch.bfloat16)
+    shift = (torch.randn(b, d, generator=g) * 0.5).to(torch.bfloat16)
+    summed = torch.zeros_like(xl)
+    output = torch.zeros((b * t, d), dtype=torch.bfloat16)
+    auxiliary = torch.zeros(b * t, dtype=torch.float32)
+    ref_packing._norm_modulation_pack[(b * t,)](
+        xl, scale, shift, yl, summed, output, auxiliary, None, d, t, d, d, 1e-6, 2048, True, True, False, False
+    )
+    out.update(fp8p_ln_x=bits(xl), fp8p_ln_y=bits(yl), fp8p_ln_scale=bits(scale), fp8p_ln_shift=bits(shift),
+               fp8p_ln_summed=bits(summed))
+    finish("ln", output, auxiliary)
+
+
 def main():
     g = torch.Generator().manual_seed(0)
     out = {}
@@ -356,6 +427,7 @@ def main():
         out[f"lin_ws_b{b}"] = ws_.detach().numpy().copy()
 
     floating_cases(out)
+    fp8_producer_cases(out)
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT}: {len(out)} arrays, {os.path.getsize(OUT)} bytes")
 

@@ -50,7 +50,12 @@ def _rel_l2(a, b):
 
 def _fused(precision):
     if precision in ("fp4", "fp8"):
-        return OptimizationConfig(precision=precision, scope="all")
+        # Every floating producer (SwiGLU, GELU, RMSNorm, DiT norm/residual),
+        # shared packs: the configuration bench.py times.
+        return OptimizationConfig(
+            precision=precision, scope="all", fp_shared_inputs=True, fp_swiglu=True, fp_gelu=True,
+            fp_rmsnorm=True, fusion=True, norm_modulation_quant=True, residual_norm_quant=True,
+        )
     return OptimizationConfig(
         precision=precision, fusion=True, scope="all", group_conditioning=True,
         norm_modulation_quant=True, residual_norm_quant=True,

@@ -1,6 +1,6 @@
 """FP8 (E4M3, per-tensor) path on the B200 kernels: the quantizer's codes
 and scale are bitwise the oracle's (both reference variants), the tcgen05
-kind::f8f6f4 GEMM matches the oracle's fp64 sum of dequantized products to
+kind::f8f6f4 GEMM and the few-token e4m3 GEMM (at most 32 rows) match the oracle's fp64 sum of dequantized products to
 one bf16 rounding step (rtol 2^-7) plus atol 1e-3 for fp32 accumulation
 order, and FloatingLinear(precision="fp8") equals quantizer + GEMM."""
 
@@ -33,6 +33,25 @@ def test_quant_fp8_codes_and_scale_equal_oracle(rows, k, fast):
     assert _lib.device_status() == 0
 
 
+@pytest.mark.parametrize("rows,k", [(1, 1536), (17, 6144), (544, 2048), (2000, 8192)])
+@pytest.mark.parametrize("fast", [False, True])
+def test_quant_fp8_two_pass_equals_cluster_quantizer(rows, k, fast):
+    """Activations take the two-launch quantizer (row maxima, then scale and
+    cast), weights the one-launch cluster kernel: same codes and scale, also
+    for rows that are a strided view."""
+    g = torch.Generator().manual_seed(rows + k)
+    x = (torch.randn(rows, k + 64, generator=g) * 3).to(torch.bfloat16).cuda()
+    x[rows // 2, 7] = float("inf")
+    view = x[:, :k]
+    q1, s1, r1 = ops.quant_fp8(view, fast=fast)
+    q2, s2, _ = ops.quant_fp8(view.contiguous(), fast=fast, weights=True)
+    assert torch.equal(s1, s2) and torch.equal(q1, q2)
+    assert torch.equal(r1, s1.expand(rows))
+    want_q, want_s = oracle.quant_fp8(bits_of(view), fast=fast)
+    assert np.float32(s1.item()) == want_s and np.array_equal(q1.cpu().numpy(), want_q)
+    assert _lib.device_status() == 0
+
+
 @pytest.mark.parametrize(
     "m,k,n",
     [(1, 2048, 4096), (17, 1536, 1536), (64, 1024, 2048), (300, 1536, 640), (544, 2048, 4096)],
@@ -51,6 +70,50 @@ def test_gemm_fp8_matches_dequantized_product(m, k, n, with_bias):
                            None if bias is None else bits_of(bias))
     got = out.float().cpu().numpy()
     np.testing.assert_allclose(got, want, rtol=2 ** -7, atol=1e-3)
+    assert _lib.device_status() == 0
+
+
+@pytest.fixture
+def few_mode():
+    """Sets the few-token kernel override for one test and restores it."""
+    previous = []
+
+    def set_mode(mode):
+        previous.append(_lib.set_few_mode(mode))
+
+    yield set_mode
+    if previous:
+        _lib.set_few_mode(previous[0])
+
+
+@pytest.mark.parametrize(
+    "m,k,n",
+    [(1, 1536, 1536), (5, 128, 1032), (9, 2048, 2048), (17, 1536, 6144), (17, 6144, 1536), (24, 4096, 640),
+     (32, 2048, 4096)],
+)
+@pytest.mark.parametrize("few", [True, False])
+def test_gemm_fp8_few_rows_both_kernels(m, k, n, few, few_mode):
+    """At most 32 token rows: the few-token kernel (warp-level e4m3 MMAs,
+    fp32 partials added in warp order) and the tcgen05 kernel both match the
+    fp64 dequantized product within the FP8 tolerance, with bias and the
+    residual epilogue; each is deterministic (two launches, equal bits)."""
+    few_mode(0 if few else 2)
+    g = torch.Generator().manual_seed(m * 7 + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    qa, sa, sa_rows = ops.quant_fp8(x.cuda())
+    qw, sw, sw_cols = ops.quant_fp8(w.cuda(), replicate=n, weights=True)
+    out = ops.gemm_fp8(qa, sa_rows, qw, sw_cols, bias.cuda(), n=n)
+    again = ops.gemm_fp8(qa, sa_rows, qw, sw_cols, bias.cuda(), n=n)
+    with_res = ops.gemm_fp8(qa, sa_rows, qw, sw_cols, bias.cuda(), n=n, residual=res.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
+    want = oracle.fp8_gemm(qa.cpu().numpy(), sa.item(), qw.cpu().numpy(), sw.item(), bits_of(bias))
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=2 ** -7, atol=1e-3)
+    # The residual epilogue adds the bf16 result and the bf16 residual in fp32.
+    assert torch.equal(with_res.cpu(), (out.cpu().float() + res.float()).to(torch.bfloat16))
     assert _lib.device_status() == 0
 
 

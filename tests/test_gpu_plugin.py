@@ -354,19 +354,46 @@ def test_text_attention_causal_kernel_matches_sdpa_path_and_restores():
     assert _lib.device_status() == 0
 
 
-@pytest.mark.parametrize("flags", [{"fp_grouped": True}, {"fp_rmsnorm": True}, {"fusion": True}])
+@pytest.mark.parametrize("precision", ["fp8", "fp4"])
+@pytest.mark.parametrize("grouped", [False, True])
 @torch.inference_mode()
-def test_fp4_session_refuses_unimplemented_floating_fusions(flags):
+def test_floating_session_installs_producers(precision, grouped):
+    """The floating session with every producer piR2 wires for fp8 / fp4
+    (coexecution/optimization/groot/floating.py:162-346 and
+    floating_connections.py): shared-input or merged (grouped) projections,
+    SwiGLU, GELU and RMSNorm producers, the DiT LayerNorm + AdaLN and
+    residual + LayerNorm producers.  Every site is covered, the actions stay
+    close to the unfused floating session's, and closing restores every
+    module."""
     from pir2_b200.config import OptimizationConfig
-    from pir2_b200.harness import DiTConfig, VLMConfig, build_policy
+    from pir2_b200.harness import DiTConfig, VLMConfig, build_policy, synthetic_inputs
     from pir2_b200.session import GrootOptimizations
 
-    policy = build_policy("cuda", dit=DiTConfig(layers=2), vlm=VLMConfig(layers=1, vocab=2048))
-    try:
-        config = OptimizationConfig(precision="fp4", scope="all", **flags)
-    except ValueError:
-        return  # refused by the config validation itself
-    with pytest.raises(ValueError, match="fp4|Floating"):
-        with GrootOptimizations(SimpleNamespace(model=policy), config):
-            pass
+    vlm, dit = VLMConfig(layers=2, vocab=2048), DiTConfig(layers=2)
+    policy = build_policy("cuda", dit=dit, vlm=vlm)
+    inputs = synthetic_inputs(1, "cuda", vlm=vlm, dit=dit)
+    bf16_actions = policy(*inputs)
+    with GrootOptimizations(SimpleNamespace(model=policy), OptimizationConfig(precision=precision, scope="all")):
+        plain = policy(*inputs)
+    config = OptimizationConfig(
+        precision=precision, scope="all", fp_shared_inputs=not grouped, fp_grouped=grouped, fp_swiglu=True,
+        fp_gelu=True, fp_rmsnorm=True, fusion=True, norm_modulation_quant=True, residual_norm_quant=True,
+    )
+    with GrootOptimizations(SimpleNamespace(model=policy), config) as session:
+        coverage = session.coverage["floating"]
+        assert len(coverage["swiglu_producers"]) == vlm.layers
+        assert len(coverage["rmsnorm_producers"]) == vlm.layers
+        assert len(coverage["gelu_producers"]) >= dit.layers
+        merged = coverage["merged_projection_groups" if grouped else "shared_input_groups"]
+        assert len(merged) >= 2 * vlm.layers
+        assert session.coverage["norm_quantization_fusion"]["attention_producers"] > 0
+        assert session.coverage["norm_quantization_fusion"]["residual_ffn_producers"] == dit.layers
+        fused = policy(*inputs)
+    assert torch.equal(policy(*inputs), bf16_actions)
     assert all("forward" not in m.__dict__ for m in policy.modules())
+    assert all("gelu" not in m.__dict__ for m in policy.modules())
+    assert torch.isfinite(fused).all()
+    rel = ((fused.float() - plain.float()).norm() / plain.float().norm()).item()
+    print(f"{precision} grouped={grouped}: fused producers vs unfused floating {rel:.3e}")
+    assert rel < (0.05 if precision == "fp8" else 0.15)
+    assert _lib.device_status() == 0

@@ -179,3 +179,45 @@ def test_fused_nvfp4_producers_match_reference():
     v = oq.modulate_values(oq.layer_norm_values(r, 1e-6), GOLDEN["fp4ln_scale"], GOLDEN["fp4ln_shift"], tokens)
     packed, sf = oq.pack_nvfp4(v)
     assert np.array_equal(packed, GOLDEN["fp4ln_packed"]) and np.array_equal(sf, GOLDEN["fp4ln_sf"])
+
+
+def _check_fp8_producer(name, values):
+    """Values, row maxima, E4M3 codes and scale of one FP8 producer case."""
+    assert np.array_equal(oracle.f32_to_bf16_bits(values), GOLDEN[f"fp8p_{name}_values"].reshape(values.shape))
+    rowmax = oracle.row_finite_max(values)
+    assert np.array_equal(rowmax.view(np.uint32), GOLDEN[f"fp8p_{name}_rowmax"].view(np.uint32))
+    q, scale = oracle.fp8_producer(values)
+    assert np.float32(scale).view(np.uint32) == GOLDEN[f"fp8p_{name}_s"].view(np.uint32)
+    assert np.array_equal(q, GOLDEN[f"fp8p_{name}_q"].reshape(q.shape))
+
+
+def test_fp8_lut_producers_match_reference():
+    """`_swiglu_pack` (one +inf gate: left out of the row maxima, clamped to
+    448 in the codes) and `_gelu_pack` with SmoothQuant division, to FP8
+    (thor/packing.py:84-107, :352-369, then `_fp8_scale_and_cast` over the
+    row maxima, :180-199): the oracle's values, maxima, codes and scale equal
+    the reference's bit for bit."""
+    v = oracle.floating_values(GOLDEN["fp8p_swiglu_gate"], lut_bits=GOLDEN["lut_silu"],
+                               up_bits=GOLDEN["fp8p_swiglu_up"])
+    _check_fp8_producer("swiglu", v)
+    v = oracle.floating_values(GOLDEN["fp8p_gelu_x"], lut_bits=GOLDEN["lut_gelu_tanh"],
+                               smooth=GOLDEN["fp8p_gelu_smooth"])
+    _check_fp8_producer("gelu", v)
+
+
+def test_fp8_norm_producers_match_reference():
+    """`_rmsnorm_pack` and `_norm_modulation_pack` (residual add + LayerNorm
+    + per-batch AdaLN) to FP8: the oracle's composition equals the
+    reference's values, maxima, codes, scale and residual sum on these
+    vectors (the variance sums differ in order, fp32 in the interpreter and
+    fp64 in the oracle; these inputs round alike)."""
+    from oracle import quant as oq
+
+    _check_fp8_producer("rms", oq.rms_norm_values(GOLDEN["fp8p_rms_x"], GOLDEN["fp8p_rms_gamma"], 1e-6))
+    tokens, d = 17, 1536
+    x = oq.bf16_bits_to_f32(GOLDEN["fp8p_ln_x"].reshape(-1, d))
+    y = oq.bf16_bits_to_f32(GOLDEN["fp8p_ln_y"].reshape(-1, d))
+    r = oq.bf16_round((x + y).astype(np.float32))
+    assert np.array_equal(oq.f32_to_bf16_bits(r), GOLDEN["fp8p_ln_summed"].reshape(-1, d))
+    v = oq.modulate_values(oq.layer_norm_values(r, 1e-6), GOLDEN["fp8p_ln_scale"], GOLDEN["fp8p_ln_shift"], tokens)
+    _check_fp8_producer("ln", v)
