@@ -103,29 +103,31 @@ int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
  * out_format PIR2B_OUT_NVFP4: q = packed E2M1 [rows, k/2], scales = the
  *   swizzled UE4M3 block-16 factors (layout of pir2b_pack_nvfp4), k % 32 == 0;
  * out_format PIR2B_OUT_FP8_VALUES: q = bf16 values [rows, k], scales = fp32
- *   [rows] maximum finite |value| per row, k % 16 == 0; pir2b_fp8_cast
- *   finishes the E4M3 pack (packing.py:180-199).  q may be NULL here: the
- *   row maxima alone, the first pass of a plain per-tensor quantization
- *   whose cast reads x in place.
+ *   [rows, ceil(k / 1024)] partial maxima of the finite |value| (each row in
+ *   slices of 1024 values), k % 16 == 0; pir2b_fp8_cast finishes the E4M3
+ *   pack (packing.py:180-199).  q may be NULL here: the maxima alone, the
+ *   first pass of a plain per-tensor quantization whose cast reads x in
+ *   place.
  * 16 <= k <= 8192; q 16-byte aligned. */
 int pir2b_floating_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
                         const void *lut, const float *smooth, int mode, int out_format,
                         int64_t rows, int64_t k, void *q, void *scales, void *stream);
 
 /* Second pass of the FP8 producers and of the two-pass per-tensor
- * quantizer: the scale from the row maxima of a PIR2B_OUT_FP8_VALUES pass
- * and the E4M3 cast,
+ * quantizer: the scale from the nmax partial maxima of the first pass (a
+ * PIR2B_OUT_FP8_VALUES pass, or the per-row maxima of a norm producer) and
+ * the E4M3 cast,
  *   coexecution/optimization/backends/thor/packing.py:180-199, :461-482
  *   (_finish_producer, _fp8_scale_and_cast), fast != 0:
- *     scale = max(max_r row_max[r] * (1/448), 1e-12);
+ *     scale = max(max_i maxima[i] * (1/448), 1e-12);
  *     q = e4m3(clamp(v / scale, +-448)) with round-to-nearest division;
  *   fp8_cutlass_linear.cu:61-120 (quantize_bf16), fast == 0:
  *     scale = max(amax / 448, 1e-12); q = e4m3(clamp(v * (1 / scale), +-448)).
  * v: bf16 rows of stride ldv (elements, % 8 == 0), k % 8 == 0; q: [rows, k]
  * bytes; the scale is written to scale[0] and to scale_rep[0..n_rep) (null
  * when n_rep == 0). */
-int pir2b_fp8_cast(const void *v, int64_t ldv, const float *row_max, int64_t rows, int64_t k, int fast,
-                   void *q, float *scale, float *scale_rep, int64_t n_rep, void *stream);
+int pir2b_fp8_cast(const void *v, int64_t ldv, const float *maxima, int64_t nmax, int64_t rows, int64_t k,
+                   int fast, void *q, float *scale, float *scale_rep, int64_t n_rep, void *stream);
 
 /* Fused norm (+ AdaLN modulation) (+ gated residual) + quantize/pack.
  * Replaces the Triton producers of

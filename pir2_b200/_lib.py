@@ -35,7 +35,7 @@ SIGNATURES = {
     "pir2b_wait_probe": [_P, _P],
     "pir2b_quant_rows": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _P, _P, _P],
     "pir2b_floating_rows": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _P, _P, _P],
-    "pir2b_fp8_cast": [_P, _I64, _P, _I64, _I64, _I, _P, _P, _P, _I64, _P],
+    "pir2b_fp8_cast": [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _P, _P, _I64, _P],
     "pir2b_norm_quant_rows": [
         _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I, _F, _I, _I64, _I64, _P, _P, _P,
     ],

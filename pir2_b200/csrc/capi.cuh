@@ -97,7 +97,9 @@ static int device_info(DeviceInfo **out) {
         reinterpret_cast<const void *>(gemm_i8_kernel<9, false>),
         reinterpret_cast<const void *>(gemm_i8_kernel<9, true>),
         reinterpret_cast<const void *>(gemm_pair_kernel<1>),
-        reinterpret_cast<const void *>(gemm_pair_kernel<2>)};
+        reinterpret_cast<const void *>(gemm_pair_kernel<2>),
+        reinterpret_cast<const void *>(gemm_pair_kernel<1, true>),
+        reinterpret_cast<const void *>(gemm_pair_kernel<2, true>)};
     e = cudaSuccess;
     for (const void *f : gemms)
       if (e == cudaSuccess)
@@ -713,8 +715,8 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
   // the output rows are 16-byte aligned; otherwise it stores directly.
   args.tma_store = tma_out(out, ldo) ? 1 : 0;
   // The 2-SM kernel stores through TMA only and has no split-K or fused pack.
-  if (plan.pair && (!args.tma_store || bits != 8 || fin != nullptr || plan.splits != 1 ||
-                    plan.bn % kPairGroup != 0 || (silu_lut != nullptr && plan.wt != 2)))
+  if (plan.pair && (!args.tma_store || (bits != 8 && bits != 9) || fin != nullptr || plan.splits != 1 ||
+                    plan.bn % kPairGroup != 0 || (silu_lut != nullptr && (plan.wt != 2 || bits != 8))))
     return fail(PIR2B_EINVAL, "internal: 2-SM GEMM plan on an unsupported call (bn=%d wt=%d)",
                 plan.bn, plan.wt);
   CUtensorMap tm_out;
@@ -755,8 +757,13 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
     cfg.blockDim = dim3(kPairThreads, 1, 1);
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.z = 1;
-    const cudaError_t e = plan.wt == 2 ? cudaLaunchKernelEx(&cfg, gemm_pair_kernel<2>, tm_w, tm_a, tm_out, args)
-                                       : cudaLaunchKernelEx(&cfg, gemm_pair_kernel<1>, tm_w, tm_a, tm_out, args);
+    cudaError_t e;
+    if (bits == 9)
+      e = plan.wt == 2 ? cudaLaunchKernelEx(&cfg, gemm_pair_kernel<2, true>, tm_w, tm_a, tm_out, args)
+                       : cudaLaunchKernelEx(&cfg, gemm_pair_kernel<1, true>, tm_w, tm_a, tm_out, args);
+    else
+      e = plan.wt == 2 ? cudaLaunchKernelEx(&cfg, gemm_pair_kernel<2>, tm_w, tm_a, tm_out, args)
+                       : cudaLaunchKernelEx(&cfg, gemm_pair_kernel<1>, tm_w, tm_a, tm_out, args);
     return cuda_status(e, "gemm (2-SM) launch");
   }
   // Token tiles above 64 rows take the wide instantiation.
@@ -923,11 +930,13 @@ int pir2b_floating_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
                      "floating_rows launch");
 }
 
-int pir2b_fp8_cast(const void *v, int64_t ldv, const float *row_max, int64_t rows, int64_t k, int fast, void *q,
-                   float *scale, float *scale_rep, int64_t n_rep, void *stream) {
+int pir2b_fp8_cast(const void *v, int64_t ldv, const float *maxima, int64_t nmax, int64_t rows, int64_t k,
+                   int fast, void *q, float *scale, float *scale_rep, int64_t n_rep, void *stream) {
   if (rows < 1 || k < 8 || k % 8 != 0 || k > (1 << 20) || rows > (int64_t(1) << 33) / k || n_rep < 0 ||
-      ldv < k || ldv % 8 != 0)
-    return fail(PIR2B_EINVAL, "fp8_cast needs rows >= 1, k %% 8 == 0, ldv >= k, ldv %% 8 == 0 and n_rep >= 0");
+      ldv < k || ldv % 8 != 0 || nmax < 1 || nmax > (int64_t(1) << 30))
+    return fail(PIR2B_EINVAL,
+                "fp8_cast needs rows >= 1, k %% 8 == 0, ldv >= k, ldv %% 8 == 0, nmax >= 1 and n_rep >= 0");
+  const float *row_max = maxima;
   if (v == nullptr || row_max == nullptr || q == nullptr || scale == nullptr ||
       (n_rep > 0 && scale_rep == nullptr))
     return fail(PIR2B_EINVAL, "fp8_cast operands must be non-null");
@@ -941,6 +950,7 @@ int pir2b_fp8_cast(const void *v, int64_t ldv, const float *row_max, int64_t row
   a.v = static_cast<const __nv_bfloat16 *>(v);
   a.ldv = ldv;
   a.row_max = row_max;
+  a.nmax = nmax;
   a.rows = rows;
   a.k = int(k);
   a.fast = fast ? 1 : 0;
@@ -1443,8 +1453,9 @@ int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float 
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
-  // E4M3 operands have the int8 byte layout: the same tile plans.
-  const GemmPlan plan = plan_gemm(8, m, npad, kpad, dev->sms, dev->max_smem);
+  // E4M3 operands have the int8 byte layout: the same tile plans, 2-SM
+  // tiles included (kind::f8f6f4 on cta_group::2).
+  const GemmPlan plan = plan_gemm(8, m, npad, kpad, dev->sms, dev->max_smem, tma_out(out, ldo));
   if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m || plan.stages < 2 ||
       plan.smem > size_t(dev->max_smem))
     return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",

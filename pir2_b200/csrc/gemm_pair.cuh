@@ -57,6 +57,18 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uin
       : "memory");
 }
 
+// E4M3 x E4M3 -> fp32 on 2-SM tiles (kind::f8f6f4, the operand layout of
+// kind::i8).
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on `bar` (same offset) in both CTAs of the pair when the
 // pair's previously issued tcgen05 operations have completed.
 __device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
@@ -114,7 +126,9 @@ constexpr int kPairStagingBytes = 2 * kPairGroup * kTileN * 2;
 // multiply (each lane one IEEE round-to-nearest step).  The bias add stays
 // scalar __fadd_rn: a packed __fadd2_rn after the packed multiply was
 // contracted into a fused multiply-add (single rounding), which moved
-// values that sit exactly on a bf16 rounding tie by one unit.
+// values that sit exactly on a bf16 rounding tie by one unit.  kF8: the
+// accumulator words are fp32 sums (E4M3), else exact int32 sums.
+template <bool kF8>
 __device__ __forceinline__ void pair_values(const uint32_t (&r)[16], const float *s_sa, int j0, float sw,
                                             float b, int bias_mode, __nv_bfloat162 (&o)[8]) {
   const float4 *sa4 = reinterpret_cast<const float4 *>(s_sa + j0);
@@ -122,8 +136,8 @@ __device__ __forceinline__ void pair_values(const uint32_t (&r)[16], const float
   for (int q = 0; q < 4; ++q) {
     const float4 sa = sa4[q];
     const float2 s01 = make_float2(sa.x, sa.y), s23 = make_float2(sa.z, sa.w);
-    float2 y0 = make_float2(__int2float_rn(int(r[4 * q])), __int2float_rn(int(r[4 * q + 1])));
-    float2 y1 = make_float2(__int2float_rn(int(r[4 * q + 2])), __int2float_rn(int(r[4 * q + 3])));
+    float2 y0 = make_float2(acc_value<kF8>(r[4 * q]), acc_value<kF8>(r[4 * q + 1]));
+    float2 y1 = make_float2(acc_value<kF8>(r[4 * q + 2]), acc_value<kF8>(r[4 * q + 3]));
     y0 = __fmul2_rn(__fmul2_rn(y0, s01), make_float2(sw, sw));
     y1 = __fmul2_rn(__fmul2_rn(y1, s23), make_float2(sw, sw));
     if (bias_mode != 0) {
@@ -140,8 +154,9 @@ __device__ __forceinline__ void pair_values(const uint32_t (&r)[16], const float
 // runs on across tiles; TMEM holds two accumulator sets when a tile needs
 // at most 256 columns (kWt x BN), so the MMAs of the next tile run while
 // the epilogue drains the previous one, else one set that the MMA warp
-// reuses once both CTAs' epilogues have read it.
-template <int kWt>
+// reuses once both CTAs' epilogues have read it.  kF8: E4M3 operands
+// (kind::f8f6f4) with fp32 accumulators, no SwiGLU epilogue.
+template <int kWt, bool kF8 = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_out, const GemmArgs args) {
@@ -253,7 +268,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue (even CTA)
     if (leader && elect_one_sync()) {
-      const uint32_t idesc = idesc_i8(2 * kTileN, uint32_t(bn));
+      const uint32_t idesc = kF8 ? idesc_f8(2 * kTileN, uint32_t(bn)) : idesc_i8(2 * kTileN, uint32_t(bn));
       uint32_t kbg = 0;
       int it = 0;
       bool ok = true;
@@ -276,9 +291,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           for (int k = 0; k < kBlockK / 32; ++k) {
             const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
 #pragma unroll
-            for (int w = 0; w < kWt; ++w)
-              mma_i8_pair(d + uint32_t(w) * acc_cols, smem_desc_sw128(a_addr + w * kWeightTileBytes + k * 32),
-                          smem_desc_sw128(b_addr + k * 32), idesc, acc);
+            for (int w = 0; w < kWt; ++w) {
+              if constexpr (kF8)
+                mma_f8_pair(d + uint32_t(w) * acc_cols, smem_desc_sw128(a_addr + w * kWeightTileBytes + k * 32),
+                            smem_desc_sw128(b_addr + k * 32), idesc, acc);
+              else
+                mma_i8_pair(d + uint32_t(w) * acc_cols, smem_desc_sw128(a_addr + w * kWeightTileBytes + k * 32),
+                            smem_desc_sw128(b_addr + k * 32), idesc, acc);
+            }
           }
           mma_commit_pair(&empty[s]);
         }
@@ -363,8 +383,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             auto gated = [&](int k, const uint32_t (&rg)[16], const uint32_t (&ru)[16]) {
               const int j0 = k * 16;
               __nv_bfloat162 gv[8], uv[8];
-              pair_values(rg, s_sa, j0, sw[0], bias[0], bias_mode, gv);
-              pair_values(ru, s_sa, j0, sw[kWt - 1], bias[kWt - 1], bias_mode, uv);
+              pair_values<kF8>(rg, s_sa, j0, sw[0], bias[0], bias_mode, gv);
+              pair_values<kF8>(ru, s_sa, j0, sw[kWt - 1], bias[kWt - 1], bias_mode, uv);
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 const float2 sg = make_float2(
@@ -392,7 +412,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                                : 0.f;
               }
               __nv_bfloat162 o[8];
-              pair_values(r, s_sa, j0, sw[w], bias[w], bias_mode, o);
+              pair_values<kF8>(r, s_sa, j0, sw[w], bias[w], bias_mode, o);
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 uint16_t lo = __bfloat16_as_ushort(o[q].x), hi = __bfloat16_as_ushort(o[q].y);

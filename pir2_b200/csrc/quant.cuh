@@ -191,13 +191,13 @@ __device__ __forceinline__ void store_nvfp4_chunk(const float (&v)[8],
 }
 
 // Stores a thread's chunks of a row (values already bf16-exact) as bf16:
-// chunk c = threadIdx.x + j * blockDim.x covers columns [8c, 8c + 8).
+// chunk c = cbase + threadIdx.x + j * blockDim.x covers columns [8c, 8c + 8).
 template <int kCpt>
 __device__ __forceinline__ void store_bf16_row(const float (&v)[kCpt][8], __nv_bfloat16 *out, int k,
-                                               int nchunks) {
+                                               int nchunks, int cbase = 0) {
 #pragma unroll
   for (int j = 0; j < kCpt; ++j) {
-    const int chunk = threadIdx.x + j * blockDim.x;
+    const int chunk = cbase + threadIdx.x + j * blockDim.x;
     if (chunk < nchunks && chunk * 8 < k) {
       uint4 raw;
       __nv_bfloat16 *p = reinterpret_cast<__nv_bfloat16 *>(&raw);
@@ -213,9 +213,12 @@ __device__ __forceinline__ void store_bf16_row(const float (&v)[kCpt][8], __nv_b
 // integer.py:27-94 (_activation_values, _prepare).  The same values (plain,
 // LUT activation, SiLU * up, SmoothQuant division) also go to the floating
 // outputs of the piR2 Thor producers (thor/packing.py:57-107, :314-369):
-// kBits 16 writes NVFP4 (store_nvfp4_chunk), kBits 32 the bf16 values and
-// the row's maximum finite |value| (the first pass of the FP8 producers,
-// whose second pass is fp8_cast_kernel).
+// kBits 16 writes NVFP4 (store_nvfp4_chunk); kBits 32 the bf16 values and
+// partial maxima of the finite |value| (the first pass of the FP8 producers,
+// whose second pass is fp8_cast_kernel).  An FP8 value needs no row
+// statistic, so a kBits 32 row is split over gridDim.y CTAs (blockIdx.y
+// takes the chunks from blockIdx.y * blockDim.x * kCpt) and each CTA writes
+// its own maximum, scales[row * gridDim.y + blockIdx.y].
 template <int kBits, int kCpt, bool kVec>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantArgs a) {
   __shared__ float red[32];
@@ -224,13 +227,14 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantArgs a) {
   pdl_launch_dependents();
   const int row = blockIdx.x;
   const int nchunks = a.kpad >> 3;
+  const int cbase = int(blockIdx.y) * int(blockDim.x) * kCpt;   // 0 unless kBits == 32
   const __nv_bfloat16 *xr = a.x + int64_t(row) * a.ldx;
   const __nv_bfloat16 *ur = a.up ? a.up + int64_t(row) * a.ldu : nullptr;
   float v[kCpt][8];
   float m = 0.f;
 #pragma unroll
   for (int j = 0; j < kCpt; ++j) {
-    const int chunk = threadIdx.x + j * blockDim.x;
+    const int chunk = cbase + threadIdx.x + j * blockDim.x;
     const int c0 = chunk * 8;
     __nv_bfloat16 xv[8];
     load8<kVec>(xr, chunk < nchunks ? c0 : a.k, a.k, xv);
@@ -271,11 +275,11 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantArgs a) {
   m = block_max(m, red);
   if constexpr (kBits == 32) {
     if (threadIdx.x == 0)
-      a.scales[row] = m;
-    // q == null: the row maxima alone (the plain FP8 activation quantizer,
+      a.scales[int64_t(row) * gridDim.y + blockIdx.y] = m;
+    // q == null: the maxima alone (the plain FP8 activation quantizer,
     // whose cast reads x in place).
     if (a.q != nullptr)
-      store_bf16_row(v, reinterpret_cast<__nv_bfloat16 *>(a.q) + int64_t(row) * a.k, a.k, nchunks);
+      store_bf16_row(v, reinterpret_cast<__nv_bfloat16 *>(a.q) + int64_t(row) * a.k, a.k, nchunks, cbase);
     return;
   }
   const float s = row_scale<kBits>(m);
@@ -703,12 +707,25 @@ cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
   const int nchunks = a.kpad / 8;
   // Floating outputs (NVFP4, FP8 first pass): rows of at most 8192 values
   // (1024 chunks) held in registers.
-  if (bits == 16 || bits == 32) {
+  if (bits == 16) {
     if (nchunks > 1024)
       return cudaErrorInvalidValue;
-    if (nchunks <= 256)
-      return bits == 16 ? launch_quant<16, 1>(a, rows, vec, st) : launch_quant<32, 1>(a, rows, vec, st);
-    return bits == 16 ? launch_quant<16, 4>(a, rows, vec, st) : launch_quant<32, 4>(a, rows, vec, st);
+    return nchunks <= 256 ? launch_quant<16, 1>(a, rows, vec, st) : launch_quant<16, 4>(a, rows, vec, st);
+  }
+  if (bits == 32) {
+    // One chunk per thread, 128 threads per CTA, fp8_value_splits(k) CTAs
+    // per row.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(rows), unsigned((nchunks + 127) / 128), 1);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return vec ? cudaLaunchKernelEx(&cfg, quant_rows_kernel<32, 1, true>, a)
+               : cudaLaunchKernelEx(&cfg, quant_rows_kernel<32, 1, false>, a);
   }
   // Few long rows: spread each row over a cluster of CTAs (<= 8, each with
   // 128 threads x 2 chunks) so the launch covers more of the 148 SMs.
@@ -943,8 +960,8 @@ cudaError_t run_fp8_quant(const Fp8QuantArgs &a, int ranks, cudaStream_t st) {
 
 // Second pass of the FP8 producers (thor/packing.py:180-199 with
 // _fp8_scale_and_cast, :461-482) and of the per-tensor activation quantizer:
-// the first pass wrote each row's maximum finite |value|; every CTA reduces
-// those maxima (one fp32 per row, a few KB) to the scale and casts its
+// the first pass wrote partial maxima of the finite |value| (a few per row);
+// every CTA reduces them (a few KB) to the scale and casts its
 // grid-stride share of 8-value chunks of v (rows of stride ldv):
 //  * fast (prepare_fp8 and the producers): scale = max(amax * (1/448),
 //    1e-12), q = e4m3_rn(clamp(v / scale, -448, 448)), IEEE division;
@@ -955,7 +972,8 @@ cudaError_t run_fp8_quant(const Fp8QuantArgs &a, int ranks, cudaStream_t st) {
 struct Fp8CastArgs {
   const __nv_bfloat16 *v;   // [rows, ldv]
   int64_t ldv;
-  const float *row_max;     // [rows]
+  const float *row_max;     // [nmax] partial maxima of the first pass
+  int64_t nmax;
   int64_t rows;
   int k;                    // k % 8 == 0
   int fast;
@@ -972,7 +990,7 @@ __global__ void __launch_bounds__(kFp8CastThreads) fp8_cast_kernel(const Fp8Cast
   pdl_wait();
   pdl_launch_dependents();
   float m = 0.f;
-  for (int64_t r = threadIdx.x; r < a.rows; r += kFp8CastThreads)
+  for (int64_t r = threadIdx.x; r < a.nmax; r += kFp8CastThreads)
     m = fmaxf(m, __ldg(a.row_max + r));
   m = block_max(m, red);
   const float scale = a.fast ? fmaxf(__fmul_rn(m, 1.0f / kFp8Max), kFp8MinScale)

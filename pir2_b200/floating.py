@@ -629,3 +629,58 @@ class FloatingConnections:
 
     def close(self):
         self._patches.restore()
+
+
+class FloatingTextFusion:
+    """Text decoder attention on the floating path with merged q|k|v
+    projections (fp_grouped): the input RMSNorm packs straight to the
+    floating format (the RMSNorm producer, as piR2's fp_rmsnorm does for the
+    MLP input), the merged q|k|v GEMM runs once, and one kernel applies
+    q_norm / k_norm, the rotary embedding and the [B, H, T, D] relayout
+    (`ops.qk_norm_rope`, the BF16 fusion piR2's operator fusion performs
+    with its own kernels, coexecution/fused_ops.py).  Layers whose q|k|v are
+    not one merged group keep their forward."""
+
+    def __init__(self, model, floating):
+        self.targets = []
+        by_q = {}
+        for _, members, group in floating.groups:
+            if isinstance(group, FloatingProjectionGroup) and len(members) == 3:
+                by_q[id(members[0])] = group
+        for layer in model.modules():
+            if type(layer).__name__ != "Qwen3VLTextDecoderLayer":
+                continue
+            attn = layer.self_attn
+            group = by_q.get(id(attn.q_proj))
+            if group is None or attn.head_dim != 128 or group.sizes != [
+                attn.heads * attn.head_dim, attn.kv_heads * attn.head_dim, attn.kv_heads * attn.head_dim
+            ]:
+                continue
+            if type(layer.input_layernorm).__name__ != "Qwen3VLTextRMSNorm":
+                continue
+            self.targets.append((layer, group, floating.input_smoothing(attn.q_proj)))
+        self.precision = floating.precision
+        self._patches = _Patches()
+
+    def set(self):
+        self.close()
+        precision = self.precision
+        for layer, group, smooth in self.targets:
+            norm, attn = layer.input_layernorm, layer.self_attn
+            self._patches.replace(norm, "forward", lambda x, norm=norm, smooth=smooth: prepare_rmsnorm_packed(
+                x.contiguous(), norm.weight, precision, eps=norm.variance_epsilon, smoothing_scale=smooth))
+
+            def forward(x, cos, sin, attn=attn, group=group):
+                b, t = x.shape[0], x.shape[1]
+                qkv = group.linear(x)
+                q, k, v = ops.qk_norm_rope(
+                    qkv.reshape(b * t, qkv.shape[-1]), attn.q_norm.weight, attn.k_norm.weight, cos, sin,
+                    tokens=t, hq=attn.heads, hk=attn.kv_heads, eps=attn.q_norm.variance_epsilon,
+                )
+                y = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+                return attn.o_proj(y.transpose(1, 2).reshape(b, t, attn.heads * attn.head_dim))
+
+            self._patches.replace(attn, "forward", forward)
+
+    def close(self):
+        self._patches.restore()

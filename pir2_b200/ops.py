@@ -84,24 +84,30 @@ def quant_rows(x, bits, *, lut=None, up=None, smooth=None, out=None):
     return data, scales
 
 
-def _floating_buffers(rows, k, out_format, device):
+def _floating_buffers(rows, k, out_format, device, maxima_per_row=1):
     """Outputs of a floating producer: NVFP4 (packed E2M1 [rows, k/2],
     swizzled UE4M3 factors) or the FP8 first pass (bf16 values [rows, k],
-    fp32 row maxima)."""
+    fp32 partial maxima, `maxima_per_row` per row)."""
     if out_format == _lib.OUT_NVFP4:
         data = torch.empty((rows, k // 2), device=device, dtype=torch.uint8)
         scales = torch.empty((-(-rows // 128) * 128, -(-(k // 16) // 4) * 4), device=device, dtype=torch.uint8)
     else:
         data = torch.empty((rows, k), device=device, dtype=torch.bfloat16)
-        scales = torch.empty(rows, device=device, dtype=torch.float32)
+        scales = torch.empty(rows * maxima_per_row, device=device, dtype=torch.float32)
     return data, scales
+
+
+def fp8_value_slices(k):
+    """Partial maxima per row of an FP8 first pass over rows of k values (one
+    per 1024-value slice)."""
+    return -(-k // 1024)
 
 
 def floating_rows(x, out_format, *, lut=None, up=None, smooth=None):
     """The activation values of `quant_rows` (plain, LUT, SiLU * up, / smooth)
     to a floating output: `_lib.OUT_NVFP4` -> (packed, swizzled factors);
-    `_lib.OUT_FP8_VALUES` -> (bf16 values, fp32 row maxima), finished by
-    `fp8_cast`."""
+    `_lib.OUT_FP8_VALUES` -> (bf16 values, fp32 partial maxima: one per row
+    and 1024-value slice), finished by `fp8_cast`."""
     if x.dtype != torch.bfloat16 or not x.is_cuda or x.stride(-1) != 1 or x.ndim < 2:
         raise ValueError("Expected CUDA BF16 rows with unit feature stride")
     matrix, rows, k, ldx = _rows(x)
@@ -113,7 +119,7 @@ def floating_rows(x, out_format, *, lut=None, up=None, smooth=None):
         _, _, _, ldu = _rows(up)
     if lut is not None and (lut.numel() != 65536 or lut.dtype != torch.bfloat16 or not lut.is_contiguous()):
         raise ValueError("Invalid activation lookup table")
-    data, scales = _floating_buffers(rows, k, out_format, x.device)
+    data, scales = _floating_buffers(rows, k, out_format, x.device, fp8_value_slices(k))
     status = _lib.lib().pir2b_floating_rows(
         x.data_ptr(), ldx, _ptr(up), ldu, _ptr(lut), _ptr(smooth), mode, out_format,
         rows, k, data.data_ptr(), scales.data_ptr(), _stream(x.device),
@@ -122,21 +128,21 @@ def floating_rows(x, out_format, *, lut=None, up=None, smooth=None):
     return data, scales
 
 
-def fp8_cast(values, row_max, *, replicate=None):
-    """Second pass of the FP8 producers: bf16 values [rows, k] and their row
-    maxima -> (E4M3 codes uint8 [rows, k], scale fp32 [1], the scale
-    replicated `replicate` times (default: once per row))."""
+def fp8_cast(values, maxima, *, replicate=None):
+    """Second pass of the FP8 producers: bf16 values [rows, k] and the first
+    pass's partial maxima -> (E4M3 codes uint8 [rows, k], scale fp32 [1], the
+    scale replicated `replicate` times (default: once per row))."""
     if values.dtype != torch.bfloat16 or not values.is_cuda or values.dim() != 2 or not values.is_contiguous():
         raise ValueError("fp8_cast needs contiguous CUDA bf16 [rows, k] values")
     rows, k = values.shape
-    if row_max.dtype != torch.float32 or row_max.numel() != rows or not row_max.is_contiguous():
-        raise ValueError("fp8_cast needs one fp32 maximum per row")
+    if maxima.dtype != torch.float32 or maxima.numel() < 1 or not maxima.is_contiguous():
+        raise ValueError("fp8_cast needs the fp32 partial maxima of the first pass")
     n_rep = rows if replicate is None else int(replicate)
     q = torch.empty((rows, k), device=values.device, dtype=torch.uint8)
     scale = torch.empty(1, device=values.device, dtype=torch.float32)
     rep = torch.empty(max(n_rep, 1), device=values.device, dtype=torch.float32)
     status = _lib.lib().pir2b_fp8_cast(
-        values.data_ptr(), k, row_max.data_ptr(), rows, k, 1, q.data_ptr(), scale.data_ptr(),
+        values.data_ptr(), k, maxima.data_ptr(), maxima.numel(), rows, k, 1, q.data_ptr(), scale.data_ptr(),
         rep.data_ptr() if n_rep > 0 else None, n_rep, _stream(values.device),
     )
     _lib.check(status, "pir2b_fp8_cast")
@@ -466,8 +472,8 @@ def attention_causal(q, k, v, *, scale=None, out=None):
 
 def quant_fp8(x, *, fast=False, replicate=None, weights=False):
     """Per-tensor E4M3 quantization of bf16 rows x [rows, k] (k % 8 == 0):
-    activations with k % 16 == 0 and k <= 8192 in two launches (row maxima,
-    then scale and cast), weights and other widths in the one-launch
+    activations with k % 16 == 0 and k <= 8192 in two launches (partial
+    maxima, then scale and cast), weights and other widths in the one-launch
     cluster quantizer; both give the same bits.
 
     Returns (codes uint8 [rows, k], scale fp32 [1], replicated fp32
@@ -489,14 +495,15 @@ def quant_fp8(x, *, fast=False, replicate=None, weights=False):
     if not weights and k % 16 == 0 and k <= 8192 and ldx % 8 == 0 and x.data_ptr() % 16 == 0:
         # Activations: two parallel launches, one CTA per row for the row
         # maxima, then the grid-wide scale and cast reading x in place.
-        row_max = torch.empty(rows, device=x.device, dtype=torch.float32)
+        row_max = torch.empty(rows * fp8_value_slices(k), device=x.device, dtype=torch.float32)
         status = _lib.lib().pir2b_floating_rows(
             x.data_ptr(), ldx, None, 0, None, None, _lib.MODE_PLAIN, _lib.OUT_FP8_VALUES, rows, k, None,
             row_max.data_ptr(), _stream(x.device),
         )
         _lib.check(status, "pir2b_floating_rows")
         status = _lib.lib().pir2b_fp8_cast(
-            x.data_ptr(), ldx, row_max.data_ptr(), rows, k, 1 if fast else 0, q.data_ptr(), scale.data_ptr(),
+            x.data_ptr(), ldx, row_max.data_ptr(), row_max.numel(), rows, k, 1 if fast else 0, q.data_ptr(),
+            scale.data_ptr(),
             rep.data_ptr() if n_rep > 0 else None, n_rep, _stream(x.device),
         )
         _lib.check(status, "pir2b_fp8_cast")

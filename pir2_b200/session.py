@@ -163,6 +163,13 @@ class GrootOptimizations:
                     "attention_producers": len(connections.norms),
                     "residual_ffn_producers": len(connections.blocks),
                 }
+            if self.config.fusion and self.config.fusion_mode in ("all", "rope_rms"):
+                from .floating import FloatingTextFusion
+
+                self.pointwise = FloatingTextFusion(model, self.floating)
+                self.stack.callback(self.pointwise.close)
+                self.pointwise.set()
+                self.coverage["text_attention_fusion"] = len(self.pointwise.targets)
             if self.config.fusion and self.config.fusion_mode == "all":
                 from .pointwise import DiTAttentionFusion
 

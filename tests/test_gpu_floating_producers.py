@@ -45,7 +45,9 @@ def assert_fp8_stage(values, row_max, q, scale, rows):
     """The cast stage of the kernel's own values equals the oracle's; `rows`
     is the replicated scale vector fp8_cast wrote."""
     v = oracle.bf16_bits_to_f32(bits_of(values))
-    assert np.array_equal(row_max.cpu().numpy().view(np.uint32), oracle.row_finite_max(v).view(np.uint32))
+    # Partial maxima: one per row and 1024-value slice (norm producers: one per row).
+    per_row = row_max.cpu().numpy().reshape(v.shape[0], -1).max(axis=1)
+    assert np.array_equal(per_row.view(np.uint32), oracle.row_finite_max(v).view(np.uint32))
     want_q, want_s = oracle.fp8_producer(v)
     assert np.float32(scale.item()) == want_s
     assert torch.equal(rows, torch.full_like(rows, float(want_s)))
@@ -71,7 +73,8 @@ def test_fp8_lut_producers_equal_reference_golden(name):
     q, scale, rep = ops.fp8_cast(values, row_max)
     torch.cuda.synchronize()
     assert np.array_equal(bits_of(values), GOLDEN[f"fp8p_{name}_values"].reshape(rows, k))
-    assert np.array_equal(row_max.cpu().numpy().view(np.uint32), GOLDEN[f"fp8p_{name}_rowmax"].view(np.uint32))
+    per_row = row_max.cpu().numpy().reshape(rows, -1).max(axis=1)
+    assert np.array_equal(per_row.view(np.uint32), GOLDEN[f"fp8p_{name}_rowmax"].view(np.uint32))
     assert np.array_equal(q.cpu().numpy(), GOLDEN[f"fp8p_{name}_q"].reshape(rows, k))
     assert np.float32(scale.item()).view(np.uint32) == GOLDEN[f"fp8p_{name}_s"].view(np.uint32)
     assert torch.equal(rep, torch.full_like(rep, scale.item()))

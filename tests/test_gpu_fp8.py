@@ -117,6 +117,32 @@ def test_gemm_fp8_few_rows_both_kernels(m, k, n, few, few_mode):
     assert _lib.device_status() == 0
 
 
+@pytest.mark.parametrize("m,k,n", [(544, 2048, 4096), (544, 6144, 2048), (1088, 2048, 12288), (4352, 2048, 4096)])
+@pytest.mark.parametrize("pair", [1, 2])
+def test_gemm_fp8_many_rows_on_two_sm_tiles(m, k, n, pair):
+    """Many token rows: the 2-SM tile kernel on kind::f8f6f4 (pair mode 1
+    forces it where it applies) and the one-SM kernel (mode 2) both match
+    the fp64 dequantized product, with bias and the residual epilogue."""
+    previous = _lib.set_pair_mode(pair)
+    try:
+        g = torch.Generator().manual_seed(m + k + n + pair)
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+        bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+        res = torch.randn(m, n, generator=g).to(torch.bfloat16)
+        qa, sa, sa_rows = ops.quant_fp8(x.cuda())
+        qw, sw, sw_cols = ops.quant_fp8(w.cuda(), replicate=n, weights=True)
+        out = ops.gemm_fp8(qa, sa_rows, qw, sw_cols, bias.cuda(), n=n)
+        with_res = ops.gemm_fp8(qa, sa_rows, qw, sw_cols, bias.cuda(), n=n, residual=res.cuda())
+        torch.cuda.synchronize()
+        want = oracle.fp8_gemm(qa.cpu().numpy(), sa.item(), qw.cpu().numpy(), sw.item(), bits_of(bias))
+        np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=2 ** -7, atol=1e-3)
+        assert torch.equal(with_res.cpu(), (out.cpu().float() + res.float()).to(torch.bfloat16))
+    finally:
+        _lib.set_pair_mode(previous)
+    assert _lib.device_status() == 0
+
+
 def test_gemm_fp8_residual_and_floating_linear():
     from pir2_b200.floating import FloatingLinear
 

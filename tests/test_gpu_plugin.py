@@ -388,6 +388,8 @@ def test_floating_session_installs_producers(precision, grouped):
         assert len(merged) >= 2 * vlm.layers
         assert session.coverage["norm_quantization_fusion"]["attention_producers"] > 0
         assert session.coverage["norm_quantization_fusion"]["residual_ffn_producers"] == dit.layers
+        # Merged q|k|v: RMSNorm producer + fused q/k norm and RoPE on every text layer.
+        assert session.coverage["text_attention_fusion"] == (vlm.layers if grouped else 0)
         fused = policy(*inputs)
     assert torch.equal(policy(*inputs), bf16_actions)
     assert all("forward" not in m.__dict__ for m in policy.modules())
