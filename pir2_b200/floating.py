@@ -304,21 +304,27 @@ class FloatingLinear(torch.nn.Module):
             return q, rows
         return ops.pack_nvfp4(matrix)
 
-    def forward_packed(self, packed, scale, leading_shape):
+    def forward_packed(self, packed, scale, leading_shape, residual=None):
+        """The GEMM of packed input; `residual` (bf16, the output's shape) is
+        added as bf16(y + residual) in fp32, in the E4M3 GEMM's epilogue (the
+        NVFP4 GEMM has none: a separate add, the same arithmetic)."""
         if self.precision == "fp8":
+            res = None if residual is None else residual.reshape(-1, self.out_features)
+            if res is not None and res.stride(-1) != 1:
+                res = res.contiguous()
             result = ops.gemm_fp8(
-                packed, scale, self.packed_weight, self.weight_scale_columns, self.bias, n=self.out_features
+                packed, scale, self.packed_weight, self.weight_scale_columns, self.bias, n=self.out_features,
+                residual=res,
             )
-        else:
-            result = ops.gemm_nvfp4(
-                packed, scale, self.packed_weight, self.weight_scale, self.bias, n=self.out_features
-            )
-        return result.reshape(*leading_shape, self.out_features)
+            return result.reshape(*leading_shape, self.out_features)
+        result = ops.gemm_nvfp4(
+            packed, scale, self.packed_weight, self.weight_scale, self.bias, n=self.out_features
+        ).reshape(*leading_shape, self.out_features)
+        return result if residual is None else result + residual
 
-    def forward(self, value):
+    def forward(self, value, residual=None):
         packed, scale = self.pack_input(value)
-        shape = value.shape[:-1] if not isinstance(value, FloatingPacked) else value.shape[:-1]
-        return self.forward_packed(packed, scale, shape)
+        return self.forward_packed(packed, scale, value.shape[:-1], residual)
 
 
 class FloatingInputGroup:
@@ -481,6 +487,13 @@ class FloatingProjections:
         self.options = {"swiglu": swiglu, "gelu": gelu, "rmsnorm": rmsnorm}
         self._patches = _Patches()
 
+    def linear_of(self, module):
+        """The FloatingLinear installed on `module` (None if it has none)."""
+        for site, linear in self.sites.values():
+            if site is module:
+                return linear
+        return None
+
     def input_smoothing(self, module):
         """The SmoothQuant scale of a quantized site (None if unsmoothed)."""
         for name, (site, _) in self.sites.items():
@@ -590,10 +603,11 @@ class FloatingConnections:
             if residual and floating._quantized(block.ff.net[0].proj):
                 if block.pos_embed is not None:
                     raise ValueError("Floating residual fusion requires no position embeddings")
-                self.blocks.append((block, floating.input_smoothing(block.ff.net[0].proj)))
+                self.blocks.append((block, floating.input_smoothing(block.ff.net[0].proj),
+                                    floating.linear_of(block.ff.net[2])))
         if not self.norms or (residual and not self.blocks):
             raise ValueError("Floating norm fusion selected no compatible DiT projections")
-        for norm in [*(n.norm for n, _ in self.norms), *(b.norm3 for b, _ in self.blocks)]:
+        for norm in [*(n.norm for n, _ in self.norms), *(b.norm3 for b, _, _ in self.blocks)]:
             if not isinstance(norm, torch.nn.LayerNorm) or norm.elementwise_affine:
                 raise ValueError("Floating norm fusion requires non-affine LayerNorm")
         self.precision = precision
@@ -611,10 +625,10 @@ class FloatingConnections:
                 return packed
 
             self._patches.replace(norm, "forward", forward)
-        for block, smooth in self.blocks:
+        for block, smooth, down in self.blocks:
 
             def forward(hidden_states, attention_mask=None, encoder_hidden_states=None,
-                        encoder_attention_mask=None, temb=None, block=block, smooth=smooth):
+                        encoder_attention_mask=None, temb=None, block=block, smooth=smooth, down=down):
                 x = hidden_states
                 normalized = block.norm1(x, temb) if block.norm_type == "ada_norm" else block.norm1(x)
                 mask = encoder_attention_mask if encoder_hidden_states is not None else attention_mask
@@ -623,7 +637,12 @@ class FloatingConnections:
                     attention = block.final_dropout(attention)
                 packed, summed = prepare_norm(x, precision, eps=block.norm3.eps, residual=attention.contiguous(),
                                               smoothing_scale=smooth)
-                return summed + block.ff(packed)
+                if down is None or len(block.ff.net) != 3:
+                    return summed + block.ff(packed)
+                # summed + ff(packed), the add in the down projection's
+                # epilogue: bf16(y + summed) in fp32, as torch's bf16 add.
+                h = block.ff.net[1](block.ff.net[0](packed))
+                return down(h, residual=summed)
 
             self._patches.replace(block, "forward", forward)
 

@@ -159,6 +159,10 @@ def test_gemm_fp8_residual_and_floating_linear():
                             residual=res)
     want = (direct.float() + res.float()).to(torch.bfloat16)
     assert torch.equal(with_res, want)
+    # The layer's residual form is the GEMM's residual epilogue (as the DiT
+    # FFN down projection uses it): exactly bf16(y + residual).
+    r3 = res.reshape(2, 17, 4608)
+    assert torch.equal(layer(x, residual=r3), (layer(x).float() + r3.float()).to(torch.bfloat16))
     fast = FloatingLinear(linear, "probe", "fp8", fast_fp8=True)
     q2, _, rows2 = ops.quant_fp8(x.reshape(-1, 1536), fast=True)
     assert torch.equal(fast(x).reshape(-1, 4608),
