@@ -94,6 +94,19 @@ int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
                      int64_t rows, int64_t k, void *q, float *scales,
                      void *stream);
 
+/* pir2b_quant_rows (plain values) for rows whose maximum |x| is already known
+ * as partial maxima: x_max [rows, parts] fp32, e.g. the per-16-channel output
+ * maxima of the GEMM that wrote x (pir2b_gemm_fused's max_out).  The row
+ * scale comes from max_i x_max[row, i] and the codes are elementwise, so the
+ * pack runs without a row reduction over x; codes and scales are bitwise
+ * those of pir2b_quant_rows when x_max holds the rows' exact maxima.  The
+ * same pack as the reference's `_prepare` (coexecution/kernels/ampere_ada/
+ * integer.py:50-94) with its row statistic supplied by the producer.
+ * q: int8 [rows, Kpad] (bits 8) or uint8 [rows, Kpad/2] (bits 4); scales:
+ * fp32 [rows]. */
+int pir2b_quant_rows_max(const void *x, int64_t ldx, const float *x_max, int64_t parts, int bits, int64_t rows,
+                         int64_t k, void *q, float *scales, void *stream);
+
 /* The values of pir2b_quant_rows (plain, LUT activation, SiLU * up; the
  * optional SmoothQuant division) to the floating formats of the piR2 Thor
  * producers:
@@ -335,10 +348,14 @@ int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float 
  * writes gate|up (coexecution/optimization/groot/integer.py:166-172) and
  * packs bf16(SiLU(gate) * up) in the down projection's gated pack
  * (coexecution/kernels/ampere_ada/integer.py:27-48); here the down
- * projection packs `out` plainly.  half_n % 128 == 0, kpad % 128 == 0. */
+ * projection packs `out` plainly.  half_n % 128 == 0, kpad % 128 == 0.
+ * max_out (fp32 [m, half_n / 16], or NULL) receives the per-16-column
+ * maxima of |out|, the row statistic pir2b_quant_rows_max packs `out` with;
+ * it needs a 16-byte aligned `out` with ldo % 8 == 0. */
 int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const float *sw,
                       const void *bias, int bias_mode, const void *silu_lut, int64_t m,
-                      int64_t half_n, int64_t kpad, void *out, int64_t ldo, void *stream);
+                      int64_t half_n, int64_t kpad, void *out, int64_t ldo, float *max_out,
+                      void *stream);
 
 /* Small-sequence attention (no mask) reading q, k, v from projection rows
  * (head h at columns h*head_dim..) and writing out[b*T + t, h*head_dim + d]

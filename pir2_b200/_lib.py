@@ -34,6 +34,7 @@ SIGNATURES = {
     "pir2b_device_status": [ctypes.POINTER(_I), _P],
     "pir2b_wait_probe": [_P, _P],
     "pir2b_quant_rows": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _P, _P, _P],
+    "pir2b_quant_rows_max": [_P, _I64, _P, _I64, _I, _I64, _I64, _P, _P, _P],
     "pir2b_floating_rows": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _P, _P, _P],
     "pir2b_fp8_cast": [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _P, _P, _I64, _P],
     "pir2b_norm_quant_rows": [
@@ -53,7 +54,7 @@ SIGNATURES = {
     "pir2b_dit_ffn_workspace": [_I64, _I64],
     "pir2b_dit_ffn": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
     "pir2b_dit_ffn_static": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I64, _P],
-    "pir2b_gemm_swiglu": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _P, _I64, _P],
+    "pir2b_gemm_swiglu": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _P, _I64, _P, _P],
     "pir2b_attention_rows": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I, _F, _P],
     "pir2b_unpack_int4": [_P, _I64, _I64, _P, _P],
     "pir2b_attention_causal": [_P, _P, _P, _I64, _I64, _I, _I, _I, _F, _P, _I64, _P],

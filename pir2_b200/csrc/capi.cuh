@@ -684,7 +684,8 @@ static int launch_gemm(const GemmPlan &plan, const void *qa, const float *sa, co
     args.x_bytes = fin->x_bytes;
   }
   args.max_out = max_out;
-  args.max_parts = int(npad / 16);
+  // Output columns per row: half the weight rows with SwiGLU.
+  args.max_parts = int((silu_lut != nullptr ? n_store : npad) / 16);
   args.sa = sa;
   args.sw = sw;
   args.bias = bias_mode == PIR2B_BIAS_ADD
@@ -882,6 +883,41 @@ int pir2b_quant_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
   return cuda_status(
       run_quant_rows(a, bits, rows, vec, static_cast<cudaStream_t>(stream)),
       "quant_rows launch");
+}
+
+int pir2b_quant_rows_max(const void *x, int64_t ldx, const float *x_max, int64_t parts, int bits, int64_t rows,
+                         int64_t k, void *q, float *scales, void *stream) {
+  if (bits != 4 && bits != 8)
+    return fail(PIR2B_EINVAL, "bits must be 4 or 8, got %d", bits);
+  if (k < 1 || k > 65536)
+    return fail(PIR2B_EINVAL, "row width k=%lld outside [1, 65536]", (long long)k);
+  if (rows < 0 || rows > 0x7fffffffLL)
+    return fail(PIR2B_EINVAL, "row count %lld out of range", (long long)rows);
+  if (parts < 1 || parts > 65536)
+    return fail(PIR2B_EINVAL, "parts (maxima per row) must be in [1, 65536]");
+  if (rows == 0)
+    return PIR2B_OK;
+  if (x == nullptr || x_max == nullptr || q == nullptr || scales == nullptr)
+    return fail(PIR2B_EINVAL, "x, x_max, q and scales must be non-null");
+  if (ldx < k)
+    return fail(PIR2B_EINVAL, "row stride smaller than the row width");
+  if (!aligned(x, 2) || !aligned(q, 16) || !aligned(scales, 4) || !aligned(x_max, 4))
+    return fail(PIR2B_EALIGN, "pointer alignment not met");
+  DeviceInfo *dev = nullptr;
+  if (int r = device_info(&dev))
+    return r;
+  QuantMaxArgs a;
+  a.x = static_cast<const __nv_bfloat16 *>(x);
+  a.ldx = ldx;
+  a.x_max = x_max;
+  a.parts = int(parts);
+  a.q = static_cast<uint8_t *>(q);
+  a.scales = scales;
+  a.k = int(k);
+  a.kpad = int((k + 127) / 128 * 128);
+  const bool vec = (k % 8 == 0) && (ldx % 8 == 0) && aligned(x, 16);
+  return cuda_status(run_quant_rows_max(a, bits, rows, vec, static_cast<cudaStream_t>(stream)),
+                     "quant_rows_max launch");
 }
 
 int pir2b_floating_rows(const void *x, int64_t ldx, const void *up, int64_t ldu,
@@ -1466,7 +1502,8 @@ int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float 
 
 int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const float *sw,
                       const void *bias, int bias_mode, const void *silu_lut, int64_t m,
-                      int64_t half_n, int64_t kpad, void *out, int64_t ldo, void *stream) {
+                      int64_t half_n, int64_t kpad, void *out, int64_t ldo, float *max_out,
+                      void *stream) {
   if (bias_mode < 0 || bias_mode > 2)
     return fail(PIR2B_EINVAL, "bias_mode must be 0, 1 or 2");
   if (m < 1 || m > 0x7fffffffLL || half_n < 128 || half_n % 128 != 0 ||
@@ -1483,8 +1520,11 @@ int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const flo
   if (!aligned(qa, 16) || !aligned(qw, 16))
     return fail(PIR2B_EALIGN, "packed operands must be 16-byte aligned");
   if (!aligned(out, 2) || !aligned(sa, 4) || !aligned(sw, 4) || (bias && !aligned(bias, 2)) ||
-      !aligned(silu_lut, 2))
+      !aligned(silu_lut, 2) || (max_out && !aligned(max_out, 4)))
     return fail(PIR2B_EALIGN, "scale/bias/output alignment not met");
+  // The maxima are taken from the staged output tile, written by TMA stores.
+  if (max_out != nullptr && !tma_out(out, ldo))
+    return fail(PIR2B_EINVAL, "max_out needs a 16-byte aligned output with ldo %% 8 == 0");
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
@@ -1492,8 +1532,10 @@ int pir2b_gemm_swiglu(const void *qa, const float *sa, const void *qw, const flo
   if (plan.smem == 0 || int64_t(plan.bn) * plan.mtiles < m)
     return fail(PIR2B_EINVAL, "no SwiGLU tile plan fits m=%lld kpad=%lld", (long long)m,
                 (long long)kpad);
+  if (max_out != nullptr && plan.splits != 1)
+    return fail(PIR2B_EINVAL, "internal: SwiGLU plan with split-K cannot write max_out");
   return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, nullptr, nullptr, 0, silu_lut, 8, m,
-                     2 * half_n, kpad, out, ldo, half_n, stream);
+                     2 * half_n, kpad, out, ldo, half_n, stream, nullptr, max_out);
 }
 
 // Workspace of pir2b_dit_ffn: [3 counters | pad to 256 B][row maxima f32

@@ -536,6 +536,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             tma_store_2d(&tm_out, stage, blockIdx.x * kTileN, m0);
             tma_store_commit_and_wait();
           }
+          // Per-16-channel maxima of h for the next pack (read from the
+          // staged tile, which the TMA store only reads as well).
+          if (args.max_out != nullptr)
+            store_group_max(args, stage, kTileN, valid_m, m0, blockIdx.x * kTileN / 16, et);
         }
       } else if (args.splits == 1) {
         const uint16_t *lut = reinterpret_cast<const uint16_t *>(args.out_lut);

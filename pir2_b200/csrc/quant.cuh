@@ -702,6 +702,70 @@ static cudaError_t launch_quant_cluster(const QuantArgs &a, int64_t rows,
   return cudaLaunchKernelEx(&cfg, quant_rows_cluster_kernel<kBits, 2, false>, a);
 }
 
+// ------------------------------------------------------------------ packs
+// with given maxima.  The symmetric-row-v1 pack of rows whose maximum |x| is
+// already known as partial maxima (e.g. the per-16-channel maxima the GEMM
+// that wrote x produced in its epilogue, `max_out`): the row scale
+// row_scale(max_i x_max[row, i]) equals quant_rows_kernel's (a maximum does
+// not depend on its order), and the codes are then elementwise, so a row is
+// split over ceil(Kpad / 1024) CTAs of 128 threads, one 8-value chunk per
+// thread, with no row reduction over x.  Bitwise the same bytes and scales
+// as quant_rows_kernel (plain mode).
+struct QuantMaxArgs {
+  const __nv_bfloat16 *x;   // [rows, ldx]
+  int64_t ldx;
+  const float *x_max;       // [rows, parts]
+  int parts;
+  uint8_t *q;
+  float *scales;
+  int k;
+  int kpad;
+};
+
+template <int kBits, bool kVec>
+__global__ void __launch_bounds__(128) quant_rows_max_kernel(const QuantMaxArgs a) {
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t row = blockIdx.x;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < a.parts; i += 128)
+    m = fmaxf(m, __ldg(a.x_max + row * a.parts + i));
+  m = block_max(m, red);
+  const float s = row_scale<kBits>(m);
+  if (blockIdx.y == 0 && threadIdx.x == 0)
+    a.scales[row] = s;
+  const int nchunks = a.kpad >> 3;
+  const int chunk = int(blockIdx.y) * 128 + int(threadIdx.x);
+  if (chunk < nchunks) {
+    const int c0 = chunk * 8;
+    __nv_bfloat16 xv[8];
+    load8<kVec>(a.x + row * a.ldx, c0, a.k, xv);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      v[i] = c0 + i < a.k ? __bfloat162float(xv[i]) : 0.f;
+    store_codes<kBits>(v, s, a.q + row * (kBits == 8 ? a.kpad : a.kpad / 2), c0);
+  }
+}
+
+cudaError_t run_quant_rows_max(const QuantMaxArgs &a, int bits, int64_t rows, bool vec, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(rows), unsigned((a.kpad / 8 + 127) / 128), 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (bits == 8)
+    return vec ? cudaLaunchKernelEx(&cfg, quant_rows_max_kernel<8, true>, a)
+               : cudaLaunchKernelEx(&cfg, quant_rows_max_kernel<8, false>, a);
+  return vec ? cudaLaunchKernelEx(&cfg, quant_rows_max_kernel<4, true>, a)
+             : cudaLaunchKernelEx(&cfg, quant_rows_max_kernel<4, false>, a);
+}
+
 cudaError_t run_quant_rows(const QuantArgs &a, int bits, int64_t rows,
                            bool vec, cudaStream_t st) {
   const int nchunks = a.kpad / 8;

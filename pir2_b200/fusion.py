@@ -20,7 +20,10 @@ quantized projection, keeping the model's own forward code:
   epilogue (the same torch-built LUT applied to its bf16 output), so the down
   projection packs plain values: the codes are identical, and the LUT
   gathers run once per output element inside a kernel that is already
-  running;
+  running; the up GEMM also writes the per-16-channel maxima of its output,
+  from which the down projection's pack takes its row scales
+  (`ops.quant_rows_max`: no second reduction over the 6144-wide rows, the
+  same codes);
 * with the fused pack enabled (`integer.FUSED_PACK_ROWS`, off by default)
   and few W8A8 rows, the up GEMM also writes the per-16-channel maxima of
   its output and the down GEMM packs that output inside itself from them
@@ -38,6 +41,12 @@ from .connections import packed_input
 from .fused import prepare_gelu, prepare_silu
 from .linear import prepare
 from .modulation import prepare_norm_modulation
+
+# The down projections' packs (DiT FFN, text MLP) take their row maxima
+# from the producing GEMM's epilogue (per-16-channel maxima of gelu(up(x))
+# or of silu(gate) * up) instead of reducing the 6144-wide rows again
+# (`ops.quant_rows_max`, the same bytes).
+PACK_FROM_GEMM_MAX = True
 
 
 class ResidualFusion:
@@ -165,6 +174,21 @@ class ResidualFusion:
                         # GEMM from the up GEMM's per-16-channel maxima.
                         return down_q.forward_rows(hidden, x_max=maxes)
                     return self.controller.dispatch(down_q, hidden)
+                if (
+                    PACK_FROM_GEMM_MAX
+                    and self.controller.candidates is None
+                    and up_q.packed_weight.shape[0] % 16 == 0
+                ):
+                    rows = packed.data.shape[0]
+                    maxes = torch.empty(
+                        (rows, up_q.packed_weight.shape[0] // 16), device=packed.data.device, dtype=torch.float32
+                    )
+                    hidden = up_q.forward_packed(packed, out_lut=lut, max_out=maxes)
+                    k = hidden.shape[-1]
+                    data, scales = ops.quant_rows_max(hidden.reshape(rows, k), maxes, bits)
+                    return down_q.forward_packed(
+                        integer.PackedActivation(data, scales, tuple(hidden.shape[:-1]), k, bits)
+                    )
                 hidden = up_q.forward_packed(packed, out_lut=lut)      # gelu(up(x)), bf16
                 return self.controller.dispatch(down_q, hidden)
 
@@ -220,6 +244,17 @@ class SwiGLUFusion:
 
             def forward(x, down_q=down_q, half=half, weight=weight, scale=scale, bias=bias, bias_mode=bias_mode):
                 packed = x.for_bits(8) if getattr(x, "_robotics_packed_input", False) else prepare(x, 8)
+                if PACK_FROM_GEMM_MAX and self.controller.candidates is None:
+                    # The down projection's pack from the SwiGLU epilogue's
+                    # per-16-column maxima (the same codes as packing h).
+                    rows = packed.data.shape[0]
+                    maxes = torch.empty((rows, half // 16), device=packed.data.device, dtype=torch.float32)
+                    hidden = ops.gemm_swiglu(
+                        packed.data, packed.scales, weight, scale, bias, self.silu, half_n=half,
+                        bias_mode=bias_mode, max_out=maxes,
+                    )
+                    data, scales = ops.quant_rows_max(hidden, maxes, 8)
+                    return down_q.forward_packed(integer.PackedActivation(data, scales, tuple(packed.shape), half, 8))
                 hidden = ops.gemm_swiglu(
                     packed.data, packed.scales, weight, scale, bias, self.silu, half_n=half, bias_mode=bias_mode
                 )

@@ -84,6 +84,27 @@ def quant_rows(x, bits, *, lut=None, up=None, smooth=None, out=None):
     return data, scales
 
 
+def quant_rows_max(x, x_max, bits):
+    """symmetric-row-v1 pack of bf16 rows x [rows, k] whose maxima are known:
+    x_max fp32 [rows, parts] partial maxima of |x| (the `max_out` of the GEMM
+    that wrote x).  Same bytes and scales as `quant_rows(x, bits)`."""
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.stride(-1) != 1 or x.ndim < 2:
+        raise ValueError("Expected CUDA BF16 rows with unit feature stride")
+    matrix, rows, k, ldx = _rows(x)
+    if x_max.dtype != torch.float32 or x_max.dim() != 2 or x_max.shape[0] != rows or not x_max.is_contiguous():
+        raise ValueError("x_max must be contiguous fp32 [rows, parts]")
+    pad = kpad(k)
+    data = torch.empty((rows, pad if bits == 8 else pad // 2), device=x.device,
+                       dtype=torch.int8 if bits == 8 else torch.uint8)
+    scales = torch.empty(rows, device=x.device, dtype=torch.float32)
+    status = _lib.lib().pir2b_quant_rows_max(
+        x.data_ptr(), ldx, x_max.data_ptr(), x_max.shape[1], bits, rows, k, data.data_ptr(), scales.data_ptr(),
+        _stream(x.device),
+    )
+    _lib.check(status, "pir2b_quant_rows_max")
+    return data, scales
+
+
 def _floating_buffers(rows, k, out_format, device, maxima_per_row=1):
     """Outputs of a floating producer: NVFP4 (packed E2M1 [rows, k/2],
     swizzled UE4M3 factors) or the FP8 first pass (bf16 values [rows, k],
@@ -340,9 +361,11 @@ def interleave_gate_up(t, half):
     return parts.reshape(t.shape).contiguous()
 
 
-def gemm_swiglu(a, sa, w, sw, bias, silu_lut, *, half_n, bias_mode=None, out=None):
+def gemm_swiglu(a, sa, w, sw, bias, silu_lut, *, half_n, bias_mode=None, out=None, max_out=None):
     """W8A8 gate|up GEMM writing bf16(silu(gate) * up) [m, half_n]; w, sw
-    and bias in the interleaved layout of `interleave_gate_up`."""
+    and bias in the interleaved layout of `interleave_gate_up`.  `max_out`
+    (fp32 [m, half_n / 16]) also receives the output's per-16-column
+    maxima of |h| (for `quant_rows_max`)."""
     m = a.shape[0]
     k_pad = a.shape[1]
     if w.dtype != torch.int8 or w.shape[1] != k_pad or w.shape[0] != 2 * half_n:
@@ -351,12 +374,16 @@ def gemm_swiglu(a, sa, w, sw, bias, silu_lut, *, half_n, bias_mode=None, out=Non
         bias_mode = _lib.BIAS_NONE if bias is None else _lib.BIAS_ADD
     if out is None:
         out = torch.empty((m, half_n), device=a.device, dtype=torch.bfloat16)
+    if max_out is not None and (
+        max_out.dtype != torch.float32 or max_out.shape != (m, half_n // 16) or not max_out.is_contiguous()
+    ):
+        raise ValueError("max_out must be contiguous fp32 [m, half_n / 16]")
     recorder = launch_recorder
     if recorder is not None:
         recorder.before(a.device)
     status = _lib.lib().pir2b_gemm_swiglu(
         a.data_ptr(), sa.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias), bias_mode,
-        silu_lut.data_ptr(), m, half_n, k_pad, out.data_ptr(), out.stride(0), _stream(a.device),
+        silu_lut.data_ptr(), m, half_n, k_pad, out.data_ptr(), out.stride(0), _ptr(max_out), _stream(a.device),
     )
     _lib.check(status, "pir2b_gemm_swiglu")
     if recorder is not None:

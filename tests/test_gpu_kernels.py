@@ -62,6 +62,32 @@ def test_quant_rows_plain_bitwise(bits, rows, k):
 
 
 @pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("rows,k", [(1, 2048), (17, 6144), (17, 130), (3, 127), (64, 6144), (1088, 6144)])
+def test_quant_rows_with_given_maxima_bitwise(bits, rows, k):
+    """The pack that takes its row maxima as per-16-column partial maxima
+    (from the producing GEMM's epilogue) writes the oracle's codes and
+    scales, including zero rows and +-inf values."""
+    g = torch.Generator().manual_seed(rows * 7 + k + bits)
+    x = randn_bf16(g, rows, k, outliers=True)
+    x[0] = 0.0
+    if rows > 2:
+        x[2, k // 2] = float("inf")
+    xc = x.cuda()
+    parts = -(-k // 16)
+    padded = torch.zeros(rows, parts * 16, dtype=torch.float32)
+    padded[:, :k] = x.float().abs()
+    maxima = padded.reshape(rows, parts, 16).amax(dim=2).contiguous().cuda()
+    q, s = ops.quant_rows_max(xc, maxima, bits)
+    rq, rs = oracle.quant_rows(bits_of(x), bits)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy().view(np.uint8), rq.view(np.uint8))
+    # The GEMM epilogue's maxima feed it directly: same bytes as quant_rows.
+    q2, s2 = ops.quant_rows(xc, bits)
+    assert torch.equal(q, q2) and torch.equal(s, s2)
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("kind", ["tanh", "none", "silu"])
 @pytest.mark.parametrize("gated", [False, True])
 def test_quant_rows_lut_modes_bitwise(bits, kind, gated):
@@ -604,6 +630,32 @@ def test_gemm_swiglu_pair_tiles_bitwise(m, k, half, pair_mode):
     detail = [(int(r), int(c), hex(got[r, c]), hex(ref[r, c]), hex(y[r, c]), hex(y[r, half_pad + c]))
               for r, c in mismatch[:4]]
     assert mismatch.size == 0, f"{len(mismatch)} mismatches (row, col, got, want, gate, up): {detail}"
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("m,k,half,mode", [(544, 2048, 6144, 1), (544, 2048, 6144, 2), (17, 1536, 1024, 0),
+                                           (300, 512, 640, 2)])
+def test_gemm_swiglu_max_out_feeds_the_pack_bitwise(m, k, half, mode, pair_mode):
+    """The SwiGLU epilogue's per-16-column maxima (2-SM and one-SM plans)
+    equal |h|'s, and packing h from them gives the bytes of packing h."""
+    from pir2_b200.fused import prepare_silu
+
+    pair_mode(mode)
+    g = torch.Generator().manual_seed(m * 3 + k + half)
+    _, _, b, qa, sa, qw, sw = quantized_problem(g, m, k, 2 * half, 8)
+    lut = prepare_silu(torch.device("cuda"))
+    cat = lambda t: ops.interleave_gate_up(t, half)   # noqa: E731
+    args = (torch.from_numpy(qa).cuda(), torch.from_numpy(sa).cuda(), cat(torch.from_numpy(qw).cuda()),
+            cat(torch.from_numpy(sw).cuda()), cat(b.cuda()), lut)
+    plain = ops.gemm_swiglu(*args, half_n=half)
+    maxes = torch.full((m, half // 16), -1.0, device="cuda")
+    out = ops.gemm_swiglu(*args, half_n=half, max_out=maxes)
+    assert torch.equal(out, plain)
+    want = out.float().abs().reshape(m, half // 16, 16).amax(dim=2)
+    assert torch.equal(maxes, want)
+    q1, s1 = ops.quant_rows_max(out, maxes, 8)
+    q2, s2 = ops.quant_rows(out, 8)
+    assert torch.equal(q1, q2) and torch.equal(s1, s2)
     assert_status_clean()
 
 
