@@ -333,11 +333,16 @@ int pir2b_quant_fp8(const void *x, int64_t ldx, int64_t rows, int64_t k, int fas
  * sw: npad floats, from pir2b_quant_fp8).  Replaces the CUTLASS FP8 GEMM
  * (fp8_cutlass_linear.cu:470-665, linear_forward_packed_tactic :1026-1145,
  * whose epilogue applies scale_a * scale_b and the per-column bias).
- * qa [m, kpad], qw [npad, kpad] E4M3 bytes, kpad % 128 == 0. */
+ * qa [m, kpad], qw [npad, kpad] E4M3 bytes, kpad % 128 == 0.  out_lut
+ * (bf16[65536] or NULL) maps each bf16 result through an activation table
+ * (GELU) before the residual; max_out (fp32 [m, npad / 16] or NULL; m <= 32)
+ * receives per-16-column maxima of the finite |out|, the partial maxima
+ * pir2b_fp8_cast packs `out` with (the GELU producer of the FP8 DiT FFN,
+ * thor/packing.py:352-392, in the GEMM's epilogue). */
 int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float *sw,
                    const void *bias, int bias_mode, const void *residual, int64_t ldr, int64_t m,
                    int64_t npad, int64_t kpad, void *out, int64_t ldo, int64_t n_store,
-                   void *stream);
+                   const void *out_lut, float *max_out, void *stream);
 
 /* W8A8 gate|up GEMM with the SwiGLU epilogue: out[m, c] =
  * bf16(f32(silu_lut[g]) * f32(u)) for c < half_n, where g and u are the

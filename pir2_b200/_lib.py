@@ -48,7 +48,7 @@ SIGNATURES = {
         _I64, _P, _P,
     ],
     "pir2b_quant_fp8": [_P, _I64, _I64, _I64, _I, _I, _P, _P, _P, _I64, _P],
-    "pir2b_gemm_fp8": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P],
+    "pir2b_gemm_fp8": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P],
     "pir2b_pack_nvfp4": [_P, _I64, _I64, _P, _P, _P],
     "pir2b_gemm_nvfp4": [_P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _P, _I64, _P],
     "pir2b_dit_ffn_workspace": [_I64, _I64],

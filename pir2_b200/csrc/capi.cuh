@@ -1466,7 +1466,7 @@ int pir2b_quant_fp8(const void *x, int64_t ldx, int64_t rows, int64_t k, int fas
 int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float *sw,
                    const void *bias, int bias_mode, const void *residual, int64_t ldr, int64_t m,
                    int64_t npad, int64_t kpad, void *out, int64_t ldo, int64_t n_store,
-                   void *stream) {
+                   const void *out_lut, float *max_out, void *stream) {
   if (bias_mode < 0 || bias_mode > 2)
     return fail(PIR2B_EINVAL, "bias_mode must be 0, 1 or 2");
   if (m < 1 || m > 0x7fffffffLL || npad < 8 || npad % 8 != 0 || kpad < 128 ||
@@ -1483,9 +1483,13 @@ int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float 
     return fail(PIR2B_EALIGN, "FP8 GEMM alignment not met");
   if (residual != nullptr && ldr < n_store)
     return fail(PIR2B_EINVAL, "residual row stride ldr must be >= n_store");
+  if ((out_lut && !aligned(out_lut, 2)) || (max_out && !aligned(max_out, 4)))
+    return fail(PIR2B_EALIGN, "FP8 GEMM alignment not met");
+  if (max_out != nullptr && (!use_few(9, m) || npad % 16 != 0))
+    return fail(PIR2B_EINVAL, "FP8 GEMM max_out needs m <= 32 token rows and npad %% 16 == 0");
   if (use_few(9, m))
-    return launch_few(qa, sa, qw, sw, bias, bias_mode, nullptr, residual, ldr, 9, m, npad, kpad, out, ldo,
-                      n_store, nullptr, stream);
+    return launch_few(qa, sa, qw, sw, bias, bias_mode, out_lut, residual, ldr, 9, m, npad, kpad, out, ldo,
+                      n_store, max_out, stream);
   DeviceInfo *dev = nullptr;
   if (int r = device_info(&dev))
     return r;
@@ -1496,7 +1500,7 @@ int pir2b_gemm_fp8(const void *qa, const float *sa, const void *qw, const float 
       plan.smem > size_t(dev->max_smem))
     return fail(PIR2B_EINVAL, "no GEMM tile plan fits m=%lld npad=%lld kpad=%lld",
                 (long long)m, (long long)npad, (long long)kpad);
-  return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, nullptr, residual, ldr, nullptr, 9, m,
+  return launch_gemm(plan, qa, sa, qw, sw, bias, bias_mode, out_lut, residual, ldr, nullptr, 9, m,
                      npad, kpad, out, ldo, n_store, stream);
 }
 

@@ -234,6 +234,10 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_few_kernel(const FewArgs a) 
         o = __float2bfloat16_rn(__fadd_rn(__bfloat162float(o), __bfloat162float(a.residual[int64_t(j) * a.ldr + c])));
       a.out[int64_t(j) * a.ldo + c] = o;
       mag = fabsf(__bfloat162float(o));
+      // E4M3 (the FP8 cast's partial maxima): only finite values count
+      // (thor/packing.py:76-78); fmaxf below already skips NaN.
+      if (kBits == 9 && mag == INFINITY)
+        mag = 0.f;
     }
     if (a.max_out != nullptr) {
       // Per-16-channel maximum of |y| for token j: the 16 threads of the row

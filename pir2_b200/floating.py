@@ -425,6 +425,28 @@ class _Patches:
         self.saved = []
 
 
+# FP8 DiT FFN: the GELU producer's table and partial maxima come from the up
+# projection's epilogue (`_fp8_gelu_from_gemm`); False keeps the separate
+# producer pass.  Both give the same codes.
+FP8_GELU_FROM_GEMM = True
+
+
+def _fp8_gelu_from_gemm(module, linear, lut, x):
+    """gelu(proj(x)) packed to E4M3 with the table and the partial maxima
+    written by the E4M3 GEMM's epilogue (at most 32 token rows), else the
+    module's GEMM followed by the GELU producer."""
+    packed, scale = linear.pack_input(x)
+    rows = packed.shape[0]
+    if rows > 32 or linear.packed_weight.shape[0] % 16:
+        return module.gelu(module.proj(x))
+    maxima = torch.empty((rows, linear.packed_weight.shape[0] // 16), device=packed.device, dtype=torch.float32)
+    y = ops.gemm_fp8(packed, scale, linear.packed_weight, linear.weight_scale_columns, linear.bias,
+                     n=linear.out_features, out_lut=lut, max_out=maxima)
+    q, s, rep = ops.fp8_cast(y, maxima)
+    shape = tuple(x.shape[:-1]) + (linear.out_features,)
+    return FloatingPacked(q, s.reshape(()), shape, "fp8", None, rep)
+
+
 class FloatingProjections:
     """Reversible installation of the floating Linear layers and producers
     (coexecution/optimization/groot/floating.py:17-372): every executed site
@@ -546,6 +568,15 @@ class FloatingProjections:
                 patches.replace(module, attr, lambda x, lut=lut, smooth=smooth: prepare_gelu_packed(
                     x.contiguous(), lut, precision, smoothing_scale=smooth))
                 self.coverage["gelu_producers"].append(down)
+                proj = getattr(module, "proj", None)
+                proj_linear = None if proj is None else self.linear_of(proj)
+                if (FP8_GELU_FROM_GEMM and precision == "fp8" and attr == "gelu" and smooth is None
+                        and proj_linear is not None):
+                    # FP8: the GELU table and the producer's partial maxima in
+                    # the up projection's epilogue (few-token launches), so
+                    # only the cast remains (the same values, maxima, codes).
+                    patches.replace(module, "forward", lambda x, module=module, lin=proj_linear, lut=lut: (
+                        _fp8_gelu_from_gemm(module, lin, lut, x)))
                 if attr == "gelu":
                     # The eval Dropout between the DiT FFN's GELU and its down
                     # projection passes the packed carrier through.

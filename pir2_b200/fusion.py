@@ -45,8 +45,12 @@ from .modulation import prepare_norm_modulation
 # The down projections' packs (DiT FFN, text MLP) take their row maxima
 # from the producing GEMM's epilogue (per-16-channel maxima of gelu(up(x))
 # or of silu(gate) * up) instead of reducing the 6144-wide rows again
-# (`ops.quant_rows_max`, the same bytes).
+# (`ops.quant_rows_max`, the same bytes), for at most PACK_FROM_GEMM_MAX_ROWS
+# rows: every CTA of a row re-reads the row's maxima (384 floats for 6144
+# columns), which costs more than the row reduction it saves at batched
+# sizes (34816 rows: ~320 MB of extra reads).
 PACK_FROM_GEMM_MAX = True
+PACK_FROM_GEMM_MAX_ROWS = 2048
 
 
 class ResidualFusion:
@@ -178,6 +182,7 @@ class ResidualFusion:
                     PACK_FROM_GEMM_MAX
                     and self.controller.candidates is None
                     and up_q.packed_weight.shape[0] % 16 == 0
+                    and packed.data.shape[0] <= PACK_FROM_GEMM_MAX_ROWS
                 ):
                     rows = packed.data.shape[0]
                     maxes = torch.empty(
@@ -244,7 +249,11 @@ class SwiGLUFusion:
 
             def forward(x, down_q=down_q, half=half, weight=weight, scale=scale, bias=bias, bias_mode=bias_mode):
                 packed = x.for_bits(8) if getattr(x, "_robotics_packed_input", False) else prepare(x, 8)
-                if PACK_FROM_GEMM_MAX and self.controller.candidates is None:
+                if (
+                    PACK_FROM_GEMM_MAX
+                    and self.controller.candidates is None
+                    and packed.data.shape[0] <= PACK_FROM_GEMM_MAX_ROWS
+                ):
                     # The down projection's pack from the SwiGLU epilogue's
                     # per-16-column maxima (the same codes as packing h).
                     rows = packed.data.shape[0]

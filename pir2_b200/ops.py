@@ -543,10 +543,12 @@ def quant_fp8(x, *, fast=False, replicate=None, weights=False):
     return q, scale, rep[:n_rep]
 
 
-def gemm_fp8(qa, sa_rows, qw, sw_cols, bias=None, *, n, residual=None, out=None):
-    """E4M3 GEMM (tcgen05 kind::f8f6f4, fp32 accumulate) -> bf16 [m, n]:
-    bf16(f32(acc * sa[m]) * sw[c] + bias[c]) with the replicated per-tensor
-    scale vectors of `quant_fp8`."""
+def gemm_fp8(qa, sa_rows, qw, sw_cols, bias=None, *, n, residual=None, out=None, out_lut=None, max_out=None):
+    """E4M3 GEMM (fp32 accumulate) -> bf16 [m, n]: bf16(f32(acc * sa[m]) *
+    sw[c] + bias[c]) with the replicated per-tensor scale vectors of
+    `quant_fp8`; `out_lut` maps the result through an activation table;
+    `max_out` (fp32 [m, npad / 16], m <= 32) receives per-16-column maxima
+    of the finite |out| for `fp8_cast`."""
     m, kpad = qa.shape
     npad = qw.shape[0]
     if qw.shape[1] != kpad or qa.dtype != torch.uint8 or qw.dtype != torch.uint8:
@@ -561,9 +563,14 @@ def gemm_fp8(qa, sa_rows, qw, sw_cols, bias=None, *, n, residual=None, out=None)
     recorder = launch_recorder
     if recorder is not None:
         recorder.before(qa.device)
+    if max_out is not None and (
+        max_out.dtype != torch.float32 or max_out.shape != (m, npad // 16) or not max_out.is_contiguous()
+    ):
+        raise ValueError("max_out must be contiguous fp32 [m, npad / 16]")
     status = _lib.lib().pir2b_gemm_fp8(
         qa.data_ptr(), sa_rows.data_ptr(), qw.data_ptr(), sw_cols.data_ptr(), _ptr(bias), bias_mode,
-        _ptr(residual), ldr, m, npad, kpad, out.data_ptr(), out.stride(0), n, _stream(qa.device),
+        _ptr(residual), ldr, m, npad, kpad, out.data_ptr(), out.stride(0), n, _ptr(out_lut), _ptr(max_out),
+        _stream(qa.device),
     )
     _lib.check(status, "pir2b_gemm_fp8")
     if recorder is not None:

@@ -203,3 +203,56 @@ def test_prepare_producers_feed_their_consumer(precision):
     sp = prepare_smoothed(gate.reshape(-1, 1536), precision, s)
     assert torch.equal(smoothed(gate).reshape(-1, 512), smoothed(sp))
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(17, 1536, 6144), (1, 256, 640), (32, 2048, 1024)])
+def test_fp8_gemm_table_and_finite_maxima_feed_the_cast(m, k, n):
+    """The E4M3 GEMM with an activation table and per-16-column maxima: the
+    maxima count finite values only (a table that sends negative results to
+    +inf), and casting the output with them gives the oracle producer's
+    codes and scale."""
+    g = torch.Generator().manual_seed(m + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).cuda()
+    qa, _, sa = ops.quant_fp8(x)
+    qw, _, sw = ops.quant_fp8(w, replicate=n, weights=True)
+    bits = torch.arange(65536, dtype=torch.int32).to(torch.int16)
+    table = torch.where(bits < 0, torch.tensor(0x7F80, dtype=torch.int16), bits).view(torch.bfloat16).cuda()
+    plain = ops.gemm_fp8(qa, sa, qw, sw, bias, n=n)
+    maxima = torch.full((m, n // 16), -1.0, device="cuda")
+    y = ops.gemm_fp8(qa, sa, qw, sw, bias, n=n, out_lut=table, max_out=maxima)
+    torch.cuda.synchronize()
+    want_y = table[plain.view(torch.int16).long() & 0xFFFF]
+    assert torch.equal(y.view(torch.int16), want_y.view(torch.int16))
+    finite = torch.where(torch.isinf(y.float()), 0.0, y.float().abs())
+    assert torch.equal(maxima, finite.reshape(m, n // 16, 16).amax(dim=2))
+    q, s, rep = ops.fp8_cast(y, maxima)
+    want_q, want_s = oracle.fp8_producer(oracle.bf16_bits_to_f32(bits_of(y)))
+    assert np.float32(s.item()) == want_s and np.array_equal(q.cpu().numpy(), want_q)
+    assert _lib.device_status() == 0
+
+
+@torch.inference_mode()
+def test_fp8_gelu_from_the_gemm_epilogue_equals_the_producer():
+    """The DiT GELU module on the FP8 path: the up projection's epilogue
+    applies the GELU table and writes the partial maxima, and the cast packs
+    it; the same codes, scale and row scales as the GEMM followed by the
+    GELU producer."""
+    from pir2_b200.floating import FloatingLinear, _fp8_gelu_from_gemm, prepare_gelu_packed
+    from pir2_b200.harness import GELU
+
+    torch.manual_seed(9)
+    with torch.device("cuda"):
+        module = GELU(1536, 6144, "tanh").to(torch.bfloat16)
+    lin = FloatingLinear(module.proj, "proj", "fp8")
+    lut = prepare_gelu(torch.device("cuda"), torch.bfloat16, "tanh")
+    # Token rows of one robot's DiT (17) and the 32-row limit of the path.
+    for rows in (17, 32, 17):
+        x = torch.randn(1, rows, 1536, device="cuda", dtype=torch.bfloat16)
+        fused = _fp8_gelu_from_gemm(module, lin, lut, x)
+        ref = prepare_gelu_packed(lin(x).contiguous(), lut, "fp8")
+        assert fused.shape == ref.shape == (1, rows, 6144)
+        assert torch.equal(fused.data, ref.data)
+        assert torch.equal(fused.scale, ref.scale) and torch.equal(fused.row_scales, ref.row_scales)
+    assert _lib.device_status() == 0
