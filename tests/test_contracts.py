@@ -273,3 +273,8 @@ def test_bench_algorithmic_bytes_per_gemm():
     # SwiGLU multiplies gate and up rows but writes half the columns.
     g = dict(bits=8, m=544, n=12288, k=2048, npad=12288, out_n=6144)
     assert bench.gemm_bytes(g) == 12288 * 2048 + 544 * 2048 + 4 * 544 + 4 * 12288 + 2 * 544 * 6144
+    # E4M3: one byte per value and replicated fp32 scales, as int8.
+    assert bench.gemm_bytes(dict(s, bits="fp8")) == bench.gemm_bytes(s)
+    # NVFP4: half a byte per value plus one UE4M3 factor per 16 values.
+    f = dict(bits="fp4", m=17, n=6144, k=1536, npad=6144)
+    assert bench.gemm_bytes(f) == (6144 + 17) * 1536 // 2 + (6144 + 17) * 1536 // 16 + 2 * 17 * 6144
